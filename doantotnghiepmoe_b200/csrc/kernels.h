@@ -1,0 +1,95 @@
+// Internal launch interface between the C-ABI layer (moe_abi.cu) and the
+// kernel translation units.  Nothing here crosses the public ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace moe {
+
+// Router + top-k (route.cu).  Reference: src/olmoe.rs:2589-2621 (decode),
+// :3421-3466 (prefill); src/backend.rs:105-120, :375-389; src/dense.rs:58-73.
+enum RouteMode : int {
+  kRouteSoftmaxTopk = 0,  // OlmoeModel: softmax over all E, top-k by probability
+  kRouteTopkSoftmax = 1,  // Router::select_top_k: top-k by score, softmax over k
+};
+enum RouterDtype : int { kRouterF32 = 0, kRouterBF16 = 1, kRouterF32Seq = 2 };
+
+struct RouteArgs {
+  const float *h;       // [T, H] MoE input
+  const void *router;   // [E, H] f32 or bf16 bits
+  int router_dtype;     // RouterDtype
+  int T, H, E, K;
+  int norm_topk_prob;
+  int mode;             // RouteMode
+  float *logits;        // [T, E] scratch (raw logits)
+  uint32_t *ids;        // [T, K]
+  float *gates;         // [T, K]
+  float *probs;         // optional [T, E] post-softmax probabilities
+  uint32_t *status;
+};
+cudaError_t launch_route(const RouteArgs &a, cudaStream_t s);
+
+// Stable bucket of routes by expert (src/olmoe.rs:3474-3480): experts in
+// ascending id, tokens ascending inside an expert.
+struct PermuteArgs {
+  const uint32_t *ids;  // [T, K]
+  const float *gates;   // [T, K]
+  int T, K, E;
+  int32_t *seg_off;     // [E + 1]
+  int32_t *active;      // [E] expert ids with at least one route, ascending
+  int32_t *n_active;    // [1]
+  int32_t *r_token;     // [T*K] permuted position -> token
+  int32_t *r_slot;      // [T*K] permuted position -> slot
+  float *r_gate;        // [T*K] permuted position -> gate (may be null)
+  int32_t *r_pos;       // [T*K] (t*K + slot) -> permuted position (may be null)
+  uint32_t *status;
+};
+cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t s);
+
+// Grouped INT8 GEMV over expert segments (expert_gemv.cu), in the exact
+// reduction order of the reference's AVX2 kernels.
+struct GemvArgs {
+  int H, I;
+  const int8_t *const *w_ptr;  // [n_experts] -> 3*I*H int8 (gate | up | down)
+  const float *const *s_ptr;   // [n_experts] -> 2*I+H f32
+  const int32_t *active;       // [<= n_experts] expert index per segment
+  const int32_t *n_active_dev; // device count of segments, or null
+  int n_active_max;            // upper bound (grid sizing) / fixed count
+  const int32_t *seg_off;      // [n_experts + 1] route ranges per expert
+  const int32_t *r_token;      // route -> row of x (gate/up) ; may be null = identity
+  const float *x;              // [*, H] inputs (gate/up)
+  float *act;                  // [routes, I]
+  // down
+  const int32_t *r_slot;       // route -> slot (contrib mode)
+  const float *r_gate;         // route -> gate weight (contrib mode)
+  int K;                       // contrib stride
+  float *contrib;              // contrib mode: [T, K, H] = gate * y
+  float *y;                    // pairs mode: [routes, H]
+  uint32_t *status;
+  int sm_count;
+  int vec;                     // 1: every expert base pointer is 8-byte aligned
+};
+cudaError_t launch_gate_up(const GemvArgs &a, cudaStream_t s);
+cudaError_t launch_down(const GemvArgs &a, cudaStream_t s);
+
+// out[t] = (resid ? resid[t] : 0) + sum_slot contrib[t, slot] (slot order);
+// src/olmoe.rs:3147-3157, :3702-3714.
+cudaError_t launch_combine(const float *contrib, const float *resid, float *out, int T, int K,
+                           int H, uint32_t *status, cudaStream_t s);
+
+// RMSNorm with unit gain (src/backend.rs:341-359) over [T, H].
+cudaError_t launch_rmsnorm(const float *x, float *out, int T, int H, float eps,
+                           uint32_t *status, cudaStream_t s);
+
+// Seeded synthetic expert weights, bit-identical to the host-side generator.
+cudaError_t launch_synth_expert(uint64_t seed, int layer, int expert, int H, int I, int8_t *w,
+                                float *sc, cudaStream_t s);
+
+// expf restatement evaluated over a range of float bit patterns; writes a
+// per-block mismatch count against `expected` (or the raw values when
+// expected == null).  Used by the parity tests.
+cudaError_t launch_expf_eval(uint32_t bits_lo, uint32_t count, float *out, cudaStream_t s);
+
+}  // namespace moe

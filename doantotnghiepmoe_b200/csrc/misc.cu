@@ -1,0 +1,178 @@
+// Small kernels around the expert GEMV/GEMM: slot-ordered combine, RMSNorm,
+// the seeded synthetic-weight generator and the expf evaluation hook.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace moe {
+namespace {
+
+// out[t, j] = resid[t, j] (or 0) + contrib[t, 0, j] + ... + contrib[t, K-1, j],
+// added one slot at a time in slot order (src/olmoe.rs:3147-3157 decode,
+// :3702-3714 prefill).  contrib already holds the rounded product gate * y.
+__global__ void combine_kernel(const float *__restrict__ contrib, const float *__restrict__ resid,
+                               float *__restrict__ out, int T, int K, int H, uint32_t *status) {
+  const size_t n4 = (size_t)T * H / 4;
+  const int H4 = H / 4;
+  bool bad = false;
+  const bool vec = (H & 3) == 0 && (((uintptr_t)contrib | (uintptr_t)resid | (uintptr_t)out) & 15) == 0;
+  if (vec) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
+         i += (size_t)gridDim.x * blockDim.x) {
+      const size_t t = i / H4, j4 = i % H4;
+      float4 acc = resid ? reinterpret_cast<const float4 *>(resid)[i] : make_float4(0, 0, 0, 0);
+      const float4 *c = reinterpret_cast<const float4 *>(contrib) + t * K * H4 + j4;
+      for (int k = 0; k < K; ++k) {
+        const float4 v = c[(size_t)k * H4];
+        acc.x = __fadd_rn(acc.x, v.x);
+        acc.y = __fadd_rn(acc.y, v.y);
+        acc.z = __fadd_rn(acc.z, v.z);
+        acc.w = __fadd_rn(acc.w, v.w);
+      }
+      bad |= !(is_finite_f(acc.x) && is_finite_f(acc.y) && is_finite_f(acc.z) &&
+               is_finite_f(acc.w));
+      reinterpret_cast<float4 *>(out)[i] = acc;
+    }
+  } else {
+    const size_t n = (size_t)T * H;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+      const size_t t = i / H, j = i % H;
+      float acc = resid ? resid[i] : 0.0f;
+      for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, contrib[(t * K + k) * H + j]);
+      bad |= !is_finite_f(acc);
+      out[i] = acc;
+    }
+  }
+  if (bad) set_status(status, kStatusNonFinite);
+}
+
+// One warp per token: sum of squares in the 8-lane order of
+// src/backend.rs:105-120, then scale = sqrt(ss / n + eps), inv = 1 / scale,
+// out = (x * inv) * 1.0  (src/backend.rs:341-359 with unit gain).
+__global__ void rmsnorm_kernel(const float *__restrict__ x, float *__restrict__ out, int T, int H,
+                               float eps, uint32_t *status) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float *xr = x + (size_t)warp * H;
+  float *orow = out + (size_t)warp * H;
+  // lanes 0..7 carry the eight accumulators; other lanes idle in the chain
+  float acc = 0.0f;
+  const int full = H / 8;
+  bool bad = false;
+  if (lane < 8) {
+    for (int c = 0; c < full; ++c) {
+      const float v = xr[8 * c + lane];
+      acc = __fadd_rn(acc, __fmul_rn(v, v));
+    }
+  }
+  float s = -0.0f;
+#pragma unroll
+  for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc, l));
+  for (int i = full * 8; i < H; ++i) s = __fadd_rn(s, __fmul_rn(xr[i], xr[i]));
+  const float scale = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)H), eps));
+  const float inv = __fdiv_rn(1.0f, scale);
+  for (int j = lane; j < H; j += 32) {
+    const float v = xr[j];
+    bad |= !is_finite_f(v);
+    const float o = __fmul_rn(__fmul_rn(v, inv), 1.0f);
+    bad |= !is_finite_f(o);
+    orow[j] = o;
+  }
+  if (bad) set_status(status, kStatusNonFinite);
+}
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+  return z ^ (z >> 31);
+}
+
+__host__ __device__ inline uint64_t synth_key(uint64_t seed, uint32_t kind, uint32_t layer,
+                                              uint32_t expert) {
+  auto mx = [](uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    return z ^ (z >> 31);
+  };
+  const uint64_t k = mx(seed ^ 0x6a09e667f3bcc909ULL);
+  return mx(k ^ ((uint64_t)kind << 48) ^ ((uint64_t)layer << 24) ^ (uint64_t)expert);
+}
+
+// Four int8 weights per 64-bit hash word: w = ((16-bit piece * 255) >> 16) - 127.
+__global__ void synth_weights_kernel(uint64_t kw, size_t nw, int8_t *__restrict__ w) {
+  const size_t nwords = (nw + 3) / 4;
+  for (size_t j = blockIdx.x * (size_t)blockDim.x + threadIdx.x; j < nwords;
+       j += (size_t)gridDim.x * blockDim.x) {
+    const uint64_t u = mix64(kw + (j + 1) * 0x9E3779B97F4A7C15ULL);
+    if (4 * j + 4 <= nw && (((uintptr_t)(w + 4 * j)) & 3) == 0) {
+      uint32_t packed = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t piece = (uint32_t)(u >> (16 * b)) & 0xffffu;
+        const int v = (int)((piece * 255u) >> 16) - 127;
+        packed |= ((uint32_t)(uint8_t)(int8_t)v) << (8 * b);
+      }
+      *reinterpret_cast<uint32_t *>(w + 4 * j) = packed;
+    } else {
+      for (int b = 0; b < 4 && 4 * j + b < nw; ++b) {
+        const uint32_t piece = (uint32_t)(u >> (16 * b)) & 0xffffu;
+        w[4 * j + b] = (int8_t)((int)((piece * 255u) >> 16) - 127);
+      }
+    }
+  }
+}
+
+// scale = 1e-4 + (u >> 40) * 2^-24 * 9e-4, rounded step by step as on the host.
+__global__ void synth_scales_kernel(uint64_t ks, size_t ns, float *__restrict__ s) {
+  for (size_t r = blockIdx.x * (size_t)blockDim.x + threadIdx.x; r < ns;
+       r += (size_t)gridDim.x * blockDim.x) {
+    const uint64_t u = mix64(ks + (r + 1) * 0x9E3779B97F4A7C15ULL);
+    const float f = __fmul_rn((float)(u >> 40), 0x1p-24f);
+    s[r] = __fadd_rn(1e-4f, __fmul_rn(f, 9e-4f));
+  }
+}
+
+__global__ void expf_eval_kernel(uint32_t lo, uint32_t count, float *out) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count;
+       i += gridDim.x * blockDim.x)
+    out[i] = expf_ref(__uint_as_float(lo + i));
+}
+
+}  // namespace
+
+cudaError_t launch_combine(const float *contrib, const float *resid, float *out, int T, int K,
+                           int H, uint32_t *status, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const size_t n = (size_t)T * H / ((H & 3) == 0 ? 4 : 1);
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
+  combine_kernel<<<blocks, 256, 0, s>>>(contrib, resid, out, T, K, H, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const float *x, float *out, int T, int H, float eps,
+                           uint32_t *status, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, out, T, H, eps, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_synth_expert(uint64_t seed, int layer, int expert, int H, int I, int8_t *w,
+                                float *sc, cudaStream_t s) {
+  const size_t nw = (size_t)3 * H * I, ns = (size_t)2 * I + H;
+  const uint64_t kw = synth_key(seed, 1, (uint32_t)layer, (uint32_t)expert);
+  const uint64_t ks = synth_key(seed, 2, (uint32_t)layer, (uint32_t)expert);
+  const int bw = (int)std::min<size_t>(((nw + 3) / 4 + 255) / 256, 148 * 16);
+  synth_weights_kernel<<<bw, 256, 0, s>>>(kw, nw, w);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  synth_scales_kernel<<<(int)((ns + 255) / 256), 256, 0, s>>>(ks, ns, sc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_expf_eval(uint32_t bits_lo, uint32_t count, float *out, cudaStream_t s) {
+  expf_eval_kernel<<<148 * 8, 256, 0, s>>>(bits_lo, count, out);
+  return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,784 @@
+// Host side of the C ABI declared in include/moe_b200.h.
+//
+// Ownership mirrors the reference: expert weights are borrowed device
+// pointers (GpuExpertWeights, src/gpu.rs:1552-1566); the handle owns its
+// device scratch and serialises calls with a mutex (src/gpu_expert.rs:241-261).
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace moe;
+
+namespace {
+
+void set_err(std::string &dst, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  dst = buf;
+}
+
+int sm_count_of(int device) {
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  return n;
+}
+
+template <typename T>
+cudaError_t dalloc(T **p, size_t count) {
+  return cudaMalloc(reinterpret_cast<void **>(p), std::max<size_t>(count, 1) * sizeof(T));
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// GpuExpertKernels drop-in
+// ---------------------------------------------------------------------------
+struct moe_expert_kernels {
+  int device = 0;
+  size_t H = 0, I = 0, max_experts = 0;
+  int sm_count = 148;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  std::string err;
+  float *d_in = nullptr, *d_act = nullptr, *d_out = nullptr;
+  const int8_t **d_wptr = nullptr;
+  const float **d_sptr = nullptr;
+  int32_t *d_seg = nullptr, *d_tok_shared = nullptr;
+  uint32_t *d_status = nullptr;
+  float *h_in = nullptr, *h_out = nullptr;
+  const void **h_ptrs = nullptr;  // pinned staging for the pointer arrays
+};
+
+extern "C" moe_status moe_expert_kernels_init(int device, size_t hidden, size_t intermediate,
+                                              size_t max_experts, moe_expert_kernels **out) {
+  if (!out) return MOE_ERR_INVALID;
+  *out = nullptr;
+  if (hidden == 0 || intermediate == 0 || max_experts == 0 || hidden > (1u << 20) ||
+      intermediate > (1u << 20) || max_experts > 4096)
+    return MOE_ERR_INVALID;
+  if (cudaSetDevice(device) != cudaSuccess) return MOE_ERR_CUDA;
+  auto *k = new moe_expert_kernels();
+  k->device = device;
+  k->H = hidden;
+  k->I = intermediate;
+  k->max_experts = max_experts;
+  k->sm_count = sm_count_of(device);
+  bool ok = cudaStreamCreateWithFlags(&k->stream, cudaStreamNonBlocking) == cudaSuccess;
+  ok = ok && dalloc(&k->d_in, max_experts * hidden) == cudaSuccess;
+  ok = ok && dalloc(&k->d_act, max_experts * intermediate) == cudaSuccess;
+  ok = ok && dalloc(&k->d_out, max_experts * hidden) == cudaSuccess;
+  ok = ok && dalloc(&k->d_wptr, max_experts) == cudaSuccess;
+  ok = ok && dalloc(&k->d_sptr, max_experts) == cudaSuccess;
+  ok = ok && dalloc(&k->d_seg, max_experts + 1) == cudaSuccess;
+  ok = ok && dalloc(&k->d_tok_shared, max_experts) == cudaSuccess;
+  ok = ok && dalloc(&k->d_status, 1) == cudaSuccess;
+  ok = ok && cudaMallocHost(&k->h_in, max_experts * hidden * sizeof(float)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&k->h_out, max_experts * hidden * sizeof(float)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&k->h_ptrs, 2 * max_experts * sizeof(void *)) == cudaSuccess;
+  if (ok) {
+    std::vector<int32_t> seg(max_experts + 1);
+    for (size_t i = 0; i <= max_experts; ++i) seg[i] = (int32_t)i;
+    ok = cudaMemcpy(k->d_seg, seg.data(), seg.size() * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    ok = ok && cudaMemset(k->d_tok_shared, 0, max_experts * 4) == cudaSuccess;
+    ok = ok && cudaMemset(k->d_status, 0, 4) == cudaSuccess;
+  }
+  if (!ok) {
+    moe_expert_kernels_destroy(k);
+    return MOE_ERR_NOMEM;
+  }
+  *out = k;
+  return MOE_OK;
+}
+
+extern "C" void moe_expert_kernels_destroy(moe_expert_kernels *k) {
+  if (!k) return;
+  {
+    DeviceGuard g(k->device);
+    if (k->stream) cudaStreamSynchronize(k->stream);
+    cudaFree(k->d_in);
+    cudaFree(k->d_act);
+    cudaFree(k->d_out);
+    cudaFree(k->d_wptr);
+    cudaFree(k->d_sptr);
+    cudaFree(k->d_seg);
+    cudaFree(k->d_tok_shared);
+    cudaFree(k->d_status);
+    cudaFreeHost(k->h_in);
+    cudaFreeHost(k->h_out);
+    cudaFreeHost(k->h_ptrs);
+    if (k->stream) cudaStreamDestroy(k->stream);
+  }
+  delete k;
+}
+
+extern "C" size_t moe_expert_kernels_max_experts(const moe_expert_kernels *k) {
+  return k ? k->max_experts : 0;
+}
+
+extern "C" const char *moe_expert_kernels_last_error(const moe_expert_kernels *k) {
+  return k ? k->err.c_str() : "null handle";
+}
+
+extern "C" moe_status moe_expert_forward_pairs(moe_expert_kernels *k, const void *const *d_weights,
+                                               const void *const *d_scales,
+                                               const size_t *weight_bytes,
+                                               const size_t *scale_bytes, size_t n,
+                                               const float *const *inputs, size_t n_inputs,
+                                               float *const *outputs) {
+  if (!k) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(k->mu);
+  const size_t H = k->H, I = k->I;
+  // Validation order follows src/gpu_expert.rs:383-403.
+  if (n_inputs != 1 && n_inputs != n) {
+    set_err(k->err, "expert/input count mismatch");
+    return MOE_ERR_INVALID;
+  }
+  if (n > k->max_experts) {
+    set_err(k->err, "expert/output count mismatch");
+    return MOE_ERR_INVALID;
+  }
+  if (n == 0) return MOE_OK;
+  if (!d_weights || !d_scales || !inputs || !outputs) {
+    set_err(k->err, "null pointer argument");
+    return MOE_ERR_INVALID;
+  }
+  for (size_t j = 0; j < n; ++j) {
+    if ((weight_bytes && weight_bytes[j] != 3 * H * I) ||
+        (scale_bytes && scale_bytes[j] != (2 * I + H) * 4)) {
+      set_err(k->err, "GPU expert compute supports INT8 experts of the loaded shape only");
+      return MOE_ERR_INVALID;
+    }
+    if (!d_weights[j] || !d_scales[j] || !outputs[j] || (j < n_inputs && !inputs[j])) {
+      set_err(k->err, "null expert, input or output pointer");
+      return MOE_ERR_INVALID;
+    }
+    if ((uintptr_t)d_scales[j] & 3) {
+      set_err(k->err, "expert scales must be 4-byte aligned");
+      return MOE_ERR_INVALID;
+    }
+  }
+  int vec = 1;
+  for (size_t j = 0; j < n; ++j) vec &= ((uintptr_t)d_weights[j] & 7) == 0;
+  DeviceGuard g(k->device);
+  for (size_t j = 0; j < n_inputs; ++j) memcpy(k->h_in + j * H, inputs[j], H * sizeof(float));
+  for (size_t j = 0; j < n; ++j) {
+    k->h_ptrs[j] = d_weights[j];
+    k->h_ptrs[k->max_experts + j] = d_scales[j];
+  }
+  cudaStream_t s = k->stream;
+  cudaMemcpyAsync(k->d_in, k->h_in, n_inputs * H * sizeof(float), cudaMemcpyHostToDevice, s);
+  cudaMemcpyAsync(k->d_wptr, k->h_ptrs, n * sizeof(void *), cudaMemcpyHostToDevice, s);
+  cudaMemcpyAsync(k->d_sptr, k->h_ptrs + k->max_experts, n * sizeof(void *),
+                  cudaMemcpyHostToDevice, s);
+  GemvArgs a{};
+  a.H = (int)H;
+  a.I = (int)I;
+  a.w_ptr = k->d_wptr;
+  a.s_ptr = k->d_sptr;
+  a.active = nullptr;
+  a.n_active_dev = nullptr;
+  a.n_active_max = (int)n;
+  a.seg_off = k->d_seg;
+  a.r_token = n_inputs == 1 ? k->d_tok_shared : nullptr;
+  a.x = k->d_in;
+  a.act = k->d_act;
+  a.y = k->d_out;
+  a.status = k->d_status;
+  a.sm_count = k->sm_count;
+  a.vec = vec;
+  cudaError_t e = launch_gate_up(a, s);
+  if (e == cudaSuccess) e = launch_down(a, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(k->h_out, k->d_out, n * H * sizeof(float), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    set_err(k->err, "CUDA error in expert kernels: %s", cudaGetErrorString(e));
+    return MOE_ERR_CUDA;
+  }
+  uint32_t st = 0;
+  cudaMemcpy(&st, k->d_status, 4, cudaMemcpyDeviceToHost);
+  if (st) cudaMemset(k->d_status, 0, 4);
+  for (size_t j = 0; j < n; ++j) memcpy(outputs[j], k->h_out + j * H, H * sizeof(float));
+  for (size_t i = 0; i < n * H; ++i)
+    if (!std::isfinite(k->h_out[i])) {
+      set_err(k->err, "GPU expert output is not finite");
+      return MOE_ERR_NONFINITE;
+    }
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_expert_forward(moe_expert_kernels *k, const void *const *d_weights,
+                                         const void *const *d_scales, const size_t *weight_bytes,
+                                         const size_t *scale_bytes, size_t n, const float *input,
+                                         float *const *outputs) {
+  const float *inputs[1] = {input};
+  return moe_expert_forward_pairs(k, d_weights, d_scales, weight_bytes, scale_bytes, n, inputs, 1,
+                                  outputs);
+}
+
+// ---------------------------------------------------------------------------
+// MoE layer handle
+// ---------------------------------------------------------------------------
+namespace {
+// CUDA-event bracketing of kernel launches (moe_profile_*).
+struct Profiler {
+  bool on = false;
+  struct Rec {
+    const char *name;
+    cudaEvent_t a, b;
+  };
+  std::vector<cudaEvent_t> pool;
+  size_t used = 0;
+  std::vector<Rec> recs;
+  cudaEvent_t take() {
+    if (used == pool.size()) {
+      cudaEvent_t e;
+      if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+      pool.push_back(e);
+    }
+    return pool[used++];
+  }
+  // Returns the start event (or null when off / out of events).
+  cudaEvent_t begin(cudaStream_t s) {
+    if (!on || recs.size() >= 1 << 16) return nullptr;
+    cudaEvent_t a = take();
+    if (a) cudaEventRecord(a, s);
+    return a;
+  }
+  void end(const char *name, cudaEvent_t a, cudaStream_t s) {
+    if (!a) return;
+    cudaEvent_t b = take();
+    if (!b) return;
+    cudaEventRecord(b, s);
+    recs.push_back({name, a, b});
+  }
+  ~Profiler() {
+    for (auto e : pool) cudaEventDestroy(e);
+  }
+};
+
+struct LayerSlot {
+  bool set = false;
+  const int8_t **d_wptr = nullptr;  // device array [E]
+  const float **d_sptr = nullptr;   // device array [E]
+  const void *router = nullptr;
+  int router_dtype = MOE_ROUTER_F32;
+  int vec = 0;  // all expert bases 8-byte aligned -> vector weight loads
+};
+}  // namespace
+
+struct moe_handle {
+  int device = 0;
+  moe_dims d{};
+  int sm_count = 148;
+  cudaStream_t own_stream = nullptr, stream = nullptr;
+  int route_mode = MOE_ROUTE_SOFTMAX_TOPK;
+  int path = MOE_PATH_AUTO;
+  std::mutex mu;
+  std::string err;
+  std::vector<LayerSlot> layers;
+  // scratch
+  float *logits = nullptr, *gates = nullptr, *r_gate = nullptr, *act = nullptr,
+        *contrib = nullptr, *hbuf = nullptr, *io_in = nullptr, *io_out = nullptr,
+        *io_resid = nullptr;
+  uint32_t *ids = nullptr, *status = nullptr;
+  int32_t *seg_off = nullptr, *active = nullptr, *n_active = nullptr, *r_token = nullptr,
+          *r_slot = nullptr, *r_pos = nullptr;
+  float *h_pin_in = nullptr, *h_pin_out = nullptr;
+  int last_launches = 0;
+  Profiler prof;
+};
+
+namespace {
+
+void free_handle(moe_handle *h) {
+  for (auto &l : h->layers) {
+    cudaFree(l.d_wptr);
+    cudaFree(l.d_sptr);
+  }
+  void *ptrs[] = {h->logits, h->gates, h->r_gate, h->act,    h->contrib, h->hbuf,
+                  h->io_in,  h->io_out, h->io_resid, h->ids, h->status,  h->seg_off,
+                  h->active, h->n_active, h->r_token, h->r_slot, h->r_pos};
+  for (void *p : ptrs) cudaFree(p);
+  cudaFreeHost(h->h_pin_in);
+  cudaFreeHost(h->h_pin_out);
+  if (h->own_stream) cudaStreamDestroy(h->own_stream);
+}
+
+cudaStream_t pick(moe_handle *h, void *stream) {
+  return stream ? reinterpret_cast<cudaStream_t>(stream) : h->stream;
+}
+
+moe_status cuda_fail(moe_handle *h, cudaError_t e, const char *what) {
+  set_err(h->err, "%s: %s", what, cudaGetErrorString(e));
+  return MOE_ERR_CUDA;
+}
+
+// Router + top-k + permutation for T tokens of `layer`.
+moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T, uint32_t *ids,
+                     float *gates, float *probs, cudaStream_t s, bool permute) {
+  RouteArgs ra{};
+  ra.h = d_h;
+  ra.router = L.router;
+  ra.router_dtype = L.router_dtype;
+  if (h->route_mode == MOE_ROUTE_TOPK_SOFTMAX && L.router_dtype == MOE_ROUTER_F32)
+    ra.router_dtype = kRouterF32Seq;  // src/router.rs:59-62 sequential dot
+  ra.T = T;
+  ra.H = h->d.hidden;
+  ra.E = h->d.num_experts;
+  ra.K = h->d.top_k;
+  ra.norm_topk_prob = h->d.norm_topk_prob;
+  ra.mode = h->route_mode;
+  ra.logits = h->logits;
+  ra.ids = ids;
+  ra.gates = gates;
+  ra.probs = probs;
+  ra.status = h->status;
+  cudaEvent_t p0 = h->prof.begin(s);
+  cudaError_t e = launch_route(ra, s);
+  h->prof.end("route", p0, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "route launch");
+  h->last_launches += 2;
+  if (!permute) return MOE_OK;
+  PermuteArgs pa{};
+  pa.ids = ids;
+  pa.gates = gates;
+  pa.T = T;
+  pa.K = h->d.top_k;
+  pa.E = h->d.num_experts;
+  pa.seg_off = h->seg_off;
+  pa.active = h->active;
+  pa.n_active = h->n_active;
+  pa.r_token = h->r_token;
+  pa.r_slot = h->r_slot;
+  pa.r_gate = h->r_gate;
+  pa.r_pos = h->r_pos;
+  pa.status = h->status;
+  p0 = h->prof.begin(s);
+  e = launch_permute(pa, s);
+  h->prof.end("permute", p0, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "permute launch");
+  h->last_launches += 1;
+  return MOE_OK;
+}
+
+moe_status check_layer(moe_handle *h, int layer, int T) {
+  if (layer < 0 || layer >= (int)h->layers.size()) {
+    set_err(h->err, "layer %d out of range [0, %d)", layer, (int)h->layers.size());
+    return MOE_ERR_INVALID;
+  }
+  if (!h->layers[layer].set) {
+    set_err(h->err, "layer %d has no weights", layer);
+    return MOE_ERR_STATE;
+  }
+  if (T < 0 || T > h->d.max_tokens) {
+    set_err(h->err, "token count %d outside [0, %d]", T, h->d.max_tokens);
+    return MOE_ERR_INVALID;
+  }
+  return MOE_OK;
+}
+
+moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, const float *d_resid,
+                                float *d_out, int T, uint32_t *d_ids, float *d_gates,
+                                cudaStream_t s) {
+  const LayerSlot &L = h->layers[layer];
+  uint32_t *ids = d_ids ? d_ids : h->ids;
+  float *gates = d_gates ? d_gates : h->gates;
+  moe_status st = run_route(h, L, d_h, T, ids, gates, nullptr, s, true);
+  if (st != MOE_OK) return st;
+  GemvArgs a{};
+  a.H = h->d.hidden;
+  a.I = h->d.intermediate;
+  a.w_ptr = L.d_wptr;
+  a.s_ptr = L.d_sptr;
+  a.active = h->active;
+  a.n_active_dev = h->n_active;
+  a.n_active_max = std::min(h->d.num_experts, T * h->d.top_k);
+  a.seg_off = h->seg_off;
+  a.r_token = h->r_token;
+  a.x = d_h;
+  a.act = h->act;
+  a.r_slot = h->r_slot;
+  a.r_gate = h->r_gate;
+  a.K = h->d.top_k;
+  a.contrib = h->contrib;
+  a.status = h->status;
+  a.sm_count = h->sm_count;
+  a.vec = L.vec && ((uintptr_t)d_h & 15) == 0;
+  cudaEvent_t p0 = h->prof.begin(s);
+  cudaError_t e = launch_gate_up(a, s);
+  h->prof.end("gate_up_gemv", p0, s);
+  if (e == cudaSuccess) {
+    p0 = h->prof.begin(s);
+    e = launch_down(a, s);
+    h->prof.end("down_gemv", p0, s);
+  }
+  if (e == cudaSuccess) {
+    p0 = h->prof.begin(s);
+    e = launch_combine(h->contrib, d_resid, d_out, T, h->d.top_k, h->d.hidden, h->status, s);
+    h->prof.end("combine", p0, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(h, e, "expert launch");
+  h->last_launches += 3;
+  return MOE_OK;
+}
+
+}  // namespace
+
+extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **out) {
+  if (!out || !dims) return MOE_ERR_INVALID;
+  *out = nullptr;
+  const moe_dims &d = *dims;
+  if (d.hidden <= 0 || d.intermediate <= 0 || d.num_experts <= 0 || d.num_experts > kMaxExperts ||
+      d.top_k <= 0 || d.top_k > kMaxTopK || d.top_k > d.num_experts || d.max_tokens <= 0 ||
+      d.num_layers <= 0 || d.hidden > (1 << 16) || d.intermediate > (1 << 16))
+    return MOE_ERR_INVALID;
+  if (cudaSetDevice(device) != cudaSuccess) return MOE_ERR_CUDA;
+  auto *h = new moe_handle();
+  h->device = device;
+  h->d = d;
+  h->sm_count = sm_count_of(device);
+  h->layers.resize(d.num_layers);
+  const size_t T = d.max_tokens, H = d.hidden, I = d.intermediate, E = d.num_experts,
+               K = d.top_k;
+  bool ok = cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) == cudaSuccess;
+  h->stream = h->own_stream;
+  ok = ok && dalloc(&h->logits, T * E) == cudaSuccess;
+  ok = ok && dalloc(&h->ids, T * K) == cudaSuccess;
+  ok = ok && dalloc(&h->gates, T * K) == cudaSuccess;
+  ok = ok && dalloc(&h->r_gate, T * K) == cudaSuccess;
+  ok = ok && dalloc(&h->r_token, T * K) == cudaSuccess;
+  ok = ok && dalloc(&h->r_slot, T * K) == cudaSuccess;
+  ok = ok && dalloc(&h->r_pos, T * K) == cudaSuccess;
+  ok = ok && dalloc(&h->seg_off, E + 1) == cudaSuccess;
+  ok = ok && dalloc(&h->active, E) == cudaSuccess;
+  ok = ok && dalloc(&h->n_active, 1) == cudaSuccess;
+  ok = ok && dalloc(&h->act, T * K * I) == cudaSuccess;
+  ok = ok && dalloc(&h->contrib, T * K * H) == cudaSuccess;
+  ok = ok && dalloc(&h->hbuf, T * H) == cudaSuccess;
+  ok = ok && dalloc(&h->io_in, T * H) == cudaSuccess;
+  ok = ok && dalloc(&h->io_out, T * H) == cudaSuccess;
+  ok = ok && dalloc(&h->io_resid, T * H) == cudaSuccess;
+  ok = ok && dalloc(&h->status, 1) == cudaSuccess;
+  ok = ok && cudaMallocHost(&h->h_pin_in, 2 * T * H * sizeof(float)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&h->h_pin_out, T * H * sizeof(float)) == cudaSuccess;
+  ok = ok && cudaMemset(h->status, 0, 4) == cudaSuccess;
+  if (!ok) {
+    free_handle(h);
+    delete h;
+    return MOE_ERR_NOMEM;
+  }
+  *out = h;
+  return MOE_OK;
+}
+
+extern "C" void moe_destroy(moe_handle *h) {
+  if (!h) return;
+  {
+    DeviceGuard g(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    free_handle(h);
+  }
+  delete h;
+}
+
+extern "C" const char *moe_last_error(const moe_handle *h) {
+  return h ? h->err.c_str() : "null handle";
+}
+
+extern "C" moe_status moe_set_stream(moe_handle *h, void *cuda_stream) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->stream = cuda_stream ? reinterpret_cast<cudaStream_t>(cuda_stream) : h->own_stream;
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_set_route_mode(moe_handle *h, int mode) {
+  if (!h || (mode != MOE_ROUTE_SOFTMAX_TOPK && mode != MOE_ROUTE_TOPK_SOFTMAX))
+    return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->route_mode = mode;
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_set_path(moe_handle *h, int path) {
+  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_TENSOR) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->path = path;
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const *d_weights,
+                                    const void *const *d_scales, const void *d_router,
+                                    int router_dtype) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (layer < 0 || layer >= (int)h->layers.size() || !d_weights || !d_scales || !d_router ||
+      (router_dtype != MOE_ROUTER_F32 && router_dtype != MOE_ROUTER_BF16)) {
+    set_err(h->err, "moe_set_layer: invalid argument");
+    return MOE_ERR_INVALID;
+  }
+  const int E = h->d.num_experts;
+  int vec = 1;
+  for (int e = 0; e < E; ++e) {
+    if (!d_weights[e] || !d_scales[e] || ((uintptr_t)d_scales[e] & 3)) {
+      set_err(h->err, "expert %d: null pointer or scales not 4-byte aligned", e);
+      return MOE_ERR_INVALID;
+    }
+    vec &= ((uintptr_t)d_weights[e] & 7) == 0;
+  }
+  DeviceGuard g(h->device);
+  LayerSlot &L = h->layers[layer];
+  if (!L.d_wptr && (dalloc(&L.d_wptr, E) != cudaSuccess || dalloc(&L.d_sptr, E) != cudaSuccess))
+    return MOE_ERR_NOMEM;
+  cudaError_t e1 = cudaMemcpy(L.d_wptr, d_weights, E * sizeof(void *), cudaMemcpyHostToDevice);
+  cudaError_t e2 = cudaMemcpy(L.d_sptr, d_scales, E * sizeof(void *), cudaMemcpyHostToDevice);
+  if (e1 != cudaSuccess || e2 != cudaSuccess) return cuda_fail(h, e1 ? e1 : e2, "set_layer");
+  L.router = d_router;
+  L.router_dtype = router_dtype;
+  L.vec = vec;
+  L.set = true;
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_set_layer_packed(moe_handle *h, int layer, const int8_t *d_experts,
+                                           const float *d_scales, const void *d_router,
+                                           int router_dtype) {
+  if (!h || !d_experts || !d_scales) return MOE_ERR_INVALID;
+  const size_t E = h->d.num_experts, H = h->d.hidden, I = h->d.intermediate;
+  std::vector<const void *> w(E), s(E);
+  for (size_t e = 0; e < E; ++e) {
+    w[e] = d_experts + e * 3 * I * H;
+    s[e] = d_scales + e * (2 * I + H);
+  }
+  return moe_set_layer(h, layer, w.data(), s.data(), d_router, router_dtype);
+}
+
+extern "C" moe_status moe_route(moe_handle *h, int layer, const float *d_h, int T,
+                                uint32_t *d_ids, float *d_gates, float *d_probs, void *stream) {
+  if (!h || !d_h || !d_ids || !d_gates) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  moe_status st = check_layer(h, layer, T);
+  if (st != MOE_OK || T == 0) return st;
+  DeviceGuard g(h->device);
+  h->last_launches = 0;
+  return run_route(h, h->layers[layer], d_h, T, d_ids, d_gates, d_probs, pick(h, stream), false);
+}
+
+extern "C" moe_status moe_route_permute(moe_handle *h, int layer, const float *d_h, int T,
+                                        uint32_t *d_ids, float *d_gates, int32_t *d_seg_off,
+                                        int32_t *d_route_token, int32_t *d_route_slot,
+                                        void *stream) {
+  if (!h || !d_h || !d_ids || !d_gates || !d_seg_off || !d_route_token || !d_route_slot)
+    return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  moe_status st = check_layer(h, layer, T);
+  if (st != MOE_OK || T == 0) return st;
+  DeviceGuard g(h->device);
+  h->last_launches = 0;
+  cudaStream_t s = pick(h, stream);
+  st = run_route(h, h->layers[layer], d_h, T, d_ids, d_gates, nullptr, s, true);
+  if (st != MOE_OK) return st;
+  const size_t R = (size_t)T * h->d.top_k;
+  cudaMemcpyAsync(d_seg_off, h->seg_off, (h->d.num_experts + 1) * 4, cudaMemcpyDeviceToDevice, s);
+  cudaMemcpyAsync(d_route_token, h->r_token, R * 4, cudaMemcpyDeviceToDevice, s);
+  cudaError_t e = cudaMemcpyAsync(d_route_slot, h->r_slot, R * 4, cudaMemcpyDeviceToDevice, s);
+  return e == cudaSuccess ? MOE_OK : cuda_fail(h, e, "route_permute copy");
+}
+
+extern "C" moe_status moe_layer_forward(moe_handle *h, int layer, const float *d_h,
+                                        const float *d_resid, float *d_out, int T,
+                                        uint32_t *d_ids, float *d_gates, void *stream) {
+  if (!h || !d_h || !d_out) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  moe_status st = check_layer(h, layer, T);
+  if (st != MOE_OK || T == 0) return st;
+  DeviceGuard g(h->device);
+  h->last_launches = 0;
+  return layer_forward_locked(h, layer, d_h, d_resid, d_out, T, d_ids, d_gates, pick(h, stream));
+}
+
+extern "C" moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_layers, float *d_x,
+                                        int T, float rms_eps, void *stream) {
+  if (!h || !d_x || n_layers <= 0) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  for (int l = first_layer; l < first_layer + n_layers; ++l) {
+    moe_status st = check_layer(h, l, T);
+    if (st != MOE_OK) return st;
+  }
+  if (T == 0) return MOE_OK;
+  DeviceGuard g(h->device);
+  cudaStream_t s = pick(h, stream);
+  h->last_launches = 0;
+  for (int l = first_layer; l < first_layer + n_layers; ++l) {
+    cudaEvent_t p0 = h->prof.begin(s);
+    cudaError_t e = launch_rmsnorm(d_x, h->hbuf, T, h->d.hidden, rms_eps, h->status, s);
+    h->prof.end("rmsnorm", p0, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
+    h->last_launches += 1;
+    moe_status st = layer_forward_locked(h, l, h->hbuf, d_x, d_x, T, nullptr, nullptr, s);
+    if (st != MOE_OK) return st;
+  }
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_sync_status(moe_handle *h, void *stream) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  DeviceGuard g(h->device);
+  cudaStream_t s = pick(h, stream);
+  uint32_t st = 0;
+  cudaError_t e = cudaMemcpyAsync(&st, h->status, 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "sync_status");
+  if (st) cudaMemsetAsync(h->status, 0, 4, s);
+  if (st & kStatusTimeout) {
+    set_err(h->err, "device wait timed out");
+    return MOE_ERR_TIMEOUT;
+  }
+  if (st & kStatusNonFinite) {
+    set_err(h->err, "non-finite computation result");
+    return MOE_ERR_NONFINITE;
+  }
+  if (st & kStatusBadRoute) {
+    set_err(h->err, "routing produced an invalid expert id");
+    return MOE_ERR_INVALID;
+  }
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_layer_forward_host(moe_handle *h, int layer, const float *h_in,
+                                             const float *h_resid, float *h_out, int T,
+                                             uint32_t *h_ids, float *h_gates) {
+  if (!h || !h_in || !h_out) return MOE_ERR_INVALID;
+  moe_status st;
+  {
+    std::lock_guard<std::mutex> lock(h->mu);
+    st = check_layer(h, layer, T);
+    if (st != MOE_OK || T == 0) return st;
+    DeviceGuard g(h->device);
+    cudaStream_t s = h->stream;
+    const size_t n = (size_t)T * h->d.hidden;
+    const size_t R = (size_t)T * h->d.top_k;
+    memcpy(h->h_pin_in, h_in, n * sizeof(float));
+    cudaMemcpyAsync(h->io_in, h->h_pin_in, n * sizeof(float), cudaMemcpyHostToDevice, s);
+    if (h_resid) {
+      memcpy(h->h_pin_in + n, h_resid, n * sizeof(float));
+      cudaMemcpyAsync(h->io_resid, h->h_pin_in + n, n * sizeof(float), cudaMemcpyHostToDevice, s);
+    }
+    h->last_launches = 0;
+    st = layer_forward_locked(h, layer, h->io_in, h_resid ? h->io_resid : nullptr, h->io_out, T,
+                              h->ids, h->gates, s);
+    if (st != MOE_OK) return st;
+    cudaMemcpyAsync(h->h_pin_out, h->io_out, n * sizeof(float), cudaMemcpyDeviceToHost, s);
+    if (h_ids) cudaMemcpyAsync(h_ids, h->ids, R * 4, cudaMemcpyDeviceToHost, s);
+    if (h_gates) cudaMemcpyAsync(h_gates, h->gates, R * 4, cudaMemcpyDeviceToHost, s);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "layer_forward_host");
+    memcpy(h_out, h->h_pin_out, n * sizeof(float));
+  }
+  return moe_sync_status(h, nullptr);
+}
+
+extern "C" int moe_last_launch_count(const moe_handle *h) { return h ? h->last_launches : 0; }
+
+extern "C" moe_status moe_synth_expert(uint64_t seed, int layer, int expert, int hidden,
+                                       int intermediate, int8_t *d_weights, float *d_scales,
+                                       void *stream) {
+  if (!d_weights || !d_scales || hidden <= 0 || intermediate <= 0) return MOE_ERR_INVALID;
+  cudaError_t e = launch_synth_expert(seed, layer, expert, hidden, intermediate, d_weights,
+                                      d_scales, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+extern "C" moe_status moe_debug_expf(uint32_t bits_lo, uint32_t count, float *d_out,
+                                     void *stream) {
+  if (!d_out) return MOE_ERR_INVALID;
+  cudaError_t e = launch_expf_eval(bits_lo, count, d_out, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+extern "C" moe_status moe_profile_enable(moe_handle *h, int enable) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->prof.on = enable != 0;
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int max_entries,
+                                       int *n_entries) {
+  if (!h || !n_entries || (max_entries > 0 && !out)) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  DeviceGuard g(h->device);
+  std::vector<moe_kernel_time> acc;
+  for (auto &r : h->prof.recs) {
+    if (cudaEventSynchronize(r.b) != cudaSuccess) return cuda_fail(h, cudaGetLastError(), "profile");
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    auto it = std::find_if(acc.begin(), acc.end(),
+                           [&](const moe_kernel_time &k) { return strcmp(k.name, r.name) == 0; });
+    if (it == acc.end()) {
+      moe_kernel_time k{};
+      snprintf(k.name, sizeof k.name, "%s", r.name);
+      acc.push_back(k);
+      it = acc.end() - 1;
+    }
+    it->launches += 1;
+    it->total_ms += ms;
+  }
+  h->prof.recs.clear();
+  h->prof.used = 0;
+  const int n = std::min<int>((int)acc.size(), max_entries);
+  for (int i = 0; i < n; ++i) out[i] = acc[i];
+  *n_entries = (int)acc.size();
+  return MOE_OK;
+}
+
+// Same stream of numbers as the test-side generator: splitmix64 counters,
+// Box-Muller in double precision.
+extern "C" moe_status moe_synth_normal_host(uint64_t seed, uint32_t kind, uint32_t layer,
+                                            size_t n, float stddev, float *out) {
+  if (!out) return MOE_ERR_INVALID;
+  auto mix = [](uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    return z ^ (z >> 31);
+  };
+  const uint64_t k0 = mix(seed ^ 0x6a09e667f3bcc909ULL);
+  const uint64_t key = mix(k0 ^ ((uint64_t)kind << 48) ^ ((uint64_t)layer << 24));
+  auto at = [&](uint64_t i) { return mix(key + (i + 1) * 0x9E3779B97F4A7C15ULL); };
+  for (size_t j = 0; 2 * j < n; ++j) {
+    const double a = (double)((at(2 * j) >> 11) + 1) * 0x1p-53;
+    const double b = (double)(at(2 * j + 1) >> 11) * 0x1p-53;
+    const double r = std::sqrt(-2.0 * std::log(a));
+    const double th = 6.283185307179586 * b;
+    out[2 * j] = (float)((double)stddev * r * std::cos(th));
+    if (2 * j + 1 < n) out[2 * j + 1] = (float)((double)stddev * r * std::sin(th));
+  }
+  return MOE_OK;
+}

@@ -1,0 +1,315 @@
+// Router projection, softmax, top-k and the by-expert permutation.
+//
+// Reference semantics (juanhuy/DoanTotNghiepMOE):
+//   logits   src/backend.rs:105-120 (`dot_product`: 8 lane accumulators over
+//            chunks of 8, lanes folded in order, sequential tail) and
+//            src/dense.rs:58-73 (`dot_bf16`, same order on widened BF16);
+//   softmax  src/backend.rs:375-389 (max, exp(x - max), sequential sum, divide);
+//   top-k    src/olmoe.rs:2595-2621 (total_cmp descending, ties -> lower id,
+//            normalizer = sequential sum of the selected p when norm_topk_prob);
+//   variant  src/router.rs:50-103 (`route_hidden`: sequential dot, sort by
+//            score, softmax over the kept k);
+//   permute  src/olmoe.rs:3474-3480 (`expert_uses`: experts ascending, tokens
+//            ascending within an expert).
+// Every floating-point step is the same IEEE operation in the same order, so
+// logits, probabilities, ids and gates are bit-identical to the CPU path.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace moe {
+namespace {
+
+constexpr int kRouteThreads = 256;
+constexpr int kChunkCols = 256;  // columns of h / W staged per smem pass
+
+__device__ __forceinline__ float load_w(const void *W, int dtype, size_t idx) {
+  if (dtype == kRouterBF16) {
+    const uint16_t v = reinterpret_cast<const uint16_t *>(W)[idx];
+    return __uint_as_float((uint32_t)v << 16);
+  }
+  return reinterpret_cast<const float *>(W)[idx];
+}
+
+// One CTA computes logits for a tile of TT tokens x TE experts.  Thread
+// (t, e, lane) owns accumulator `lane` of the 8-lane chain for (t, e).  All
+// 256 threads stage h / W columns through shared memory; the first
+// 8*TE*TT threads run the chains.
+template <int TT, int TE>
+__global__ void __launch_bounds__(kRouteThreads) route_logits_kernel(RouteArgs a) {
+  __shared__ float hs[TT][kChunkCols];
+  __shared__ float ws[TE][kChunkCols];
+  const int tid = threadIdx.x;
+  const int e0 = blockIdx.x * TE, t0 = blockIdx.y * TT;
+  const int lane = tid & 7;
+  const int el = (tid >> 3) % TE;
+  const int tl = tid / (8 * TE);
+  const bool worker = tid < 8 * TE * TT;
+  const int H = a.H;
+  const int full = H / 8;  // complete chunks of eight
+  // Rust's f32 `Sum` folds from -0.0; the 8-lane chains start at 0.0
+  // (`[0.0f32; 8]`, src/backend.rs:107).
+  float acc = a.router_dtype == kRouterF32Seq ? -0.0f : 0.0f;
+  bool bad_input = false;
+  for (int c0 = 0; c0 < H; c0 += kChunkCols) {
+    const int ncol = min(kChunkCols, H - c0);
+    for (int i = tid; i < TT * kChunkCols; i += kRouteThreads) {
+      const int r = i / kChunkCols, c = i % kChunkCols;
+      float v = 0.0f;
+      if (t0 + r < a.T && c < ncol) {
+        v = a.h[(size_t)(t0 + r) * H + c0 + c];
+        if (blockIdx.x == 0 && !is_finite_f(v)) bad_input = true;
+      }
+      hs[r][c] = v;
+    }
+    for (int i = tid; i < TE * kChunkCols; i += kRouteThreads) {
+      const int r = i / kChunkCols, c = i % kChunkCols;
+      ws[r][c] = (e0 + r < a.E && c < ncol) ? load_w(a.router, a.router_dtype,
+                                                     (size_t)(e0 + r) * H + c0 + c)
+                                            : 0.0f;
+    }
+    __syncthreads();
+    if (worker) {
+      const int nchunk = min(ncol, full * 8 - c0) / 8;  // complete chunks in this pass
+      if (a.router_dtype == kRouterF32Seq) {
+        // src/router.rs:59-62: one sequential chain; lane 0 carries it.
+        if (lane == 0)
+          for (int c = 0; c < ncol; ++c) acc = __fadd_rn(acc, __fmul_rn(ws[el][c], hs[tl][c]));
+      } else {
+#pragma unroll 8
+        for (int c = 0; c < nchunk; ++c)
+          acc = __fadd_rn(acc, __fmul_rn(ws[el][8 * c + lane], hs[tl][8 * c + lane]));
+      }
+    }
+    __syncthreads();
+  }
+  if (bad_input) set_status(a.status, kStatusNonFinite);
+  if (!worker) return;
+  const int t = t0 + tl, e = e0 + el;
+  float logit;
+  if (a.router_dtype == kRouterF32Seq) {
+    logit = acc;
+  } else {
+    // Fold the 8 lanes in order starting from -0.0, then the tail.
+    float s = -0.0f;
+    const int base = (threadIdx.x & 31) & ~7;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc, base + l));
+    logit = s;
+    if (lane == 0 && t < a.T && e < a.E)
+      for (int i = full * 8; i < H; ++i)
+        logit = __fadd_rn(logit, __fmul_rn(load_w(a.router, a.router_dtype, (size_t)e * H + i),
+                                           a.h[(size_t)t * H + i]));
+  }
+  if (lane == 0 && t < a.T && e < a.E) {
+    a.logits[(size_t)t * a.E + e] = logit;
+    if (!is_finite_f(logit)) set_status(a.status, kStatusNonFinite);
+  }
+}
+
+// One warp per token: softmax over all E in index order, then K rounds of a
+// warp-wide argmax on (total_cmp key, lower index first).
+__global__ void __launch_bounds__(256) route_select_kernel(RouteArgs a) {
+  __shared__ float ex_s[8][kMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= a.T) return;
+  const int E = a.E, K = a.K;
+  constexpr int kPer = kMaxExperts / 32;
+  float v[kPer];
+  const float *lg = a.logits + (size_t)t * E;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < E ? lg[e] : __int_as_float(0xff800000);  // -inf pad
+  }
+  if (a.mode == kRouteSoftmaxTopk) {
+    float mx = __int_as_float(0xff800000);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) mx = fmaxf(mx, v[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E) {
+        v[j] = expf_ref(__fsub_rn(v[j], mx));
+        ex_s[warp][e] = v[j];
+      }
+    }
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0) {
+      sum = -0.0f;
+      for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, ex_s[warp][e]);
+    }
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E) {
+        v[j] = __fdiv_rn(v[j], sum);
+        if (a.probs) a.probs[(size_t)t * E + e] = v[j];
+      }
+    }
+  } else {
+    // partial_cmp treats -0.0 == +0.0; canonicalise zero so the total-order
+    // key ties them (and the lower index wins, as in the reference sort).
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (v[j] == 0.0f) v[j] = 0.0f;
+  }
+  // K rounds of argmax.  Key: order-preserving bits of the value, then the
+  // complement of the index so that equal values prefer the lower index.
+  __shared__ float sel_v[8][kMaxTopK];
+  __shared__ uint32_t sel_i[8][kMaxTopK];
+  uint32_t taken = 0;  // bit j set when candidate j of this lane was selected
+  for (int k = 0; k < K; ++k) {
+    unsigned long long best = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !(taken & (1u << j))) {
+        const unsigned long long key =
+            ((unsigned long long)total_order_u32(v[j]) << 32) | (uint32_t)(0xFFFFFFFFu - e);
+        best = key > best ? key : best;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    const uint32_t e = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
+    if ((int)(e & 31) == lane) {
+      const int j = (int)(e >> 5);
+      taken |= 1u << j;
+      float val = 0.0f;
+#pragma unroll
+      for (int jj = 0; jj < kPer; ++jj)
+        if (jj == j) val = v[jj];
+      sel_v[warp][k] = val;
+      sel_i[warp][k] = e;
+    }
+    __syncwarp();
+  }
+  if (lane == 0) {
+    uint32_t *ids = a.ids + (size_t)t * K;
+    float *gates = a.gates + (size_t)t * K;
+    if (a.mode == kRouteSoftmaxTopk) {
+      float norm = 1.0f;
+      if (a.norm_topk_prob) {
+        norm = -0.0f;
+        for (int k = 0; k < K; ++k) norm = __fadd_rn(norm, sel_v[warp][k]);
+      }
+      for (int k = 0; k < K; ++k) {
+        ids[k] = sel_i[warp][k];
+        gates[k] = __fdiv_rn(sel_v[warp][k], norm);
+        if (sel_i[warp][k] >= (uint32_t)E) set_status(a.status, kStatusBadRoute);
+      }
+    } else {
+      const float mx = sel_v[warp][0];
+      float total = -0.0f;
+      float ex[kMaxTopK];
+      for (int k = 0; k < K; ++k) {
+        ex[k] = expf_ref(__fsub_rn(sel_v[warp][k], mx));
+        total = __fadd_rn(total, ex[k]);
+      }
+      for (int k = 0; k < K; ++k) {
+        ids[k] = sel_i[warp][k];
+        gates[k] = __fdiv_rn(ex[k], total);
+      }
+    }
+  }
+}
+
+// Single-CTA stable counting sort of the T*K routes by expert.
+constexpr int kPermThreads = 1024;
+__global__ void __launch_bounds__(kPermThreads) permute_kernel(PermuteArgs a) {
+  __shared__ int32_t cnt[kMaxExperts + 1];
+  __shared__ int32_t run[kMaxExperts];
+  __shared__ int32_t wcnt[kPermThreads / 32][kMaxExperts];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int E = a.E, R = a.T * a.K;
+  for (int e = tid; e <= E; e += kPermThreads) cnt[e] = 0;
+  for (int i = tid; i < (kPermThreads / 32) * kMaxExperts; i += kPermThreads)
+    (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  for (int r = tid; r < R; r += kPermThreads) {
+    const uint32_t e = a.ids[r];
+    if (e < (uint32_t)E) atomicAdd(&cnt[e], 1);
+    else set_status(a.status, kStatusBadRoute);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0, na = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = cnt[e];
+      a.seg_off[e] = acc;
+      run[e] = acc;
+      if (c > 0) a.active[na++] = e;
+      acc += c;
+    }
+    a.seg_off[E] = acc;
+    *a.n_active = na;
+  }
+  __syncthreads();
+  // Tiles of 1024 routes in route order; rank inside the tile from the warp
+  // match mask plus the per-warp counts of earlier warps.
+  for (int base = 0; base < R; base += kPermThreads) {
+    const int r = base + tid;
+    const bool valid = r < R;
+    const uint32_t e = valid ? a.ids[r] : 0xFFFFFFFFu;
+    const bool ok = valid && e < (uint32_t)E;
+    const uint32_t key = ok ? e : 0xFFFFFFFFu;
+    const unsigned mask = __match_any_sync(0xffffffffu, key);
+    const int intra = __popc(mask & ((1u << lane) - 1u));
+    if (ok && intra == 0) wcnt[warp][e] = __popc(mask);
+    __syncthreads();
+    if (ok) {
+      int pos = run[e] + intra;
+      for (int w = 0; w < warp; ++w) pos += wcnt[w][e];
+      const int t = r / a.K, slot = r % a.K;
+      a.r_token[pos] = t;
+      a.r_slot[pos] = slot;
+      if (a.r_gate) a.r_gate[pos] = a.gates[r];
+      if (a.r_pos) a.r_pos[r] = pos;
+    }
+    __syncthreads();
+    // advance the running offsets by this tile's totals, then clear
+    for (int ee = tid; ee < E; ee += kPermThreads) {
+      int tot = 0;
+      for (int w = 0; w < kPermThreads / 32; ++w) {
+        tot += wcnt[w][ee];
+        wcnt[w][ee] = 0;
+      }
+      run[ee] += tot;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_route(const RouteArgs &a, cudaStream_t s) {
+  if (a.T <= 0) return cudaSuccess;
+  if (a.T <= 4) {
+    constexpr int TT = 1, TE = 4;
+    dim3 grid((a.E + TE - 1) / TE, (a.T + TT - 1) / TT);
+    route_logits_kernel<TT, TE><<<grid, kRouteThreads, 0, s>>>(a);
+  } else {
+    constexpr int TT = 8, TE = 4;
+    dim3 grid((a.E + TE - 1) / TE, (a.T + TT - 1) / TT);
+    route_logits_kernel<TT, TE><<<grid, kRouteThreads, 0, s>>>(a);
+  }
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  route_select_kernel<<<(a.T + 7) / 8, 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t s) {
+  permute_kernel<<<1, kPermThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,166 @@
+"""Device MoE layer: router -> softmax -> top-k -> permutation -> INT8
+SwiGLU experts -> slot-ordered combine, behind the C ABI's ``moe_handle``.
+
+It replaces the MoE block of the reference's ``OlmoeModel::step_inner``
+(src/olmoe.rs:2583-3158) and ``OlmoeModel::prefill`` (:3417-3714).  Tensors are
+passed as CUDA tensors (torch provides device memory and streams only); every
+computation happens in libmoe_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import (MOE_OK, MOE_ROUTER_BF16, MOE_ROUTER_F32, MoeDims, MoeError, lib,
+                   ptr_array)
+
+
+@dataclass
+class MoeConfig:
+    hidden: int
+    intermediate: int
+    num_experts: int
+    top_k: int
+    norm_topk_prob: bool
+    max_tokens: int = 1
+    num_layers: int = 1
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        return None
+    return getattr(stream, "cuda_stream", stream)
+
+
+class MoeLayerEngine:
+    def __init__(self, cfg: MoeConfig, device: int = 0):
+        self.cfg = cfg
+        self.device = device
+        dims = MoeDims(cfg.hidden, cfg.intermediate, cfg.num_experts, cfg.top_k,
+                       int(cfg.norm_topk_prob), cfg.max_tokens, cfg.num_layers)
+        out = ctypes.c_void_p()
+        st = lib().moe_create(device, ctypes.byref(dims), ctypes.byref(out))
+        if st != MOE_OK:
+            raise MoeError(st, "moe_create failed")
+        self._h = out.value
+        self._keep = {}
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, st: int):
+        if st != MOE_OK:
+            msg = lib().moe_last_error(self._h)
+            raise MoeError(st, msg.decode() if msg else "")
+
+    # -- configuration ---------------------------------------------------
+    def set_stream(self, stream):
+        self._check(lib().moe_set_stream(self._h, _stream(stream)))
+
+    def set_route_mode(self, mode: int):
+        self._check(lib().moe_set_route_mode(self._h, mode))
+
+    def set_path(self, path: int):
+        self._check(lib().moe_set_path(self._h, path))
+
+    def set_layer_packed(self, layer: int, experts, scales, router):
+        """experts: CUDA int8 [E, 3*I*H]; scales: CUDA f32 [E, 2I+H]; router: CUDA
+        f32 [E, H] or int16/uint16-viewed bf16 bits [E, H]."""
+        import torch
+        dtype = MOE_ROUTER_F32 if router.dtype == torch.float32 else MOE_ROUTER_BF16
+        self._keep[layer] = (experts, scales, router)
+        self._check(lib().moe_set_layer_packed(self._h, layer, experts.data_ptr(),
+                                               scales.data_ptr(), router.data_ptr(), dtype))
+
+    def set_layer(self, layer: int, expert_weights: list, expert_scales: list, router):
+        """Per-expert device pointers (pool slots) -- the GpuExpertWeights borrow."""
+        import torch
+        dtype = MOE_ROUTER_F32 if router.dtype == torch.float32 else MOE_ROUTER_BF16
+        self._keep[layer] = (expert_weights, expert_scales, router)
+        w = ptr_array([t.data_ptr() for t in expert_weights])
+        s = ptr_array([t.data_ptr() for t in expert_scales])
+        self._check(lib().moe_set_layer(self._h, layer, w, s, router.data_ptr(), dtype))
+
+    # -- compute -----------------------------------------------------------
+    def route(self, layer: int, h, ids, gates, probs=None, stream=None):
+        self._check(lib().moe_route(self._h, layer, h.data_ptr(), h.shape[0], ids.data_ptr(),
+                                    gates.data_ptr(), _ptr(probs), _stream(stream)))
+
+    def route_permute(self, layer: int, h, ids, gates, seg_off, route_token, route_slot,
+                      stream=None):
+        self._check(lib().moe_route_permute(self._h, layer, h.data_ptr(), h.shape[0],
+                                            ids.data_ptr(), gates.data_ptr(),
+                                            seg_off.data_ptr(), route_token.data_ptr(),
+                                            route_slot.data_ptr(), _stream(stream)))
+
+    def forward(self, layer: int, h, out, resid=None, ids=None, gates=None, stream=None):
+        self._check(lib().moe_layer_forward(self._h, layer, h.data_ptr(), _ptr(resid),
+                                            out.data_ptr(), h.shape[0], _ptr(ids), _ptr(gates),
+                                            _stream(stream)))
+
+    def stack_forward(self, first_layer: int, n_layers: int, x, eps: float = 1e-5, stream=None):
+        self._check(lib().moe_stack_forward(self._h, first_layer, n_layers, x.data_ptr(),
+                                            x.shape[0], eps, _stream(stream)))
+
+    def forward_host(self, layer: int, h: np.ndarray, resid: np.ndarray | None = None):
+        h = np.ascontiguousarray(h, np.float32)
+        T = h.shape[0]
+        out = np.empty_like(h)
+        ids = np.empty((T, self.cfg.top_k), np.uint32)
+        gates = np.empty((T, self.cfg.top_k), np.float32)
+        r = None if resid is None else np.ascontiguousarray(resid, np.float32)
+        self._check(lib().moe_layer_forward_host(self._h, layer, h.ctypes.data,
+                                                 None if r is None else r.ctypes.data,
+                                                 out.ctypes.data, T, ids.ctypes.data,
+                                                 gates.ctypes.data))
+        return out, ids, gates
+
+    def sync_status(self, stream=None):
+        self._check(lib().moe_sync_status(self._h, _stream(stream)))
+
+    def last_launch_count(self) -> int:
+        return int(lib().moe_last_launch_count(self._h))
+
+    def profile(self, enable: bool):
+        self._check(lib().moe_profile_enable(self._h, int(enable)))
+
+    def profile_read(self) -> dict:
+        """{kernel name: (launches, total ms)} since the previous read."""
+        from ._lib import MoeKernelTime
+        buf = (MoeKernelTime * 64)()
+        n = ctypes.c_int()
+        self._check(lib().moe_profile_read(self._h, buf, 64, ctypes.byref(n)))
+        return {buf[i].name.decode(): (int(buf[i].launches), float(buf[i].total_ms))
+                for i in range(min(n.value, 64))}
+
+
+def synth_normal(seed: int, kind: int, layer: int, n: int, std: float) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    st = lib().moe_synth_normal_host(seed, kind, layer, n, std, out.ctypes.data)
+    if st != MOE_OK:
+        raise MoeError(st, "moe_synth_normal_host failed")
+    return out
+
+
+KIND_ROUTER, KIND_HIDDEN = 3, 4
+
+
+def synth_expert(seed: int, layer: int, expert: int, H: int, I: int, w, s, stream=None):
+    st = lib().moe_synth_expert(seed, layer, expert, H, I, w.data_ptr(), s.data_ptr(),
+                                _stream(stream))
+    if st != MOE_OK:
+        raise MoeError(st, "moe_synth_expert failed")

@@ -1,0 +1,198 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * Drop-in boundary for the MoE-TierEngine reference (Rust crate
+ * `moe-tier-engine`, juanhuy/DoanTotNghiepMOE).  Plain C types only: device
+ * pointers are `const void *` / typed pointers into CUDA device memory, a
+ * stream is an opaque `void *` holding a `cudaStream_t` (NULL = the handle's
+ * own stream).  Every entry point returns a moe_status; nothing throws across
+ * the boundary.  Calls on one handle are serialised by an internal mutex,
+ * like the reference's `Mutex<Scratch>` (src/gpu_expert.rs:241-261).
+ *
+ * Numerics: routing (logits, softmax, top-k ids and gates) and the INT8
+ * SwiGLU expert GEMV path reproduce the reference's CPU arithmetic bit for
+ * bit (src/backend.rs:105-120, :375-389; src/olmoe.rs:2589-2621;
+ * src/int8_expert.rs:380-458, :653-781, :1058-1127).
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum moe_status {
+  MOE_OK = 0,
+  MOE_ERR_INVALID = 1,   /* bad argument / shape / count; nothing was launched */
+  MOE_ERR_NONFINITE = 2, /* non-finite input or output (reference `finite`, src/backend.rs:325-330) */
+  MOE_ERR_CUDA = 3,      /* CUDA runtime error; see moe_last_error() */
+  MOE_ERR_NCCL = 4,      /* collective failure (expert-parallel calls) */
+  MOE_ERR_TIMEOUT = 5,   /* a bounded device-side wait gave up */
+  MOE_ERR_STATE = 6,     /* handle not ready (e.g. layer weights not set) */
+  MOE_ERR_NOMEM = 7      /* device allocation failed */
+} moe_status;
+
+/* ------------------------------------------------------------------------
+ * 1. GpuExpertKernels drop-in (src/gpu_expert.rs:250-495).
+ *    Same argument meaning and error behaviour as the Rust type: shape or
+ *    count mismatch -> MOE_ERR_INVALID before any launch (:384-403); a
+ *    non-finite output -> MOE_ERR_NONFINITE (:492-493).  Inputs and outputs
+ *    are HOST buffers; expert weights are DEVICE pointers borrowed for the
+ *    call (GpuExpertWeights, src/gpu.rs:1552-1566).
+ * ---------------------------------------------------------------------- */
+typedef struct moe_expert_kernels moe_expert_kernels;
+
+/* GpuExpertKernels::init (src/gpu_expert.rs:268). */
+moe_status moe_expert_kernels_init(int device, size_t hidden, size_t intermediate,
+                                   size_t max_experts, moe_expert_kernels **out);
+
+/* GpuExpertKernels::forward_pairs (src/gpu_expert.rs:377): pair j runs
+ * d_weights[j] / d_scales[j] (3*I*H int8 [gate|up|down], 2*I+H f32) on
+ * inputs[n_inputs == 1 ? 0 : j] (H floats) into outputs[j] (H floats).
+ * weight_bytes / scale_bytes give each expert's sizes for validation (may be
+ * NULL to skip, matching `GpuExpertWeights::{weight_bytes, scale_bytes}`). */
+moe_status moe_expert_forward_pairs(moe_expert_kernels *k, const void *const *d_weights,
+                                    const void *const *d_scales, const size_t *weight_bytes,
+                                    const size_t *scale_bytes, size_t n_experts,
+                                    const float *const *inputs, size_t n_inputs,
+                                    float *const *outputs);
+
+/* GpuExpertKernels::forward (src/gpu_expert.rs:366): every expert on one input. */
+moe_status moe_expert_forward(moe_expert_kernels *k, const void *const *d_weights,
+                              const void *const *d_scales, const size_t *weight_bytes,
+                              const size_t *scale_bytes, size_t n_experts, const float *input,
+                              float *const *outputs);
+
+size_t moe_expert_kernels_max_experts(const moe_expert_kernels *k); /* :362 */
+const char *moe_expert_kernels_last_error(const moe_expert_kernels *k);
+void moe_expert_kernels_destroy(moe_expert_kernels *k); /* Drop, :497-510 */
+
+/* ------------------------------------------------------------------------
+ * 2. MoE layer on the device: router projection -> softmax -> top-k ->
+ *    permutation by expert -> INT8 SwiGLU experts -> slot-ordered combine.
+ *    Replaces the host loop of OlmoeModel::step_inner (src/olmoe.rs:2583-3158)
+ *    and OlmoeModel::prefill (src/olmoe.rs:3417-3714) for the MoE block.
+ * ---------------------------------------------------------------------- */
+typedef struct moe_handle moe_handle;
+
+typedef struct moe_dims {
+  int32_t hidden;         /* H  (config hidden_size) */
+  int32_t intermediate;   /* I  (intermediate_size / moe_intermediate_size) */
+  int32_t num_experts;    /* E  (<= 256; the reference caps at 128, src/olmoe.rs:72) */
+  int32_t top_k;          /* K  (num_experts_per_tok, <= 16) */
+  int32_t norm_topk_prob; /* 0/1 (src/olmoe.rs:2614-2621) */
+  int32_t max_tokens;     /* largest T per call (sizes the scratch) */
+  int32_t num_layers;     /* size of the layer table */
+} moe_dims;
+
+enum {
+  MOE_ROUTER_F32 = 0,  /* f32 [E,H], 8-lane dot (src/backend.rs:105-120) */
+  MOE_ROUTER_BF16 = 1, /* bf16 bits [E,H] (src/dense.rs:58-73) */
+};
+
+/* Routing semantics. */
+enum {
+  MOE_ROUTE_SOFTMAX_TOPK = 0, /* OlmoeModel (default): softmax over E, top-k, optional renorm */
+  MOE_ROUTE_TOPK_SOFTMAX = 1  /* Router::select_top_k (src/router.rs:84-103) */
+};
+
+/* Expert GEMM back-end for a layer call. */
+enum {
+  MOE_PATH_AUTO = 0,   /* GEMV for small T, tensor cores for large T */
+  MOE_PATH_GEMV = 1,   /* exact-order INT8 GEMV (bit-identical to the CPU path) */
+  MOE_PATH_TENSOR = 2  /* tcgen05 grouped GEMM (within the 1e-3 tolerance) */
+};
+
+moe_status moe_create(int device, const moe_dims *dims, moe_handle **out);
+void moe_destroy(moe_handle *h);
+const char *moe_last_error(const moe_handle *h);
+/* Default stream for calls that pass stream == NULL. */
+moe_status moe_set_stream(moe_handle *h, void *cuda_stream);
+moe_status moe_set_route_mode(moe_handle *h, int route_mode);
+moe_status moe_set_path(moe_handle *h, int path);
+
+/* Register one layer's weights by borrowing device pointers (the pool owns
+ * them, as with GpuExpertWeights).  d_weights[e] -> 3*I*H int8
+ * [gate I*H | up I*H | down H*I] (src/int8_expert.rs:90-97), d_scales[e] ->
+ * 2*I+H f32 [gate | up | down]; d_router -> [E,H] in router_dtype. */
+moe_status moe_set_layer(moe_handle *h, int layer, const void *const *d_weights,
+                         const void *const *d_scales, const void *d_router, int router_dtype);
+
+/* Same, for experts packed back to back: expert e at d_experts + e*3*I*H and
+ * d_scales + e*(2*I+H). */
+moe_status moe_set_layer_packed(moe_handle *h, int layer, const int8_t *d_experts,
+                                const float *d_scales, const void *d_router, int router_dtype);
+
+/* Routing only: ids/gates [T,K] (device).  probs (optional, device [T,E])
+ * receives the post-softmax probabilities. */
+moe_status moe_route(moe_handle *h, int layer, const float *d_h, int T, uint32_t *d_ids,
+                     float *d_gates, float *d_probs, void *stream);
+
+/* Routing + the by-expert permutation (src/olmoe.rs:3474-3480), device
+ * outputs: seg_off [E+1], route_token / route_slot [T*K]. */
+moe_status moe_route_permute(moe_handle *h, int layer, const float *d_h, int T,
+                             uint32_t *d_ids, float *d_gates, int32_t *d_seg_off,
+                             int32_t *d_route_token, int32_t *d_route_slot, void *stream);
+
+/* One MoE layer: d_out[t] = (d_resid ? d_resid[t] : 0) + sum over slots, in
+ * slot order, of gate * expert(d_h[t]).  All pointers are device memory;
+ * stream-ordered and asynchronous.  d_ids / d_gates (optional) receive the
+ * routing.  Non-finite values are recorded in the handle's device status
+ * word; read it with moe_sync_status(). */
+moe_status moe_layer_forward(moe_handle *h, int layer, const float *d_h, const float *d_resid,
+                             float *d_out, int T, uint32_t *d_ids, float *d_gates, void *stream);
+
+/* Stacked decode: for l in [first, first+n): x <- x + MoE_l(RMSNorm(x; eps, unit gain)),
+ * in place on d_x [T,H] (src/olmoe.rs:2583-2588 then :3147-3157 per layer). */
+moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_layers, float *d_x, int T,
+                             float rms_eps, void *stream);
+
+/* Host-buffer variant of moe_layer_forward (copies in and out inside the
+ * call, synchronous, checks the status word like the reference's `finite`). */
+moe_status moe_layer_forward_host(moe_handle *h, int layer, const float *h_in,
+                                  const float *h_resid, float *h_out, int T, uint32_t *h_ids,
+                                  float *h_gates);
+
+/* Synchronise the handle's stream (or `stream`), read and clear the device
+ * status word: MOE_OK, MOE_ERR_NONFINITE or MOE_ERR_TIMEOUT. */
+moe_status moe_sync_status(moe_handle *h, void *stream);
+
+/* Number of kernel launches issued by the last layer/stack call. */
+int moe_last_launch_count(const moe_handle *h);
+
+/* ------------------------------------------------------------------------
+ * 3. Utilities for tests and benchmarks (no reference counterpart).
+ * ---------------------------------------------------------------------- */
+/* Per-kernel device timing: when enabled, every kernel the handle launches is
+ * bracketed by CUDA events on its stream.  moe_profile_read synchronises,
+ * then reports, per kernel name, the launch count and total milliseconds
+ * since the previous read. */
+typedef struct moe_kernel_time {
+  char name[32];
+  int32_t launches;
+  float total_ms;
+} moe_kernel_time;
+moe_status moe_profile_enable(moe_handle *h, int enable);
+moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int max_entries,
+                            int *n_entries);
+
+/* Seeded N(0, stddev^2) values on the host (Box-Muller in double precision);
+ * kind/layer select an independent stream. */
+moe_status moe_synth_normal_host(uint64_t seed, uint32_t kind, uint32_t layer, size_t n,
+                                 float stddev, float *out);
+
+/* Fill an expert with the seeded synthetic generator (int8 weights
+ * U[-127,127], scales U[1e-4,1e-3]); bit-identical to the CPU generator. */
+moe_status moe_synth_expert(uint64_t seed, int layer, int expert, int hidden, int intermediate,
+                            int8_t *d_weights, float *d_scales, void *stream);
+/* Evaluate the device expf used by the softmax on `count` consecutive float
+ * bit patterns starting at bits_lo (device output). */
+moe_status moe_debug_expf(uint32_t bits_lo, uint32_t count, float *d_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

@@ -737,3 +737,16 @@ void oracle_gen_xorshift64_case(uint64_t seed, int H, int I, int8_t *w, float *s
     }
 #undef NEXT64
 }
+
+/* libm expf over consecutive float bit patterns (the comparator for the
+ * device exponential). */
+void oracle_expf_libm_range(uint32_t bits_lo, size_t count, float *out)
+{
+#pragma omp parallel for schedule(static)
+    for (size_t i = 0; i < count; i++) {
+        uint32_t u = bits_lo + (uint32_t)i;
+        float x;
+        memcpy(&x, &u, 4);
+        out[i] = expf(x);
+    }
+}

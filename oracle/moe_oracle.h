@@ -73,6 +73,7 @@ int oracle_expert_forward(const int8_t *w, const float *s, int H, int I,
 float oracle_expf_table(float x);
 uint64_t oracle_expf_table_mismatches(uint32_t bits_lo, uint32_t bits_hi,
                                       uint32_t stride);
+void oracle_expf_libm_range(uint32_t bits_lo, size_t count, float *out);
 
 /* ---- one MoE layer over T tokens ----
  * router: [E,H] f32 (bf16=0) or bf16 bits (bf16=1)

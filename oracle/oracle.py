@@ -52,6 +52,7 @@ def lib():
             "oracle_expert_forward": (i32, [P, P, i32, i32, P, P, P, i32]),
             "oracle_expf_table": (f32, [f32]),
             "oracle_expf_table_mismatches": (u64, [u32, u32, u32]),
+            "oracle_expf_libm_range": (None, [u32, sz, P]),
             "oracle_layer_forward": (i32, [P, i32, P, P, P, P, P, P, P, P, P, i32, i32]),
             "oracle_stack_forward": (i32, [P, i32, i32, P, f32, P, P, i32, i32]),
             "oracle_synth_key": (u64, [u64, u32, u32, u32]),
@@ -124,6 +125,12 @@ def dot_i8(q, x, scalar: bool = False) -> np.float32:
     q = np.ascontiguousarray(q, np.int8); x = np.ascontiguousarray(x, np.float32)
     fn = lib().oracle_dot_i8_scalar if scalar else lib().oracle_dot_i8_avx2
     return np.float32(fn(_p(q), _p(x), q.size))
+
+
+def expf_libm_range(bits_lo: int, count: int) -> np.ndarray:
+    out = np.empty(count, np.float32)
+    lib().oracle_expf_libm_range(bits_lo, count, _p(out))
+    return out
 
 
 def softmax(v) -> np.ndarray:
