@@ -72,6 +72,8 @@ SIGNATURES = {
     "moe_profile_enable": (I32, [P, I32]),
     "moe_profile_read": (I32, [P, P, I32, ctypes.POINTER(ctypes.c_int)]),
     "moe_synth_normal_host": (I32, [U64, U32, U32, SZ, F32, P]),
+    "moe_layer_forward_noalloc": (I32, [ctypes.POINTER(MoeDims), P, P, P, I32, P, P, P, I32,
+                                        P, ctypes.c_char_p, SZ]),
 }
 
 _lib = None

@@ -163,6 +163,28 @@ moe_status moe_sync_status(moe_handle *h, void *stream);
 /* Number of kernel launches issued by the last layer/stack call. */
 int moe_last_launch_count(const moe_handle *h);
 
+/* One MoE layer that allocates no device memory.  No counterpart in the
+ * reference: it is for callers that cannot allocate on the GPU -- a host
+ * whose own allocator or VRAM budget owns every byte (an allocation made
+ * behind its back can push its expert pool out of memory), or a
+ * latency-critical decode thread on which cudaMalloc/cudaFree would block
+ * or synchronise the device.  It needs no moe_handle: weights are the packed
+ * device layout of moe_set_layer_packed(), d_h / d_resid / d_out are device
+ * [T,H] as in moe_layer_forward(), and the results equal that call's.
+ * Intermediates live in a fixed 8 MiB device array inside this library that
+ * every GPU loading the library holds until the process exits; a call whose
+ * T needs more returns MOE_ERR_INVALID with the reason in err_msg (optional
+ * buffer).  The first call on each device looks the array up with that
+ * device current, so make it before any stream capture.  Calls share the
+ * array: calls that overlap on the GPU race on it.  The call synchronises
+ * `stream` (NULL = legacy default stream) and returns MOE_ERR_NONFINITE like
+ * moe_layer_forward_host() when an input or output is not finite. */
+moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8_t *d_experts,
+                                     const float *d_scales, const void *d_router,
+                                     int router_dtype, const float *d_h, const float *d_resid,
+                                     float *d_out, int T, void *stream, char *err_msg,
+                                     size_t err_len);
+
 /* ------------------------------------------------------------------------
  * 3. Utilities for tests and benchmarks (no reference counterpart).
  * ---------------------------------------------------------------------- */
