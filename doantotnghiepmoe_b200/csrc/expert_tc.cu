@@ -1,0 +1,530 @@
+// Grouped INT8 expert GEMM on the 5th-generation tensor cores (tcgen05) for
+// prefill-sized batches.
+//
+// Math.  The reference computes g = (W_g . x) * s_g, u = (W_u . x) * s_u,
+// act = silu(g) * u, y = (W_d . act) * s_d with INT8 weights and FP32
+// activations (src/int8_expert.rs:969-1055).  Here the INT8 weights go to
+// the tensor cores untouched and each activation row r is written as two
+// signed int8 digits with a per-row scale:
+//     x_r ~= s_r * (d1 + d2 / 254),   s_r = max|x_r| / 127,
+// so the per-element error is <= max|x_r| / 64516.  Both digit planes are
+// multiplied with `tcgen05.mma ... kind::i8` into separate int32 TMEM
+// accumulators (exact integer sums), and the epilogue forms
+//     dot = s_r * D1 + (s_r / 254) * D2
+// in fp32.  Against the CPU path the layer output stays within the 1e-3
+// relative tolerance with a wide margin (the parity tests assert it).
+//
+// Kernel shape (both GEMMs): one CTA per (128-row weight tile, token tile of
+// up to 128 routes of one expert), 192 threads:
+//   warp 0  : TMA producer (3D tiled loads, 128B swizzle, mbarrier tx count)
+//   warp 1  : TMEM allocator + single-thread MMA issuer (tcgen05.commit
+//             releases a pipeline stage / signals the epilogue)
+//   warps 2-5: epilogue, tcgen05.ld of the accumulators (warp w reads TMEM
+//             lanes 32*(w%4) .. +31).
+// Every mbarrier wait is bounded: on expiry the kernel records
+// kStatusTimeout, stops issuing work, waits (bounded) for its in-flight
+// copies, frees its TMEM and returns.
+//
+// No TMA multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "expert_tc.h"
+
+namespace moe {
+namespace tc {
+namespace {
+
+constexpr int BM = 128;          // weight rows per tile (UMMA M)
+constexpr int BN = kTcBlockN;    // routes per tile (UMMA N)
+constexpr int BK = 128;          // int8 K elements per stage (= 128 B swizzle row)
+constexpr int UK = 32;           // K per tcgen05.mma kind::i8
+constexpr int kThreads = 192;
+constexpr int kStages1 = 3;      // gate/up: 4 tiles of 16 KB per stage
+constexpr int kStages2 = 4;      // down: 3 tiles of 16 KB per stage
+constexpr uint32_t kTileBytes = BM * BK;  // 16 KB (A and B tiles are both 128 x 128 B)
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t su32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(su32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false on timeout, or (when abort_flag is given) as soon as
+// another role has aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          volatile int *abort_flag) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (abort_flag && *abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(su32(dst)),
+      "l"(map), "r"(su32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   su32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          su32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t v[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand with 128-byte swizzle:
+// 8-row x 128-byte atoms, atoms 1024 B apart (SBO), version 1, layout 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: s32 accumulate, s8 x s8, both K-major, M=128, N=BN.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+struct Pipe {
+  uint64_t full[4];
+  uint64_t empty[4];
+  uint64_t done;
+  uint32_t tmem_base;
+  int abort_flag;
+  int consumed;
+};
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+  return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// ---------------------------------------------------------------------------
+// Mainloop shared by both GEMMs: NA weight tiles x NB digit tiles per stage,
+// accumulator (a, b) at TMEM column (a * NB + b) * BN.
+// ---------------------------------------------------------------------------
+template <int NA, int NB, int S>
+__device__ __forceinline__ void mainloop(Pipe &pp, uint8_t *tiles, const CUtensorMap *mapA,
+                                         const CUtensorMap *mapB, const int a_row[NA], int a_e,
+                                         int b_row, int nk, uint32_t tmem) {
+  constexpr uint32_t kStageBytes = (NA + NB) * kTileBytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0 && lane == 0) {
+    int issued = 0;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % S;
+      const int use = kb / S;
+      if (use > 0 && !mbar_wait(&pp.empty[s], (use - 1) & 1, &pp.abort_flag)) {
+        pp.abort_flag = 1;
+        break;
+      }
+      uint8_t *st = tiles + s * kStageBytes;
+      mbar_expect_tx(&pp.full[s], kStageBytes);
+#pragma unroll
+      for (int a = 0; a < NA; ++a)
+        tma_load_3d(st + a * kTileBytes, mapA, &pp.full[s], kb * BK, a_row[a], a_e);
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        tma_load_3d(st + (NA + b) * kTileBytes, mapB, &pp.full[s], kb * BK, b_row, b);
+      ++issued;
+    }
+    // On abort, the stages issued but not yet consumed must land before the
+    // CTA may exit (their bytes target this CTA's shared memory).
+    if (pp.abort_flag) {
+      const int from = *(volatile int *)&pp.consumed;
+      for (int kb = from; kb < issued; ++kb) mbar_wait(&pp.full[kb % S], (kb / S) & 1, nullptr);
+    }
+  } else if (warp == 1 && lane == 0) {
+    int kb = 0;
+    for (; kb < nk; ++kb) {
+      const int s = kb % S;
+      if (!mbar_wait(&pp.full[s], (kb / S) & 1, &pp.abort_flag)) {
+        pp.abort_flag = 1;
+        break;
+      }
+      fence_after_sync();
+      const uint32_t base = su32(tiles + s * kStageBytes);
+#pragma unroll
+      for (int k = 0; k < BK / UK; ++k) {
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+          const uint64_t ad = sw128_desc(base + a * kTileBytes + k * UK);
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const uint64_t bd = sw128_desc(base + (NA + b) * kTileBytes + k * UK);
+            mma_i8(tmem + (uint32_t)((a * NB + b) * BN), ad, bd, kIdesc,
+                   (kb > 0 || k > 0) ? 1u : 0u);
+          }
+        }
+      }
+      mma_commit(&pp.empty[s]);
+      pp.consumed = kb + 1;
+    }
+    // Signals the epilogue once every issued MMA has completed.
+    mma_commit(&pp.done);
+  }
+}
+
+__device__ __forceinline__ void setup(Pipe &pp, int stages, uint32_t ncols) {
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&pp.full[s], 1);
+      mbar_init(&pp.empty[s], 1);
+    }
+    mbar_init(&pp.done, 1);
+    pp.abort_flag = 0;
+    pp.consumed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(&pp.tmem_base, ncols);
+  __syncthreads();
+  fence_after_sync();
+}
+
+__device__ __forceinline__ void teardown(Pipe &pp, uint32_t ncols, uint32_t *status) {
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && pp.abort_flag) set_status(status, kStatusTimeout);
+  if ((threadIdx.x >> 5) == 1) tmem_dealloc(pp.tmem_base, ncols);
+}
+
+// Dynamic smem: [Pipe | pad | tiles (1024-aligned)].
+constexpr size_t smem_bytes(int na, int nb, int stages) {
+  return 1024 + sizeof(Pipe) + 1024 + (size_t)stages * (na + nb) * kTileBytes;
+}
+
+// ---------------------------------------------------------------------------
+// GEMM 1: gate/up.  A = gate rows [m0, m0+128) and up rows [I+m0, ...) of
+// expert e; B = the two digit planes of the tile's routes.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1)
+    gate_up_tc_kernel(const __grid_constant__ CUtensorMap mapW,
+                      const __grid_constant__ CUtensorMap mapX, TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const int g = blockIdx.y;
+  if (g >= *a.n_tiles) return;
+  Pipe &pp = *reinterpret_cast<Pipe *>(smem_raw);
+  uint8_t *tiles = align1024(smem_raw + sizeof(Pipe));
+  const int e = a.tile_expert[g], r0 = a.tile_row0[g], nr = a.tile_rows[g];
+  const int m0 = blockIdx.x * BM;
+  const int nk = (a.H + BK - 1) / BK;
+  constexpr uint32_t kCols = 4 * BN;
+  setup(pp, kStages1, kCols);
+  const int arow[2] = {m0, a.I + m0};
+  mainloop<2, 2, kStages1>(pp, tiles, &mapW, &mapX, arow, e, r0, nk, pp.tmem_base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp >= 2) {
+    const int q = warp & 3;
+    const int i = m0 + 32 * q + lane;  // weight row of this thread
+    bool ok = mbar_wait(&pp.done, 0, &pp.abort_flag);
+    if (!ok) pp.abort_flag = 1;
+    ok = ok && !*(volatile int *)&pp.abort_flag;  // an aborted mainloop leaves partial sums
+    if (ok) {
+      fence_after_sync();
+      const float *S = a.s_ptr[e];
+      const float sg = i < a.I ? S[i] : 0.0f, su = i < a.I ? S[a.I + i] : 0.0f;
+      const uint32_t trow = pp.tmem_base + ((uint32_t)(32 * q) << 16);
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (c0 >= nr) break;  // warp-uniform
+        int32_t v[4][16];
+#pragma unroll
+        for (int acc = 0; acc < 4; ++acc) tmem_ld16(trow + acc * BN + c0, v[acc]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int c = c0 + j;
+          float act = 0.0f;
+          if (c < nr) {
+            const int r = r0 + c;
+            const float s1 = a.xs1[r], s2 = a.xs2[r];
+            const float gd = fmaf(s1, (float)v[0][j], s2 * (float)v[1][j]);
+            const float ud = fmaf(s1, (float)v[2][j], s2 * (float)v[3][j]);
+            const float gg = gd * sg, uu = ud * su;
+            act = gg / (1.0f + expf_ref(-gg)) * uu;
+            if (i < a.I) a.act[(size_t)r * a.I + i] = act;
+          }
+          // max |act| over this warp's 32 rows for route column c
+          float m = fabsf(act);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0 && c < nr) atomicMax(&a.act_amax[r0 + c], __float_as_uint(m));
+        }
+      }
+    }
+  }
+  teardown(pp, kCols, a.status);
+}
+
+// ---------------------------------------------------------------------------
+// GEMM 2: down.  A = down rows [m0, m0+128) of expert e (K = I); B = the
+// digit planes of the tile's activations.  Epilogue writes gate * y into the
+// (token, slot) contribution row.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1)
+    down_tc_kernel(const __grid_constant__ CUtensorMap mapW,
+                   const __grid_constant__ CUtensorMap mapA, TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const int g = blockIdx.y;
+  if (g >= *a.n_tiles) return;
+  Pipe &pp = *reinterpret_cast<Pipe *>(smem_raw);
+  uint8_t *tiles = align1024(smem_raw + sizeof(Pipe));
+  const int e = a.tile_expert[g], r0 = a.tile_row0[g], nr = a.tile_rows[g];
+  const int m0 = blockIdx.x * BM;
+  const int nk = (a.I + BK - 1) / BK;
+  constexpr uint32_t kCols = 2 * BN;
+  setup(pp, kStages2, kCols);
+  const int arow[1] = {m0};
+  mainloop<1, 2, kStages2>(pp, tiles, &mapW, &mapA, arow, e, r0, nk, pp.tmem_base);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp >= 2) {
+    const int q = warp & 3;
+    const int j = m0 + 32 * q + lane;  // output row (hidden index)
+    bool ok = mbar_wait(&pp.done, 0, &pp.abort_flag);
+    if (!ok) pp.abort_flag = 1;
+    ok = ok && !*(volatile int *)&pp.abort_flag;  // an aborted mainloop leaves partial sums
+    if (ok) {
+      fence_after_sync();
+      const float sd = j < a.H ? a.s_ptr[e][2 * a.I + j] : 0.0f;
+      const uint32_t trow = pp.tmem_base + ((uint32_t)(32 * q) << 16);
+      bool bad = false;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (c0 >= nr) break;
+        int32_t v[2][16];
+        tmem_ld16(trow + c0, v[0]);
+        tmem_ld16(trow + BN + c0, v[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int c = c0 + jj;
+          if (c < nr && j < a.H) {
+            const int r = r0 + c;
+            const float y = fmaf(a.as1[r], (float)v[0][jj], a.as2[r] * (float)v[1][jj]) * sd;
+            bad |= !is_finite_f(y);
+            const int tok = a.r_token[r], slot = a.r_slot[r];
+            a.contrib[((size_t)tok * a.K + slot) * a.H + j] = __fmul_rn(a.r_gate[r], y);
+          }
+        }
+      }
+      if (bad) set_status(a.status, kStatusNonFinite);
+    }
+  }
+  teardown(pp, kCols, a.status);
+}
+
+// ---------------------------------------------------------------------------
+// Tile table and activation digit planes
+// ---------------------------------------------------------------------------
+__global__ void build_tiles_kernel(const int32_t *seg_off, const int32_t *active,
+                                   const int32_t *n_active, int32_t *tile_expert,
+                                   int32_t *tile_row0, int32_t *tile_rows, int32_t *n_tiles,
+                                   int max_tiles) {
+  if (threadIdx.x != 0) return;
+  int n = 0;
+  const int na = *n_active;
+  for (int j = 0; j < na; ++j) {
+    const int e = active[j];
+    for (int r = seg_off[e]; r < seg_off[e + 1] && n < max_tiles; r += BN) {
+      tile_expert[n] = e;
+      tile_row0[n] = r;
+      tile_rows[n] = min(BN, seg_off[e + 1] - r);
+      ++n;
+    }
+  }
+  *n_tiles = n;
+}
+
+// One warp per route row: s = max|v| / 127, d1 = rint(v/s), d2 = rint((v/s - d1) * 254).
+// src rows are gathered through `rows` (null = identity).  Also resets the
+// per-row amax used by the next stage when `amax_reset` is given.
+__global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_t *__restrict__ rows,
+                                     const uint32_t *__restrict__ amax_in, int R, int n,
+                                     int8_t *__restrict__ q, size_t plane, float *__restrict__ s1,
+                                     float *__restrict__ s2, uint32_t *__restrict__ amax_reset) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= R) return;
+  const int row = rows ? rows[warp] : warp;
+  const float *x = src + (size_t)row * n;
+  float amax;
+  if (amax_in) {
+    amax = __uint_as_float(amax_in[warp]);
+  } else {
+    amax = 0.0f;
+    for (int c = lane * 4; c < n; c += 128) {
+      const float4 v = *reinterpret_cast<const float4 *>(x + c);
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  }
+  const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+  const float inv = 1.0f / s;
+  int8_t *q1 = q + (size_t)warp * n;
+  int8_t *q2 = q + plane + (size_t)warp * n;
+  for (int c = lane * 4; c < n; c += 128) {
+    const float4 v = *reinterpret_cast<const float4 *>(x + c);
+    const float in[4] = {v.x, v.y, v.z, v.w};
+    uint32_t p1 = 0, p2 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float t = in[k] * inv;
+      const float a1 = fminf(fmaxf(rintf(t), -127.0f), 127.0f);
+      const float a2 = fminf(fmaxf(rintf((t - a1) * 254.0f), -127.0f), 127.0f);
+      p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
+      p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
+    }
+    *reinterpret_cast<uint32_t *>(q1 + c) = p1;
+    *reinterpret_cast<uint32_t *>(q2 + c) = p2;
+  }
+  if (lane == 0) {
+    s1[warp] = s;
+    s2[warp] = s / 254.0f;
+    if (amax_reset) amax_reset[warp] = 0u;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+bool encode_map3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
+                  uint64_t stride1, uint64_t stride2) {
+  auto enc = encoder();
+  if (!enc) return false;
+  if (((uintptr_t)base & 15) || (stride1 & 15) || (stride2 & 15)) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1, stride2};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)BM, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+cudaError_t launch_build_tiles(const int32_t *seg_off, const int32_t *active,
+                               const int32_t *n_active, int32_t *tile_expert, int32_t *tile_row0,
+                               int32_t *tile_rows, int32_t *n_tiles, int max_tiles,
+                               cudaStream_t s) {
+  build_tiles_kernel<<<1, 32, 0, s>>>(seg_off, active, n_active, tile_expert, tile_row0,
+                                      tile_rows, n_tiles, max_tiles);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const float *src, const int32_t *rows, const uint32_t *amax_in,
+                                 int R, int n, int8_t *q, size_t plane, float *s1, float *s2,
+                                 uint32_t *amax_reset, cudaStream_t s) {
+  if (R <= 0) return cudaSuccess;
+  quantize_rows_kernel<<<(R + 7) / 8, 256, 0, s>>>(src, rows, amax_in, R, n, q, plane, s1, s2,
+                                                   amax_reset);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
+                              int max_tiles, cudaStream_t s) {
+  const size_t smem = smem_bytes(2, 2, kStages1);
+  cudaFuncSetAttribute(gate_up_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  dim3 grid((a.I + BM - 1) / BM, max_tiles);
+  gate_up_tc_kernel<<<grid, kThreads, smem, s>>>(mapW, mapX, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_down_tc(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
+                           int max_tiles, cudaStream_t s) {
+  const size_t smem = smem_bytes(1, 2, kStages2);
+  cudaFuncSetAttribute(down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid((a.H + BM - 1) / BM, max_tiles);
+  down_tc_kernel<<<grid, kThreads, smem, s>>>(mapW, mapA, a);
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+}  // namespace moe

@@ -14,9 +14,15 @@
 
 #include "../../include/moe_b200.h"
 #include "common.cuh"
+#include "expert_tc.h"
 #include "kernels.h"
 
 using namespace moe;
+
+namespace {
+// Prefill-sized calls (T >= this) take the tensor-core path under MOE_PATH_AUTO.
+constexpr int kTcMinTokens = 128;
+}  // namespace
 
 namespace {
 
@@ -289,6 +295,9 @@ struct LayerSlot {
   const void *router = nullptr;
   int router_dtype = MOE_ROUTER_F32;
   int vec = 0;  // all expert bases 8-byte aligned -> vector weight loads
+  // tensor-core path: only for the packed layout (one 3D tensor map per GEMM)
+  bool tc_ok = false;
+  CUtensorMap map_gu{}, map_dn{};
 };
 }  // namespace
 
@@ -312,6 +321,14 @@ struct moe_handle {
   float *h_pin_in = nullptr, *h_pin_out = nullptr;
   int last_launches = 0;
   Profiler prof;
+  // tensor-core path scratch
+  bool tc_ok = false;
+  int max_tiles = 0;
+  int8_t *xq = nullptr, *aq = nullptr;  // [2][R][H], [2][R][I] digit planes
+  float *xs1 = nullptr, *xs2 = nullptr, *as1 = nullptr, *as2 = nullptr;
+  uint32_t *act_amax = nullptr;
+  int32_t *tile_expert = nullptr, *tile_row0 = nullptr, *tile_rows = nullptr, *n_tiles = nullptr;
+  CUtensorMap map_x{}, map_a{};
 };
 
 namespace {
@@ -321,9 +338,11 @@ void free_handle(moe_handle *h) {
     cudaFree(l.d_wptr);
     cudaFree(l.d_sptr);
   }
-  void *ptrs[] = {h->logits, h->gates, h->r_gate, h->act,    h->contrib, h->hbuf,
-                  h->io_in,  h->io_out, h->io_resid, h->ids, h->status,  h->seg_off,
-                  h->active, h->n_active, h->r_token, h->r_slot, h->r_pos};
+  void *ptrs[] = {h->logits,  h->gates,     h->r_gate,    h->act,       h->contrib, h->hbuf,
+                  h->io_in,   h->io_out,    h->io_resid,  h->ids,       h->status,  h->seg_off,
+                  h->active,  h->n_active,  h->r_token,   h->r_slot,    h->r_pos,   h->xq,
+                  h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
+                  h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles};
   for (void *p : ptrs) cudaFree(p);
   cudaFreeHost(h->h_pin_in);
   cudaFreeHost(h->h_pin_out);
@@ -403,14 +422,90 @@ moe_status check_layer(moe_handle *h, int layer, int T) {
   return MOE_OK;
 }
 
+bool use_tensor_path(const moe_handle *h, const LayerSlot &L, int T, const float *d_h) {
+  const bool avail = h->tc_ok && L.tc_ok && ((uintptr_t)d_h & 15) == 0;
+  if (h->path == MOE_PATH_TENSOR) return avail;
+  if (h->path == MOE_PATH_GEMV) return false;
+  return avail && T >= kTcMinTokens;
+}
+
+// Experts on the tensor cores: digit planes of the routed inputs, gate/up
+// GEMM with SwiGLU epilogue, digit planes of the activations, down GEMM with
+// the gate-weighted contribution epilogue, slot-ordered combine.
+moe_status tensor_experts(moe_handle *h, const LayerSlot &L, const float *d_h,
+                          const float *d_resid, float *d_out, int T, cudaStream_t s) {
+  const int H = h->d.hidden, I = h->d.intermediate, K = h->d.top_k;
+  const int R = T * K;
+  const size_t Rcap = (size_t)h->d.max_tokens * K;
+  cudaError_t e;
+  cudaEvent_t p0 = h->prof.begin(s);
+  e = tc::launch_build_tiles(h->seg_off, h->active, h->n_active, h->tile_expert, h->tile_row0,
+                             h->tile_rows, h->n_tiles, h->max_tiles, s);
+  if (e == cudaSuccess)
+    e = tc::launch_quantize_rows(d_h, h->r_token, nullptr, R, H, h->xq, Rcap * H, h->xs1, h->xs2,
+                                 h->act_amax, s);
+  h->prof.end("tc_prep", p0, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "tensor prep launch");
+  tc::TcArgs a{};
+  a.H = H;
+  a.I = I;
+  a.K = K;
+  a.tile_expert = h->tile_expert;
+  a.tile_row0 = h->tile_row0;
+  a.tile_rows = h->tile_rows;
+  a.n_tiles = h->n_tiles;
+  a.s_ptr = L.d_sptr;
+  a.xs1 = h->xs1;
+  a.xs2 = h->xs2;
+  a.act = h->act;
+  a.act_amax = h->act_amax;
+  a.as1 = h->as1;
+  a.as2 = h->as2;
+  a.r_token = h->r_token;
+  a.r_slot = h->r_slot;
+  a.r_gate = h->r_gate;
+  a.contrib = h->contrib;
+  a.status = h->status;
+  const int tiles = std::min(h->max_tiles, (R + tc::kTcBlockN - 1) / tc::kTcBlockN +
+                                               std::min(h->d.num_experts, R));
+  p0 = h->prof.begin(s);
+  e = tc::launch_gate_up_tc(L.map_gu, h->map_x, a, tiles, s);
+  h->prof.end("gate_up_tc", p0, s);
+  if (e == cudaSuccess) {
+    p0 = h->prof.begin(s);
+    e = tc::launch_quantize_rows(h->act, nullptr, h->act_amax, R, I, h->aq, Rcap * I, h->as1,
+                                 h->as2, nullptr, s);
+    h->prof.end("tc_act_digits", p0, s);
+  }
+  if (e == cudaSuccess) {
+    p0 = h->prof.begin(s);
+    e = tc::launch_down_tc(L.map_dn, h->map_a, a, tiles, s);
+    h->prof.end("down_tc", p0, s);
+  }
+  if (e == cudaSuccess) {
+    p0 = h->prof.begin(s);
+    e = launch_combine(h->contrib, d_resid, d_out, T, K, H, h->status, s);
+    h->prof.end("combine", p0, s);
+  }
+  if (e != cudaSuccess) return cuda_fail(h, e, "tensor expert launch");
+  h->last_launches += 6;
+  return MOE_OK;
+}
+
 moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, const float *d_resid,
                                 float *d_out, int T, uint32_t *d_ids, float *d_gates,
                                 cudaStream_t s) {
   const LayerSlot &L = h->layers[layer];
   uint32_t *ids = d_ids ? d_ids : h->ids;
   float *gates = d_gates ? d_gates : h->gates;
+  if (h->path == MOE_PATH_TENSOR && !use_tensor_path(h, L, T, d_h)) {
+    set_err(h->err, "tensor-core path unavailable for layer %d (needs the packed expert layout, "
+            "H and I multiples of 16, 16-byte aligned inputs)", layer);
+    return MOE_ERR_STATE;
+  }
   moe_status st = run_route(h, L, d_h, T, ids, gates, nullptr, s, true);
   if (st != MOE_OK) return st;
+  if (use_tensor_path(h, L, T, d_h)) return tensor_experts(h, L, d_h, d_resid, d_out, T, s);
   GemvArgs a{};
   a.H = h->d.hidden;
   a.I = h->d.intermediate;
@@ -488,11 +583,26 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && cudaMallocHost(&h->h_pin_in, 2 * T * H * sizeof(float)) == cudaSuccess;
   ok = ok && cudaMallocHost(&h->h_pin_out, T * H * sizeof(float)) == cudaSuccess;
   ok = ok && cudaMemset(h->status, 0, 4) == cudaSuccess;
+  // tensor-core path scratch and the activation-side tensor maps
+  const size_t R = T * K;
+  h->max_tiles = (int)((R + tc::kTcBlockN - 1) / tc::kTcBlockN + std::min(E, R));
+  ok = ok && dalloc(&h->xq, 2 * R * H) == cudaSuccess;
+  ok = ok && dalloc(&h->aq, 2 * R * I) == cudaSuccess;
+  ok = ok && dalloc(&h->xs1, R) == cudaSuccess && dalloc(&h->xs2, R) == cudaSuccess;
+  ok = ok && dalloc(&h->as1, R) == cudaSuccess && dalloc(&h->as2, R) == cudaSuccess;
+  ok = ok && dalloc(&h->act_amax, R) == cudaSuccess;
+  ok = ok && dalloc(&h->tile_expert, h->max_tiles) == cudaSuccess;
+  ok = ok && dalloc(&h->tile_row0, h->max_tiles) == cudaSuccess;
+  ok = ok && dalloc(&h->tile_rows, h->max_tiles) == cudaSuccess;
+  ok = ok && dalloc(&h->n_tiles, 1) == cudaSuccess;
   if (!ok) {
     free_handle(h);
     delete h;
     return MOE_ERR_NOMEM;
   }
+  h->tc_ok = H % 16 == 0 && I % 16 == 0 &&
+             tc::encode_map3d(&h->map_x, h->xq, H, R, 2, H, R * H) &&
+             tc::encode_map3d(&h->map_a, h->aq, I, R, 2, I, R * I);
   *out = h;
   return MOE_OK;
 }
@@ -562,6 +672,17 @@ extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const 
   L.router = d_router;
   L.router_dtype = router_dtype;
   L.vec = vec;
+  // Packed layout (expert e at base + e * 3IH, scales at sbase + e * (2I+H))
+  // enables the tensor-core path.
+  const size_t H = h->d.hidden, I = h->d.intermediate;
+  bool packed = true;
+  for (int e = 1; e < E && packed; ++e)
+    packed = (const char *)d_weights[e] == (const char *)d_weights[0] + e * 3 * I * H &&
+             (const float *)d_scales[e] == (const float *)d_scales[0] + e * (2 * I + H);
+  const char *wb = (const char *)d_weights[0];
+  L.tc_ok = packed && h->tc_ok &&
+            tc::encode_map3d(&L.map_gu, wb, H, 2 * I, E, H, 3 * I * H) &&
+            tc::encode_map3d(&L.map_dn, wb + 2 * I * H, I, H, E, I, 3 * I * H);
   L.set = true;
   return MOE_OK;
 }
