@@ -25,23 +25,32 @@
 namespace moe {
 namespace {
 
-constexpr int kThreads = 256;       // 8 warps
+constexpr int kThreads = 128;       // 4 warps: small items, many CTAs per SM
+constexpr int kPF = 16;             // weight chunk-steps loaded ahead per thread (128 B)
 constexpr int kTG = 4;              // tokens per pass
 constexpr int kGURowsPerWarp = 4;   // gate/up: 8 lanes per row (4 gate + 4 up banks)
 constexpr int kGURows = kGURowsPerWarp * (kThreads / 32);
 constexpr int kDNRowsPerWarp = 8;   // down: 4 lanes per row
 constexpr int kDNRows = kDNRowsPerWarp * (kThreads / 32);
 
+// Streaming 8-byte weight load: read once, never reused by this CTA.
+__device__ __forceinline__ uint2 ldg_stream8(const int8_t *p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p));
+  return v;
+}
+
 template <bool kVec>
-__device__ __forceinline__ void load_w8(const int8_t *p, float w[8]) {
-  if (kVec) {
-    const uint2 v = *reinterpret_cast<const uint2 *>(p);
-    i8x4_to_f32(v.x, w[0], w[1], w[2], w[3]);
-    i8x4_to_f32(v.y, w[4], w[5], w[6], w[7]);
-  } else {
-#pragma unroll
-    for (int l = 0; l < 8; ++l) w[l] = (float)p[l];
-  }
+__device__ __forceinline__ uint2 load_w8_raw(const int8_t *p) {
+  if (kVec) return ldg_stream8(p);
+  uint2 v;
+  v.x = (uint32_t)(uint8_t)p[0] | ((uint32_t)(uint8_t)p[1] << 8) |
+        ((uint32_t)(uint8_t)p[2] << 16) | ((uint32_t)(uint8_t)p[3] << 24);
+  v.y = (uint32_t)(uint8_t)p[4] | ((uint32_t)(uint8_t)p[5] << 8) |
+        ((uint32_t)(uint8_t)p[6] << 16) | ((uint32_t)(uint8_t)p[7] << 24);
+  return v;
 }
 
 template <bool kVec>
@@ -58,7 +67,9 @@ __device__ __forceinline__ void load_x8(const float *p, float x[8]) {
 }
 
 // Bank `bank` of a row dot for ng (<= kTG) tokens whose inputs sit in smem
-// rows xs + t*ld.
+// rows xs + t*ld.  Weights are fetched kPF chunk-steps ahead into registers so
+// that enough bytes are in flight to cover HBM latency; the FMA chains still
+// run strictly in chunk order.
 template <bool kVec>
 __device__ __forceinline__ void bank_chain(const int8_t *__restrict__ wrow,
                                            const float *__restrict__ xs, int ld, int n, int bank,
@@ -68,18 +79,27 @@ __device__ __forceinline__ void bank_chain(const int8_t *__restrict__ wrow,
 #pragma unroll
     for (int l = 0; l < 8; ++l) acc[t][l] = 0.0f;
   const int nc = n / 32;
-#pragma unroll 2
-  for (int c = 0; c < nc; ++c) {
-    const int off = 32 * c + 8 * bank;
-    float w[8];
-    load_w8<kVec>(wrow + off, w);
+  for (int c0 = 0; c0 < nc; c0 += kPF) {
+    uint2 raw[kPF];
 #pragma unroll
-    for (int t = 0; t < kTG; ++t) {
-      if (t < ng) {
-        float x[8];
-        load_x8<kVec>(xs + t * ld + off, x);
+    for (int i = 0; i < kPF; ++i)
+      if (c0 + i < nc) raw[i] = load_w8_raw<kVec>(wrow + 32 * (c0 + i) + 8 * bank);
 #pragma unroll
-        for (int l = 0; l < 8; ++l) acc[t][l] = __fmaf_rn(w[l], x[l], acc[t][l]);
+    for (int i = 0; i < kPF; ++i) {
+      if (c0 + i < nc) {
+        const int off = 32 * (c0 + i) + 8 * bank;
+        float w[8];
+        i8x4_to_f32(raw[i].x, w[0], w[1], w[2], w[3]);
+        i8x4_to_f32(raw[i].y, w[4], w[5], w[6], w[7]);
+#pragma unroll
+        for (int t = 0; t < kTG; ++t) {
+          if (t < ng) {
+            float x[8];
+            load_x8<kVec>(xs + t * ld + off, x);
+#pragma unroll
+            for (int l = 0; l < 8; ++l) acc[t][l] = __fmaf_rn(w[l], x[l], acc[t][l]);
+          }
+        }
       }
     }
   }
@@ -116,18 +136,32 @@ __device__ __forceinline__ int seg_count(const GemvArgs &a) {
   return a.n_active_dev ? *a.n_active_dev : a.n_active_max;
 }
 
-// Stage ng input rows (gathered through r_token) into smem.
+// Stage ng input rows (gathered through r_token) into smem.  Loads are
+// issued in batches of kSB per thread before any store, so a row costs about
+// one memory round trip instead of one per loop trip.
+constexpr int kSB = 8;
 template <bool kVec>
 __device__ __forceinline__ void stage_rows(float *__restrict__ xs, const float *__restrict__ src,
                                            const int32_t *__restrict__ r_token, int g0, int ng,
                                            int n) {
   if (kVec) {
-    const int n4 = n / 4;
-    for (int i = threadIdx.x; i < ng * n4; i += blockDim.x) {
-      const int t = i / n4, c = i % n4;
-      const int row = r_token ? r_token[g0 + t] : g0 + t;
-      reinterpret_cast<float4 *>(xs + t * n)[c] =
-          reinterpret_cast<const float4 *>(src + (size_t)row * n)[c];
+    const int n4 = n / 4, total = ng * n4;
+    for (int base = 0; base < total; base += kThreads * kSB) {
+      float4 v[kSB];
+#pragma unroll
+      for (int k = 0; k < kSB; ++k) {
+        const int i = base + k * kThreads + threadIdx.x;
+        if (i < total) {
+          const int t = i / n4, c = i % n4;
+          const int row = r_token ? r_token[g0 + t] : g0 + t;
+          v[k] = reinterpret_cast<const float4 *>(src + (size_t)row * n)[c];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kSB; ++k) {
+        const int i = base + k * kThreads + threadIdx.x;
+        if (i < total) reinterpret_cast<float4 *>(xs)[(i / n4) * n4 + i % n4] = v[k];
+      }
     }
   } else {
     for (int i = threadIdx.x; i < ng * n; i += blockDim.x) {
@@ -228,21 +262,25 @@ __global__ void __launch_bounds__(kThreads) down_kernel(GemvArgs a) {
   if (bad) set_status(a.status, kStatusNonFinite);
 }
 
-int grid_for(int items, int sm_count) { return std::max(1, std::min(items, sm_count * 4)); }
+int grid_for(int items, int sm_count) { return std::max(1, std::min(items, sm_count * 8)); }
 
 }  // namespace
+
+template <typename K>
+void ensure_smem(K kernel, size_t smem) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
 
 cudaError_t launch_gate_up(const GemvArgs &a, cudaStream_t s) {
   const int nblk = (a.I + kGURows - 1) / kGURows;
   const int grid = grid_for(a.n_active_max * nblk, a.sm_count);
   const size_t smem = sizeof(float) * kTG * a.H;
   if (a.H % 8 == 0 && a.vec) {
-    cudaFuncSetAttribute(gate_up_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    ensure_smem(gate_up_kernel<true>, smem);
     gate_up_kernel<true><<<grid, kThreads, smem, s>>>(a);
   } else {
-    cudaFuncSetAttribute(gate_up_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    ensure_smem(gate_up_kernel<false>, smem);
     gate_up_kernel<false><<<grid, kThreads, smem, s>>>(a);
   }
   return cudaGetLastError();
@@ -253,12 +291,10 @@ cudaError_t launch_down(const GemvArgs &a, cudaStream_t s) {
   const int grid = grid_for(a.n_active_max * nblk, a.sm_count);
   const size_t smem = sizeof(float) * kTG * a.I;
   if (a.I % 8 == 0 && a.vec) {
-    cudaFuncSetAttribute(down_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    ensure_smem(down_kernel<true>, smem);
     down_kernel<true><<<grid, kThreads, smem, s>>>(a);
   } else {
-    cudaFuncSetAttribute(down_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    ensure_smem(down_kernel<false>, smem);
     down_kernel<false><<<grid, kThreads, smem, s>>>(a);
   }
   return cudaGetLastError();

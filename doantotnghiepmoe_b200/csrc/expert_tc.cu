@@ -39,13 +39,10 @@ namespace tc {
 namespace {
 
 constexpr int BM = 128;          // weight rows per tile (UMMA M)
-constexpr int BN = kTcBlockN;    // routes per tile (UMMA N)
 constexpr int BK = 128;          // int8 K elements per stage (= 128 B swizzle row)
 constexpr int UK = 32;           // K per tcgen05.mma kind::i8
 constexpr int kThreads = 192;
-constexpr int kStages1 = 3;      // gate/up: 4 tiles of 16 KB per stage
-constexpr int kStages2 = 4;      // down: 3 tiles of 16 KB per stage
-constexpr uint32_t kTileBytes = BM * BK;  // 16 KB (A and B tiles are both 128 x 128 B)
+constexpr uint32_t kTileBytes = BM * BK;  // 16 KB weight tile; a digit tile is BN * 128 B
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // ---------------------------------------------------------------------------
@@ -157,8 +154,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 
 // Instruction descriptor: s32 accumulate, s8 x s8, both K-major, M=128, N=BN.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+template <int BN>
+__host__ __device__ constexpr uint32_t idesc_i8() {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
 
 struct Pipe {
   uint64_t full[4];
@@ -177,11 +177,13 @@ __device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
 // Mainloop shared by both GEMMs: NA weight tiles x NB digit tiles per stage,
 // accumulator (a, b) at TMEM column (a * NB + b) * BN.
 // ---------------------------------------------------------------------------
-template <int NA, int NB, int S>
+template <int NA, int NB, int S, int BN>
 __device__ __forceinline__ void mainloop(Pipe &pp, uint8_t *tiles, const CUtensorMap *mapA,
                                          const CUtensorMap *mapB, const int a_row[NA], int a_e,
                                          int b_row, int nk, uint32_t tmem) {
-  constexpr uint32_t kStageBytes = (NA + NB) * kTileBytes;
+  constexpr uint32_t kBTile = BN * BK;
+  constexpr uint32_t kStageBytes = NA * kTileBytes + NB * kBTile;
+  constexpr uint32_t kIdesc = idesc_i8<BN>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0 && lane == 0) {
     int issued = 0;
@@ -199,7 +201,7 @@ __device__ __forceinline__ void mainloop(Pipe &pp, uint8_t *tiles, const CUtenso
         tma_load_3d(st + a * kTileBytes, mapA, &pp.full[s], kb * BK, a_row[a], a_e);
 #pragma unroll
       for (int b = 0; b < NB; ++b)
-        tma_load_3d(st + (NA + b) * kTileBytes, mapB, &pp.full[s], kb * BK, b_row, b);
+        tma_load_3d(st + NA * kTileBytes + b * kBTile, mapB, &pp.full[s], kb * BK, b_row, b);
       ++issued;
     }
     // On abort, the stages issued but not yet consumed must land before the
@@ -225,7 +227,7 @@ __device__ __forceinline__ void mainloop(Pipe &pp, uint8_t *tiles, const CUtenso
           const uint64_t ad = sw128_desc(base + a * kTileBytes + k * UK);
 #pragma unroll
           for (int b = 0; b < NB; ++b) {
-            const uint64_t bd = sw128_desc(base + (NA + b) * kTileBytes + k * UK);
+            const uint64_t bd = sw128_desc(base + NA * kTileBytes + b * kBTile + k * UK);
             mma_i8(tmem + (uint32_t)((a * NB + b) * BN), ad, bd, kIdesc,
                    (kb > 0 || k > 0) ? 1u : 0u);
           }
@@ -263,41 +265,58 @@ __device__ __forceinline__ void teardown(Pipe &pp, uint32_t ncols, uint32_t *sta
   if ((threadIdx.x >> 5) == 1) tmem_dealloc(pp.tmem_base, ncols);
 }
 
-// Dynamic smem: [Pipe | pad | tiles (1024-aligned)].
-constexpr size_t smem_bytes(int na, int nb, int stages) {
-  return 1024 + sizeof(Pipe) + 1024 + (size_t)stages * (na + nb) * kTileBytes;
+// Dynamic smem: [Pipe | per-route epilogue table | pad | tiles (1024-aligned)].
+struct RouteTab {
+  float s1[128], s2[128], gate[128];
+  int32_t tok[128], slot[128];
+};
+constexpr size_t smem_bytes(int na, int nb, int bn, int stages) {
+  return 1024 + sizeof(Pipe) + sizeof(RouteTab) + 1024 +
+         (size_t)stages * (na * kTileBytes + nb * bn * BK);
 }
+
+// Named barrier among the four epilogue warps (ids 1.., 128 threads).
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // GEMM 1: gate/up.  A = gate rows [m0, m0+128) and up rows [I+m0, ...) of
-// expert e; B = the two digit planes of the tile's routes.
+// expert e; B = the two digit planes of the tile's routes.  BN routes per
+// tile, S pipeline stages; MINB CTAs per SM.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int S, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB)
     gate_up_tc_kernel(const __grid_constant__ CUtensorMap mapW,
                       const __grid_constant__ CUtensorMap mapX, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const int g = blockIdx.y;
   if (g >= *a.n_tiles) return;
   Pipe &pp = *reinterpret_cast<Pipe *>(smem_raw);
-  uint8_t *tiles = align1024(smem_raw + sizeof(Pipe));
+  RouteTab &tab = *reinterpret_cast<RouteTab *>(smem_raw + sizeof(Pipe));
+  uint8_t *tiles = align1024(smem_raw + sizeof(Pipe) + sizeof(RouteTab));
   const int e = a.tile_expert[g], r0 = a.tile_row0[g], nr = a.tile_rows[g];
   const int m0 = blockIdx.x * BM;
   const int nk = (a.H + BK - 1) / BK;
   constexpr uint32_t kCols = 4 * BN;
-  setup(pp, kStages1, kCols);
+  setup(pp, S, kCols);
   const int arow[2] = {m0, a.I + m0};
-  mainloop<2, 2, kStages1>(pp, tiles, &mapW, &mapX, arow, e, r0, nk, pp.tmem_base);
+  mainloop<2, 2, S, BN>(pp, tiles, &mapW, &mapX, arow, e, r0, nk, pp.tmem_base);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= 2) {
+    // while the mainloop runs: this tile's per-route scales into smem
+    for (int c = threadIdx.x - 64; c < nr; c += 128) {
+      tab.s1[c] = a.xs1[r0 + c];
+      tab.s2[c] = a.xs2[r0 + c];
+    }
     const int q = warp & 3;
     const int i = m0 + 32 * q + lane;  // weight row of this thread
+    const float *Sc = a.s_ptr[e];
+    const float sg = i < a.I ? Sc[i] : 0.0f, su = i < a.I ? Sc[a.I + i] : 0.0f;
+    epi_sync();
     bool ok = mbar_wait(&pp.done, 0, &pp.abort_flag);
     if (!ok) pp.abort_flag = 1;
     ok = ok && !*(volatile int *)&pp.abort_flag;  // an aborted mainloop leaves partial sums
     if (ok) {
       fence_after_sync();
-      const float *S = a.s_ptr[e];
-      const float sg = i < a.I ? S[i] : 0.0f, su = i < a.I ? S[a.I + i] : 0.0f;
       const uint32_t trow = pp.tmem_base + ((uint32_t)(32 * q) << 16);
       for (int c0 = 0; c0 < BN; c0 += 16) {
         if (c0 >= nr) break;  // warp-uniform
@@ -311,11 +330,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           float act = 0.0f;
           if (c < nr) {
             const int r = r0 + c;
-            const float s1 = a.xs1[r], s2 = a.xs2[r];
+            const float s1 = tab.s1[c], s2 = tab.s2[c];
             const float gd = fmaf(s1, (float)v[0][j], s2 * (float)v[1][j]);
             const float ud = fmaf(s1, (float)v[2][j], s2 * (float)v[3][j]);
             const float gg = gd * sg, uu = ud * su;
-            act = gg / (1.0f + expf_ref(-gg)) * uu;
+            // tolerance path: the hardware exp (the GEMV path keeps libm's)
+            act = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
             if (i < a.I) a.act[(size_t)r * a.I + i] = act;
           }
           // max |act| over this warp's 32 rows for route column c
@@ -335,31 +355,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 // digit planes of the tile's activations.  Epilogue writes gate * y into the
 // (token, slot) contribution row.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int S, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB)
     down_tc_kernel(const __grid_constant__ CUtensorMap mapW,
                    const __grid_constant__ CUtensorMap mapA, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const int g = blockIdx.y;
   if (g >= *a.n_tiles) return;
   Pipe &pp = *reinterpret_cast<Pipe *>(smem_raw);
-  uint8_t *tiles = align1024(smem_raw + sizeof(Pipe));
+  RouteTab &tab = *reinterpret_cast<RouteTab *>(smem_raw + sizeof(Pipe));
+  uint8_t *tiles = align1024(smem_raw + sizeof(Pipe) + sizeof(RouteTab));
   const int e = a.tile_expert[g], r0 = a.tile_row0[g], nr = a.tile_rows[g];
   const int m0 = blockIdx.x * BM;
   const int nk = (a.I + BK - 1) / BK;
   constexpr uint32_t kCols = 2 * BN;
-  setup(pp, kStages2, kCols);
+  setup(pp, S, kCols);
   const int arow[1] = {m0};
-  mainloop<1, 2, kStages2>(pp, tiles, &mapW, &mapA, arow, e, r0, nk, pp.tmem_base);
+  mainloop<1, 2, S, BN>(pp, tiles, &mapW, &mapA, arow, e, r0, nk, pp.tmem_base);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= 2) {
+    for (int c = threadIdx.x - 64; c < nr; c += 128) {
+      const int r = r0 + c;
+      tab.s1[c] = a.as1[r];
+      tab.s2[c] = a.as2[r];
+      tab.gate[c] = a.r_gate[r];
+      tab.tok[c] = a.r_token[r];
+      tab.slot[c] = a.r_slot[r];
+    }
     const int q = warp & 3;
     const int j = m0 + 32 * q + lane;  // output row (hidden index)
+    const float sd = j < a.H ? a.s_ptr[e][2 * a.I + j] : 0.0f;
+    epi_sync();
     bool ok = mbar_wait(&pp.done, 0, &pp.abort_flag);
     if (!ok) pp.abort_flag = 1;
     ok = ok && !*(volatile int *)&pp.abort_flag;  // an aborted mainloop leaves partial sums
     if (ok) {
       fence_after_sync();
-      const float sd = j < a.H ? a.s_ptr[e][2 * a.I + j] : 0.0f;
       const uint32_t trow = pp.tmem_base + ((uint32_t)(32 * q) << 16);
       bool bad = false;
       for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -372,11 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int jj = 0; jj < 16; ++jj) {
           const int c = c0 + jj;
           if (c < nr && j < a.H) {
-            const int r = r0 + c;
-            const float y = fmaf(a.as1[r], (float)v[0][jj], a.as2[r] * (float)v[1][jj]) * sd;
+            const float y = fmaf(tab.s1[c], (float)v[0][jj], tab.s2[c] * (float)v[1][jj]) * sd;
             bad |= !is_finite_f(y);
-            const int tok = a.r_token[r], slot = a.r_slot[r];
-            a.contrib[((size_t)tok * a.K + slot) * a.H + j] = __fmul_rn(a.r_gate[r], y);
+            a.contrib[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + j] =
+                __fmul_rn(tab.gate[c], y);
           }
         }
       }
@@ -389,23 +419,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Tile table and activation digit planes
 // ---------------------------------------------------------------------------
-__global__ void build_tiles_kernel(const int32_t *seg_off, const int32_t *active,
-                                   const int32_t *n_active, int32_t *tile_expert,
-                                   int32_t *tile_row0, int32_t *tile_rows, int32_t *n_tiles,
-                                   int max_tiles) {
-  if (threadIdx.x != 0) return;
-  int n = 0;
+// Tile table: tile t of the layer covers routes [row0, row0 + rows) of one
+// expert.  One thread per active expert; block-wide exclusive scan of the
+// per-expert tile counts (E <= 256).
+__global__ void __launch_bounds__(256) build_tiles_kernel(const int32_t *seg_off,
+                                                          const int32_t *active,
+                                                          const int32_t *n_active, int bn,
+                                                          int32_t *tile_expert,
+                                                          int32_t *tile_row0, int32_t *tile_rows,
+                                                          int32_t *n_tiles, int max_tiles) {
+  __shared__ int32_t scan[256];
+  const int j = threadIdx.x;
   const int na = *n_active;
-  for (int j = 0; j < na; ++j) {
-    const int e = active[j];
-    for (int r = seg_off[e]; r < seg_off[e + 1] && n < max_tiles; r += BN) {
-      tile_expert[n] = e;
-      tile_row0[n] = r;
-      tile_rows[n] = min(BN, seg_off[e + 1] - r);
-      ++n;
-    }
+  int e = -1, cnt = 0;
+  if (j < na) {
+    e = active[j];
+    cnt = (seg_off[e + 1] - seg_off[e] + bn - 1) / bn;
   }
-  *n_tiles = n;
+  scan[j] = cnt;
+  __syncthreads();
+  for (int o = 1; o < 256; o <<= 1) {  // inclusive Hillis-Steele scan
+    const int v = j >= o ? scan[j - o] : 0;
+    __syncthreads();
+    scan[j] += v;
+    __syncthreads();
+  }
+  const int first = scan[j] - cnt;
+  for (int k = 0; k < cnt && first + k < max_tiles; ++k) {
+    const int r = seg_off[e] + k * bn;
+    tile_expert[first + k] = e;
+    tile_row0[first + k] = r;
+    tile_rows[first + k] = min(bn, seg_off[e + 1] - r);
+  }
+  if (j == 255) *n_tiles = min(scan[255], max_tiles);
 }
 
 // One warp per route row: s = max|v| / 127, d1 = rint(v/s), d2 = rint((v/s - d1) * 254).
@@ -474,13 +520,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 }  // namespace
 
 bool encode_map3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
-                  uint64_t stride1, uint64_t stride2) {
+                  uint64_t stride1, uint64_t stride2, uint32_t box_rows) {
   auto enc = encoder();
   if (!enc) return false;
   if (((uintptr_t)base & 15) || (stride1 & 15) || (stride2 & 15)) return false;
   cuuint64_t dims[3] = {d0, d1, d2};
   cuuint64_t strides[2] = {stride1, stride2};
-  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)BM, 1};
+  cuuint32_t box[3] = {(cuuint32_t)BK, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims,
                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -490,11 +536,11 @@ bool encode_map3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, 
 }
 
 cudaError_t launch_build_tiles(const int32_t *seg_off, const int32_t *active,
-                               const int32_t *n_active, int32_t *tile_expert, int32_t *tile_row0,
-                               int32_t *tile_rows, int32_t *n_tiles, int max_tiles,
-                               cudaStream_t s) {
-  build_tiles_kernel<<<1, 32, 0, s>>>(seg_off, active, n_active, tile_expert, tile_row0,
-                                      tile_rows, n_tiles, max_tiles);
+                               const int32_t *n_active, int bn, int32_t *tile_expert,
+                               int32_t *tile_row0, int32_t *tile_rows, int32_t *n_tiles,
+                               int max_tiles, cudaStream_t s) {
+  build_tiles_kernel<<<1, 256, 0, s>>>(seg_off, active, n_active, bn, tile_expert, tile_row0,
+                                       tile_rows, n_tiles, max_tiles);
   return cudaGetLastError();
 }
 
@@ -507,23 +553,41 @@ cudaError_t launch_quantize_rows(const float *src, const int32_t *rows, const ui
   return cudaGetLastError();
 }
 
-cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
-                              int max_tiles, cudaStream_t s) {
-  const size_t smem = smem_bytes(2, 2, kStages1);
-  cudaFuncSetAttribute(gate_up_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       (int)smem);
+// Tile configurations.  BN = 64: 2 CTAs per SM (TMEM 4*64 and 2*64 columns,
+// 96 KB of pipeline each).  BN = 128: gate/up one CTA per SM (512 TMEM
+// columns, 3 stages), down two per SM.
+template <int BN, int S, int MINB>
+cudaError_t launch_gu(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
+                      int max_tiles, cudaStream_t s) {
+  const size_t smem = smem_bytes(2, 2, BN, S);
+  auto k = gate_up_tc_kernel<BN, S, MINB>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((a.I + BM - 1) / BM, max_tiles);
-  gate_up_tc_kernel<<<grid, kThreads, smem, s>>>(mapW, mapX, a);
+  k<<<grid, kThreads, smem, s>>>(mapW, mapX, a);
   return cudaGetLastError();
 }
 
-cudaError_t launch_down_tc(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
-                           int max_tiles, cudaStream_t s) {
-  const size_t smem = smem_bytes(1, 2, kStages2);
-  cudaFuncSetAttribute(down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+template <int BN, int S, int MINB>
+cudaError_t launch_dn(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
+                      int max_tiles, cudaStream_t s) {
+  const size_t smem = smem_bytes(1, 2, BN, S);
+  auto k = down_tc_kernel<BN, S, MINB>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((a.H + BM - 1) / BM, max_tiles);
-  down_tc_kernel<<<grid, kThreads, smem, s>>>(mapW, mapA, a);
+  k<<<grid, kThreads, smem, s>>>(mapW, mapA, a);
   return cudaGetLastError();
+}
+
+cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
+                              int bn, int max_tiles, cudaStream_t s) {
+  return bn == 64 ? launch_gu<64, 2, 2>(mapW, mapX, a, max_tiles, s)
+                  : launch_gu<128, 3, 1>(mapW, mapX, a, max_tiles, s);
+}
+
+cudaError_t launch_down_tc(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
+                           int bn, int max_tiles, cudaStream_t s) {
+  return bn == 64 ? launch_dn<64, 3, 2>(mapW, mapA, a, max_tiles, s)
+                  : launch_dn<128, 2, 2>(mapW, mapA, a, max_tiles, s);
 }
 
 }  // namespace tc

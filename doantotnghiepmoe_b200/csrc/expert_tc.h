@@ -10,13 +10,15 @@
 namespace moe {
 namespace tc {
 
-constexpr int kTcBlockN = 128;  // routes per GEMM tile
+// Routes per GEMM tile: 64 when experts average few routes (prefill of a
+// few hundred tokens), 128 otherwise.
+inline int tc_block_n(int routes, int experts) { return routes <= 96 * experts ? 64 : 128; }
 
 struct TcArgs {
   int H, I, K;
   const int32_t *tile_expert;  // [max_tiles] expert of each route tile
   const int32_t *tile_row0;    // [max_tiles] first permuted route of the tile
-  const int32_t *tile_rows;    // [max_tiles] routes in the tile (<= kTcBlockN)
+  const int32_t *tile_rows;    // [max_tiles] routes in the tile (<= the tile width)
   const int32_t *n_tiles;      // device count of valid tiles
   const float *const *s_ptr;   // per-expert scales [gate I | up I | down H]
   const float *xs1, *xs2;      // per-route digit scales of the inputs
@@ -31,21 +33,21 @@ struct TcArgs {
 
 // 3D uint8 tiled map with a 128 x 128 box and 128-byte swizzle.
 bool encode_map3d(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
-                  uint64_t stride1, uint64_t stride2);
+                  uint64_t stride1, uint64_t stride2, uint32_t box_rows);
 
 cudaError_t launch_build_tiles(const int32_t *seg_off, const int32_t *active,
-                               const int32_t *n_active, int32_t *tile_expert, int32_t *tile_row0,
-                               int32_t *tile_rows, int32_t *n_tiles, int max_tiles,
-                               cudaStream_t s);
+                               const int32_t *n_active, int bn, int32_t *tile_expert,
+                               int32_t *tile_row0, int32_t *tile_rows, int32_t *n_tiles,
+                               int max_tiles, cudaStream_t s);
 
 cudaError_t launch_quantize_rows(const float *src, const int32_t *rows, const uint32_t *amax_in,
                                  int R, int n, int8_t *q, size_t plane, float *s1, float *s2,
                                  uint32_t *amax_reset, cudaStream_t s);
 
 cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
-                              int max_tiles, cudaStream_t s);
+                              int bn, int max_tiles, cudaStream_t s);
 cudaError_t launch_down_tc(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
-                           int max_tiles, cudaStream_t s);
+                           int bn, int max_tiles, cudaStream_t s);
 
 }  // namespace tc
 }  // namespace moe

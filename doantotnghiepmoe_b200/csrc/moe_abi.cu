@@ -328,7 +328,7 @@ struct moe_handle {
   float *xs1 = nullptr, *xs2 = nullptr, *as1 = nullptr, *as2 = nullptr;
   uint32_t *act_amax = nullptr;
   int32_t *tile_expert = nullptr, *tile_row0 = nullptr, *tile_rows = nullptr, *n_tiles = nullptr;
-  CUtensorMap map_x{}, map_a{};
+  CUtensorMap map_x64{}, map_x128{}, map_a64{}, map_a128{};  // digit planes, box 64/128 rows
 };
 
 namespace {
@@ -437,10 +437,11 @@ moe_status tensor_experts(moe_handle *h, const LayerSlot &L, const float *d_h,
   const int H = h->d.hidden, I = h->d.intermediate, K = h->d.top_k;
   const int R = T * K;
   const size_t Rcap = (size_t)h->d.max_tokens * K;
+  const int bn = tc::tc_block_n(R, h->d.num_experts);
   cudaError_t e;
   cudaEvent_t p0 = h->prof.begin(s);
-  e = tc::launch_build_tiles(h->seg_off, h->active, h->n_active, h->tile_expert, h->tile_row0,
-                             h->tile_rows, h->n_tiles, h->max_tiles, s);
+  e = tc::launch_build_tiles(h->seg_off, h->active, h->n_active, bn, h->tile_expert,
+                             h->tile_row0, h->tile_rows, h->n_tiles, h->max_tiles, s);
   if (e == cudaSuccess)
     e = tc::launch_quantize_rows(d_h, h->r_token, nullptr, R, H, h->xq, Rcap * H, h->xs1, h->xs2,
                                  h->act_amax, s);
@@ -466,10 +467,9 @@ moe_status tensor_experts(moe_handle *h, const LayerSlot &L, const float *d_h,
   a.r_gate = h->r_gate;
   a.contrib = h->contrib;
   a.status = h->status;
-  const int tiles = std::min(h->max_tiles, (R + tc::kTcBlockN - 1) / tc::kTcBlockN +
-                                               std::min(h->d.num_experts, R));
+  const int tiles = std::min(h->max_tiles, (R + bn - 1) / bn + std::min(h->d.num_experts, R));
   p0 = h->prof.begin(s);
-  e = tc::launch_gate_up_tc(L.map_gu, h->map_x, a, tiles, s);
+  e = tc::launch_gate_up_tc(L.map_gu, bn == 64 ? h->map_x64 : h->map_x128, a, bn, tiles, s);
   h->prof.end("gate_up_tc", p0, s);
   if (e == cudaSuccess) {
     p0 = h->prof.begin(s);
@@ -479,7 +479,7 @@ moe_status tensor_experts(moe_handle *h, const LayerSlot &L, const float *d_h,
   }
   if (e == cudaSuccess) {
     p0 = h->prof.begin(s);
-    e = tc::launch_down_tc(L.map_dn, h->map_a, a, tiles, s);
+    e = tc::launch_down_tc(L.map_dn, bn == 64 ? h->map_a64 : h->map_a128, a, bn, tiles, s);
     h->prof.end("down_tc", p0, s);
   }
   if (e == cudaSuccess) {
@@ -585,7 +585,7 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && cudaMemset(h->status, 0, 4) == cudaSuccess;
   // tensor-core path scratch and the activation-side tensor maps
   const size_t R = T * K;
-  h->max_tiles = (int)((R + tc::kTcBlockN - 1) / tc::kTcBlockN + std::min(E, R));
+  h->max_tiles = (int)((R + 63) / 64 + std::min(E, R));  // bound for the 64-route tiles
   ok = ok && dalloc(&h->xq, 2 * R * H) == cudaSuccess;
   ok = ok && dalloc(&h->aq, 2 * R * I) == cudaSuccess;
   ok = ok && dalloc(&h->xs1, R) == cudaSuccess && dalloc(&h->xs2, R) == cudaSuccess;
@@ -601,8 +601,10 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
     return MOE_ERR_NOMEM;
   }
   h->tc_ok = H % 16 == 0 && I % 16 == 0 &&
-             tc::encode_map3d(&h->map_x, h->xq, H, R, 2, H, R * H) &&
-             tc::encode_map3d(&h->map_a, h->aq, I, R, 2, I, R * I);
+             tc::encode_map3d(&h->map_x64, h->xq, H, R, 2, H, R * H, 64) &&
+             tc::encode_map3d(&h->map_x128, h->xq, H, R, 2, H, R * H, 128) &&
+             tc::encode_map3d(&h->map_a64, h->aq, I, R, 2, I, R * I, 64) &&
+             tc::encode_map3d(&h->map_a128, h->aq, I, R, 2, I, R * I, 128);
   *out = h;
   return MOE_OK;
 }
@@ -681,8 +683,8 @@ extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const 
              (const float *)d_scales[e] == (const float *)d_scales[0] + e * (2 * I + H);
   const char *wb = (const char *)d_weights[0];
   L.tc_ok = packed && h->tc_ok &&
-            tc::encode_map3d(&L.map_gu, wb, H, 2 * I, E, H, 3 * I * H) &&
-            tc::encode_map3d(&L.map_dn, wb + 2 * I * H, I, H, E, I, 3 * I * H);
+            tc::encode_map3d(&L.map_gu, wb, H, 2 * I, E, H, 3 * I * H, 128) &&
+            tc::encode_map3d(&L.map_dn, wb + 2 * I * H, I, H, E, I, 3 * I * H, 128);
   L.set = true;
   return MOE_OK;
 }

@@ -20,7 +20,6 @@ namespace moe {
 namespace {
 
 constexpr int kRouteThreads = 256;
-constexpr int kChunkCols = 256;  // columns of h / W staged per smem pass
 
 __device__ __forceinline__ float load_w(const void *W, int dtype, size_t idx) {
   if (dtype == kRouterBF16) {
@@ -30,80 +29,167 @@ __device__ __forceinline__ float load_w(const void *W, int dtype, size_t idx) {
   return reinterpret_cast<const float *>(W)[idx];
 }
 
-// One CTA computes logits for a tile of TT tokens x TE experts.  Thread
-// (t, e, lane) owns accumulator `lane` of the 8-lane chain for (t, e).  All
-// 256 threads stage h / W columns through shared memory; the first
-// 8*TE*TT threads run the chains.
-template <int TT, int TE>
-__global__ void __launch_bounds__(kRouteThreads) route_logits_kernel(RouteArgs a) {
-  __shared__ float hs[TT][kChunkCols];
-  __shared__ float ws[TE][kChunkCols];
+// Small T (decode): one CTA per (token, 4 experts).  The token row and the 4
+// router rows are staged into shared memory in one shot -- every thread
+// issues its loads of a batch before the first store -- so the kernel pays
+// about one memory round trip; then 32 threads run the 8-lane chains.
+constexpr int kSmallTE = 4;
+__global__ void __launch_bounds__(kRouteThreads) route_logits_small_kernel(RouteArgs a) {
+  extern __shared__ float sm[];  // [1 + kSmallTE][H]
   const int tid = threadIdx.x;
-  const int e0 = blockIdx.x * TE, t0 = blockIdx.y * TT;
-  const int lane = tid & 7;
-  const int el = (tid >> 3) % TE;
-  const int tl = tid / (8 * TE);
-  const bool worker = tid < 8 * TE * TT;
+  const int e0 = blockIdx.x * kSmallTE, t = blockIdx.y;
   const int H = a.H;
-  const int full = H / 8;  // complete chunks of eight
-  // Rust's f32 `Sum` folds from -0.0; the 8-lane chains start at 0.0
-  // (`[0.0f32; 8]`, src/backend.rs:107).
-  float acc = a.router_dtype == kRouterF32Seq ? -0.0f : 0.0f;
+  float *hs = sm, *ws = sm + H;
   bool bad_input = false;
-  for (int c0 = 0; c0 < H; c0 += kChunkCols) {
-    const int ncol = min(kChunkCols, H - c0);
-    for (int i = tid; i < TT * kChunkCols; i += kRouteThreads) {
-      const int r = i / kChunkCols, c = i % kChunkCols;
-      float v = 0.0f;
-      if (t0 + r < a.T && c < ncol) {
-        v = a.h[(size_t)(t0 + r) * H + c0 + c];
-        if (blockIdx.x == 0 && !is_finite_f(v)) bad_input = true;
-      }
-      hs[r][c] = v;
-    }
-    for (int i = tid; i < TE * kChunkCols; i += kRouteThreads) {
-      const int r = i / kChunkCols, c = i % kChunkCols;
-      ws[r][c] = (e0 + r < a.E && c < ncol) ? load_w(a.router, a.router_dtype,
-                                                     (size_t)(e0 + r) * H + c0 + c)
-                                            : 0.0f;
-    }
-    __syncthreads();
-    if (worker) {
-      const int nchunk = min(ncol, full * 8 - c0) / 8;  // complete chunks in this pass
-      if (a.router_dtype == kRouterF32Seq) {
-        // src/router.rs:59-62: one sequential chain; lane 0 carries it.
-        if (lane == 0)
-          for (int c = 0; c < ncol; ++c) acc = __fadd_rn(acc, __fmul_rn(ws[el][c], hs[tl][c]));
-      } else {
-#pragma unroll 8
-        for (int c = 0; c < nchunk; ++c)
-          acc = __fadd_rn(acc, __fmul_rn(ws[el][8 * c + lane], hs[tl][8 * c + lane]));
+  constexpr int kBatch = 8;
+  const int total = (1 + kSmallTE) * H;
+  for (int base = 0; base < total; base += kRouteThreads * kBatch) {
+    float v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = base + k * kRouteThreads + tid;
+      v[k] = 0.0f;
+      if (i < H) {
+        v[k] = a.h[(size_t)t * H + i];
+      } else if (i < total) {
+        const int r = i / H - 1, c = i % H;
+        if (e0 + r < a.E) v[k] = load_w(a.router, a.router_dtype, (size_t)(e0 + r) * H + c);
       }
     }
-    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = base + k * kRouteThreads + tid;
+      if (i < total) {
+        sm[i] = v[k];
+        if (i < H && blockIdx.x == 0 && !is_finite_f(v[k])) bad_input = true;
+      }
+    }
   }
+  __syncthreads();
   if (bad_input) set_status(a.status, kStatusNonFinite);
-  if (!worker) return;
-  const int t = t0 + tl, e = e0 + el;
+  if (tid >= 8 * kSmallTE) return;
+  const int lane = tid & 7, el = tid >> 3, e = e0 + el;
+  const float *w = ws + (size_t)el * H;
+  const int full = H / 8;
   float logit;
   if (a.router_dtype == kRouterF32Seq) {
+    // src/router.rs:59-62: one sequential chain (from -0.0, Rust's f32 Sum)
+    float acc = -0.0f;
+    if (lane == 0)
+      for (int c = 0; c < H; ++c) acc = __fadd_rn(acc, __fmul_rn(w[c], hs[c]));
     logit = acc;
   } else {
-    // Fold the 8 lanes in order starting from -0.0, then the tail.
+    float acc = 0.0f;  // `[0.0f32; 8]`, src/backend.rs:107
+#pragma unroll 8
+    for (int c = 0; c < full; ++c)
+      acc = __fadd_rn(acc, __fmul_rn(w[8 * c + lane], hs[8 * c + lane]));
     float s = -0.0f;
-    const int base = (threadIdx.x & 31) & ~7;
+    const int base = (tid & 31) & ~7;
 #pragma unroll
     for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc, base + l));
+    for (int i = full * 8; i < H; ++i) s = __fadd_rn(s, __fmul_rn(w[i], hs[i]));
     logit = s;
-    if (lane == 0 && t < a.T && e < a.E)
-      for (int i = full * 8; i < H; ++i)
-        logit = __fadd_rn(logit, __fmul_rn(load_w(a.router, a.router_dtype, (size_t)e * H + i),
-                                           a.h[(size_t)t * H + i]));
   }
-  if (lane == 0 && t < a.T && e < a.E) {
+  if (lane == 0 && e < a.E) {
     a.logits[(size_t)t * a.E + e] = logit;
     if (!is_finite_f(logit)) set_status(a.status, kStatusNonFinite);
   }
+}
+
+// Register-tiled logits for larger T.  A CTA covers 32 tokens x 16 experts;
+// thread (lane l, token group, expert group) owns lane l of the 8-lane chain
+// of 4 x 4 (token, expert) pairs, so each shared-memory load feeds four
+// multiply-adds and every chain still runs in chunk order.
+constexpr int kTT = 32, kTE = 16, kCW = 128;  // tokens, experts, columns per pass
+constexpr int kHStride = kCW + 2;             // padding: conflict-free token rows
+__global__ void __launch_bounds__(256) route_logits_tiled_kernel(RouteArgs a) {
+  __shared__ float hs[kTT][kHStride];
+  __shared__ float ws[kTE][kCW];
+  const int tid = threadIdx.x;
+  const int l = tid & 7, st = tid >> 3;
+  const int tg = st & 7, eg = st >> 3;  // 8 token groups x 4 expert groups
+  const int t0 = blockIdx.y * kTT, e0 = blockIdx.x * kTE;
+  const int H = a.H, full = H / 8;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  bool bad_input = false;
+  // Software pipeline: the loads of pass p+1 go out into registers before
+  // pass p is computed, and are stored to shared memory after it.
+  constexpr int kHPer = kTT * kCW / 256, kWPer = kTE * kCW / 256;
+  float hreg[kHPer], wreg[kWPer];
+  auto fetch = [&](int c0) {
+    const int ncol = min(kCW, full * 8 - c0);
+#pragma unroll
+    for (int k = 0; k < kHPer; ++k) {
+      const int i = k * 256 + tid, r = i / kCW, c = i % kCW;
+      hreg[k] = (t0 + r < a.T && c < ncol) ? a.h[(size_t)(t0 + r) * H + c0 + c] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kWPer; ++k) {
+      const int i = k * 256 + tid, r = i / kCW, c = i % kCW;
+      wreg[k] = (e0 + r < a.E && c < ncol)
+                    ? load_w(a.router, a.router_dtype, (size_t)(e0 + r) * H + c0 + c)
+                    : 0.0f;
+    }
+  };
+  if (full > 0) fetch(0);
+  for (int c0 = 0; c0 < full * 8; c0 += kCW) {
+    const int ncol = min(kCW, full * 8 - c0);
+#pragma unroll
+    for (int k = 0; k < kHPer; ++k) {
+      const int i = k * 256 + tid;
+      hs[i / kCW][i % kCW] = hreg[k];
+      if (blockIdx.x == 0 && !is_finite_f(hreg[k])) bad_input = true;
+    }
+#pragma unroll
+    for (int k = 0; k < kWPer; ++k) {
+      const int i = k * 256 + tid;
+      ws[i / kCW][i % kCW] = wreg[k];
+    }
+    __syncthreads();
+    if (c0 + kCW < full * 8) fetch(c0 + kCW);
+    const int nchunk = ncol / 8;
+#pragma unroll 4
+    for (int c = 0; c < nchunk; ++c) {
+      float hv[4], wv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hv[i] = hs[4 * tg + i][8 * c + l];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) wv[j] = ws[4 * eg + j][8 * c + l];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[j], hv[i]));
+    }
+    __syncthreads();
+  }
+  // tail columns (H % 8) are folded below; the finite check must see them too
+  if (blockIdx.x == 0)
+    for (int i = tid; i < kTT * (H - full * 8); i += 256) {
+      const int r = i / (H - full * 8), c = full * 8 + i % (H - full * 8);
+      if (t0 + r < a.T && !is_finite_f(a.h[(size_t)(t0 + r) * H + c])) bad_input = true;
+    }
+  if (bad_input) set_status(a.status, kStatusNonFinite);
+  const int base = (tid & 31) & ~7;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float s = -0.0f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc[i][j], base + k));
+      const int t = t0 + 4 * tg + i, e = e0 + 4 * eg + j;
+      if (l == 0 && t < a.T && e < a.E) {
+        for (int c = full * 8; c < H; ++c)
+          s = __fadd_rn(s, __fmul_rn(load_w(a.router, a.router_dtype, (size_t)e * H + c),
+                                     a.h[(size_t)t * H + c]));
+        a.logits[(size_t)t * a.E + e] = s;
+        if (!is_finite_f(s)) set_status(a.status, kStatusNonFinite);
+      }
+    }
 }
 
 // One warp per token: softmax over all E in index order, then K rounds of a
@@ -292,14 +378,16 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(PermuteArgs a) {
 
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
-  if (a.T <= 4) {
-    constexpr int TT = 1, TE = 4;
-    dim3 grid((a.E + TE - 1) / TE, (a.T + TT - 1) / TT);
-    route_logits_kernel<TT, TE><<<grid, kRouteThreads, 0, s>>>(a);
+  const size_t small_smem = sizeof(float) * (size_t)(1 + kSmallTE) * a.H;
+  if (a.T >= 16 && a.router_dtype != kRouterF32Seq) {
+    dim3 grid((a.E + kTE - 1) / kTE, (a.T + kTT - 1) / kTT);
+    route_logits_tiled_kernel<<<grid, 256, 0, s>>>(a);
   } else {
-    constexpr int TT = 8, TE = 4;
-    dim3 grid((a.E + TE - 1) / TE, (a.T + TT - 1) / TT);
-    route_logits_kernel<TT, TE><<<grid, kRouteThreads, 0, s>>>(a);
+    if (small_smem > 48 * 1024)
+      cudaFuncSetAttribute(route_logits_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)small_smem);
+    dim3 grid((a.E + kSmallTE - 1) / kSmallTE, a.T);
+    route_logits_small_kernel<<<grid, kRouteThreads, small_smem, s>>>(a);
   }
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;

@@ -275,3 +275,35 @@ def test_invalid_arguments_rejected_before_launch():
     assert ei.value.status == _lib.MOE_ERR_INVALID
     with pytest.raises(M.MoeError):
         eng.forward(5, h[:2], out[:2])  # layer out of range
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_route_tiled_ragged_shapes(bf16):
+    """T >= 16 takes the register-tiled router; E not a multiple of the tile,
+    H with a ragged tail (H % 8 != 0), f32 and bf16 routers: bit-exact."""
+    T, H, E, K = 50, 1030, 20, 3
+    router = O.synth_normal(61, O.KIND_ROUTER, 0, E * H, 0.02).reshape(E, H)
+    if bf16:
+        bits16 = (router.view(np.uint32) >> 16).astype(np.uint16)
+        router = bits16.reshape(E, H)
+    lw = O.LayerWeights(H, 8, E, K, True, np.ascontiguousarray(router),
+                        np.zeros((E, 3 * 8 * H), np.int8), np.ones((E, 2 * 8 + H), np.float32),
+                        router_bf16=bf16)
+    h = O.synth_hidden(62, T, H)
+    eng = engine_for(lw, T)
+    ex, sc, rt = helpers.to_device(lw)
+    eng.set_layer_packed(0, ex, sc, rt)
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    gates = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    probs = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    eng.route(0, torch.from_numpy(h).cuda(), ids, gates, probs=probs)
+    torch.cuda.synchronize()
+    for t in range(T):
+        lg = np.empty(E, np.float32)
+        O.lib().oracle_router_logits(lw.router.ctypes.data, int(bf16), E, H, h[t].ctypes.data,
+                                     lg.ctypes.data)
+        p = O.softmax(lg)
+        rid, rg = O.topk(p, K, True)
+        assert np.array_equal(bits(probs.cpu().numpy()[t]), bits(p)), t
+        assert np.array_equal(ids.cpu().numpy()[t].astype(np.uint32), rid), t
+        assert np.array_equal(bits(gates.cpu().numpy()[t]), bits(rg)), t
