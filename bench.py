@@ -330,6 +330,9 @@ def main():
     # ---- roofline of the dominant kernel --------------------------------
     hbm_peak, _, peak_kind = measured_peaks()
     alg = algorithmic_bytes(cfg, D, T)
+    alg["fused_decode"] = alg["layer"] * n_stack  # one launch runs the whole step
+    phases = {k: v for k, v in prof.items() if ":" in k}
+    prof = {k: v for k, v in prof.items() if ":" not in k}
     top = max(prof.items(), key=lambda kv: kv[1][1]) if prof else ("none", (1, 0.0))
     kname, (klaunch, kms) = top
     k_avg_ms = kms / max(1, klaunch)
@@ -348,7 +351,8 @@ def main():
                 "peak_kind": peak_kind, "alg_bytes_per_launch": kbytes,
                 "mean_launch_ms": k_avg_ms,
                 "kernel_share": {k: round(v[1] / max(1e-9, sum(x[1] for x in prof.values())), 4)
-                                 for k, v in prof.items()}}
+                                 for k, v in prof.items()},
+                "fused_phases_us": {k: round(v[1] * 1e3, 2) for k, v in phases.items()}}
     layer_gbs = alg["layer"] * n_stack / (ms_max / 1e3) / 1e9
 
     cpu = None

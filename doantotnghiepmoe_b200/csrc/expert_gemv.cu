@@ -1,265 +1,65 @@
-// Grouped INT8 x FP32 GEMV over expert segments: the decode-sized expert path.
-//
-// Arithmetic is the reference's AVX2 path, operation for operation
-// (src/int8_expert.rs:380-458 `dot_i8_f32_avx2`, :653-781
-// `dot_i8_f32_pair_avx2`, :1058-1127 the `_seq` row loops):
-//   * a row dot of length n keeps 32 accumulators = 4 banks x 8 lanes; lane l
-//     of bank b is an FMA chain over elements 32c + 8b + l, c = 0 .. n/32-1;
-//   * banks fold as (b0 + b1) + (b2 + b3); leftover 8-chunks FMA into that;
-//   * 8 -> 4 -> 2 -> 1 fold ((t0+t4)+(t2+t6)) + ((t1+t5)+(t3+t7)); scalar tail
-//     with separate multiply and add;
-//   * g = dot_g * s_g, u = dot_u * s_u, act = (g / (1 + exp(-g))) * u;
-//     y = dot_d(act) * s_d.
-// On the GPU one thread holds one bank (its 8 lanes) of one row for up to
-// kTG tokens, so the four banks of a row sit in four adjacent lanes and fold
-// with warp shuffles.  Results are bit-identical to the CPU path.
+// Grouped INT8 x FP32 GEMV over expert segments, one launch per phase
+// (gate/up, then down): the decode-sized expert path used by the layer API
+// and by the GpuExpertKernels drop-in.  The arithmetic lives in
+// gemv_core.cuh; this file only maps work items to CTAs.
 //
 // Work decomposition: an item is (expert segment, block of rows); a
 // persistent grid walks the items.  Tokens of the segment are staged through
 // shared memory kTG at a time.
 #include <algorithm>
 
-#include "common.cuh"
+#include "gemv_core.cuh"
 #include "kernels.h"
 
 namespace moe {
 namespace {
 
-constexpr int kThreads = 128;       // 4 warps: small items, many CTAs per SM
-constexpr int kPF = 16;             // weight chunk-steps loaded ahead per thread (128 B)
-constexpr int kTG = 4;              // tokens per pass
-constexpr int kGURowsPerWarp = 4;   // gate/up: 8 lanes per row (4 gate + 4 up banks)
-constexpr int kGURows = kGURowsPerWarp * (kThreads / 32);
-constexpr int kDNRowsPerWarp = 8;   // down: 4 lanes per row
-constexpr int kDNRows = kDNRowsPerWarp * (kThreads / 32);
-
-// Streaming 8-byte weight load: read once, never reused by this CTA.
-__device__ __forceinline__ uint2 ldg_stream8(const int8_t *p) {
-  uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
-               : "=r"(v.x), "=r"(v.y)
-               : "l"(p));
-  return v;
-}
-
-template <bool kVec>
-__device__ __forceinline__ uint2 load_w8_raw(const int8_t *p) {
-  if (kVec) return ldg_stream8(p);
-  uint2 v;
-  v.x = (uint32_t)(uint8_t)p[0] | ((uint32_t)(uint8_t)p[1] << 8) |
-        ((uint32_t)(uint8_t)p[2] << 16) | ((uint32_t)(uint8_t)p[3] << 24);
-  v.y = (uint32_t)(uint8_t)p[4] | ((uint32_t)(uint8_t)p[5] << 8) |
-        ((uint32_t)(uint8_t)p[6] << 16) | ((uint32_t)(uint8_t)p[7] << 24);
-  return v;
-}
-
-template <bool kVec>
-__device__ __forceinline__ void load_x8(const float *p, float x[8]) {
-  if (kVec) {
-    const float4 a = *reinterpret_cast<const float4 *>(p);
-    const float4 b = *reinterpret_cast<const float4 *>(p + 4);
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-  } else {
-#pragma unroll
-    for (int l = 0; l < 8; ++l) x[l] = p[l];
-  }
-}
-
-// Bank `bank` of a row dot for ng (<= kTG) tokens whose inputs sit in smem
-// rows xs + t*ld.  Weights are fetched kPF chunk-steps ahead into registers so
-// that enough bytes are in flight to cover HBM latency; the FMA chains still
-// run strictly in chunk order.
-template <bool kVec>
-__device__ __forceinline__ void bank_chain(const int8_t *__restrict__ wrow,
-                                           const float *__restrict__ xs, int ld, int n, int bank,
-                                           int ng, float acc[kTG][8]) {
-#pragma unroll
-  for (int t = 0; t < kTG; ++t)
-#pragma unroll
-    for (int l = 0; l < 8; ++l) acc[t][l] = 0.0f;
-  const int nc = n / 32;
-  for (int c0 = 0; c0 < nc; c0 += kPF) {
-    uint2 raw[kPF];
-#pragma unroll
-    for (int i = 0; i < kPF; ++i)
-      if (c0 + i < nc) raw[i] = load_w8_raw<kVec>(wrow + 32 * (c0 + i) + 8 * bank);
-#pragma unroll
-    for (int i = 0; i < kPF; ++i) {
-      if (c0 + i < nc) {
-        const int off = 32 * (c0 + i) + 8 * bank;
-        float w[8];
-        i8x4_to_f32(raw[i].x, w[0], w[1], w[2], w[3]);
-        i8x4_to_f32(raw[i].y, w[4], w[5], w[6], w[7]);
-#pragma unroll
-        for (int t = 0; t < kTG; ++t) {
-          if (t < ng) {
-            float x[8];
-            load_x8<kVec>(xs + t * ld + off, x);
-#pragma unroll
-            for (int l = 0; l < 8; ++l) acc[t][l] = __fmaf_rn(w[l], x[l], acc[t][l]);
-          }
-        }
-      }
-    }
-  }
-}
-
-// Fold the four banks held by lanes L..L+3 into lane L's `tot`, then finish
-// the dot there: leftover 8-chunks, horizontal fold, scalar tail.
-__device__ __forceinline__ float fold_and_finish(const float acc[8], const int8_t *__restrict__ wrow,
-                                                 const float *__restrict__ x, int n,
-                                                 bool leader) {
-  float b1[8], b2[8], b3[8];
-#pragma unroll
-  for (int l = 0; l < 8; ++l) {
-    b1[l] = __shfl_down_sync(0xffffffffu, acc[l], 1);
-    b2[l] = __shfl_down_sync(0xffffffffu, acc[l], 2);
-    b3[l] = __shfl_down_sync(0xffffffffu, acc[l], 3);
-  }
-  if (!leader) return 0.0f;
-  float tot[8];
-#pragma unroll
-  for (int l = 0; l < 8; ++l) tot[l] = __fadd_rn(__fadd_rn(acc[l], b1[l]), __fadd_rn(b2[l], b3[l]));
-  int i = 32 * (n / 32);
-  for (; i + 8 <= n; i += 8)
-#pragma unroll
-    for (int l = 0; l < 8; ++l) tot[l] = __fmaf_rn((float)wrow[i + l], x[i + l], tot[l]);
-  const float s0 = __fadd_rn(tot[0], tot[4]), s1 = __fadd_rn(tot[1], tot[5]);
-  const float s2 = __fadd_rn(tot[2], tot[6]), s3 = __fadd_rn(tot[3], tot[7]);
-  float s = __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
-  for (; i < n; ++i) s = __fadd_rn(s, __fmul_rn((float)wrow[i], x[i]));
-  return s;
-}
+using namespace gemv;
+constexpr int kThreads = 128;  // 4 warps: small items, many CTAs per SM
 
 __device__ __forceinline__ int seg_count(const GemvArgs &a) {
   return a.n_active_dev ? *a.n_active_dev : a.n_active_max;
 }
 
-// Stage ng input rows (gathered through r_token) into smem.  Loads are
-// issued in batches of kSB per thread before any store, so a row costs about
-// one memory round trip instead of one per loop trip.
-constexpr int kSB = 8;
-template <bool kVec>
-__device__ __forceinline__ void stage_rows(float *__restrict__ xs, const float *__restrict__ src,
-                                           const int32_t *__restrict__ r_token, int g0, int ng,
-                                           int n) {
-  if (kVec) {
-    const int n4 = n / 4, total = ng * n4;
-    for (int base = 0; base < total; base += kThreads * kSB) {
-      float4 v[kSB];
-#pragma unroll
-      for (int k = 0; k < kSB; ++k) {
-        const int i = base + k * kThreads + threadIdx.x;
-        if (i < total) {
-          const int t = i / n4, c = i % n4;
-          const int row = r_token ? r_token[g0 + t] : g0 + t;
-          v[k] = reinterpret_cast<const float4 *>(src + (size_t)row * n)[c];
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < kSB; ++k) {
-        const int i = base + k * kThreads + threadIdx.x;
-        if (i < total) reinterpret_cast<float4 *>(xs)[(i / n4) * n4 + i % n4] = v[k];
-      }
-    }
-  } else {
-    for (int i = threadIdx.x; i < ng * n; i += blockDim.x) {
-      const int t = i / n, c = i % n;
-      const int row = r_token ? r_token[g0 + t] : g0 + t;
-      xs[t * n + c] = src[(size_t)row * n + c];
-    }
-  }
-}
-
 template <bool kVec>
 __global__ void __launch_bounds__(kThreads) gate_up_kernel(GemvArgs a) {
   extern __shared__ float xs[];  // [kTG][H]
-  const int H = a.H, I = a.I;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = lane & 7, bank = q & 3;
-  const bool is_up = q >= 4;
-  const int nblk = (I + kGURows - 1) / kGURows;
+  const int rows_per_item = kGURowsPerWarp * (kThreads / 32);
+  const int nblk = (a.I + rows_per_item - 1) / rows_per_item;
   const int nitems = seg_count(a) * nblk;
   for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
     const int j = item / nblk, b = item % nblk;
     const int e = a.active ? a.active[j] : j;
-    const int r0 = a.seg_off[e], r1 = a.seg_off[e + 1];
-    const int8_t *W = a.w_ptr[e];
-    const float *S = a.s_ptr[e];
-    const int row = b * kGURows + warp * kGURowsPerWarp + (lane >> 3);
-    const bool row_ok = row < I;
-    const int8_t *wrow = W + (is_up ? (size_t)I * H : 0) + (size_t)(row_ok ? row : 0) * H;
-    for (int g0 = r0; g0 < r1; g0 += kTG) {
-      const int ng = min(kTG, r1 - g0);
-      __syncthreads();
-      stage_rows<kVec>(xs, a.x, a.r_token, g0, ng, H);
-      __syncthreads();
-      float acc[kTG][8];
-      bank_chain<kVec>(wrow, xs, H, H, bank, ng, acc);
-#pragma unroll
-      for (int t = 0; t < kTG; ++t) {
-        if (t < ng) {
-          const float dot = fold_and_finish(acc[t], wrow, xs + t * H, H, bank == 0);
-          const float v = __fmul_rn(dot, row_ok ? S[(is_up ? I : 0) + row] : 0.0f);
-          const float u = __shfl_down_sync(0xffffffffu, v, 4);
-          if (q == 0 && row_ok) {
-            const float g = v;
-            const float den = __fadd_rn(1.0f, expf_ref(-g));
-            const float silu = __fdiv_rn(g, den);
-            a.act[(size_t)(g0 + t) * I + row] = __fmul_rn(silu, u);
-          }
-        }
-      }
-    }
+    gate_up_item<kVec>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item, a.seg_off[e],
+                       a.seg_off[e + 1], a.r_token, a.x, xs, a.act);
   }
 }
 
 template <bool kVec>
 __global__ void __launch_bounds__(kThreads) down_kernel(GemvArgs a) {
   extern __shared__ float xs[];  // [kTG][I]
-  const int H = a.H, I = a.I;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bank = lane & 3;
-  const int nblk = (H + kDNRows - 1) / kDNRows;
+  const int rows_per_item = kDNRowsPerWarp * (kThreads / 32);
+  const int nblk = (a.H + rows_per_item - 1) / rows_per_item;
   const int nitems = seg_count(a) * nblk;
-  bool bad = false;
+  bool good = true;
   for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
     const int j = item / nblk, b = item % nblk;
     const int e = a.active ? a.active[j] : j;
-    const int r0 = a.seg_off[e], r1 = a.seg_off[e + 1];
-    const int8_t *W = a.w_ptr[e] + (size_t)2 * I * H;
-    const float *S = a.s_ptr[e] + 2 * I;
-    const int row = b * kDNRows + warp * kDNRowsPerWarp + (lane >> 2);
-    const bool row_ok = row < H;
-    const int8_t *wrow = W + (size_t)(row_ok ? row : 0) * I;
-    for (int g0 = r0; g0 < r1; g0 += kTG) {
-      const int ng = min(kTG, r1 - g0);
-      __syncthreads();
-      stage_rows<kVec>(xs, a.act, nullptr, g0, ng, I);
-      __syncthreads();
-      float acc[kTG][8];
-      bank_chain<kVec>(wrow, xs, I, I, bank, ng, acc);
-#pragma unroll
-      for (int t = 0; t < kTG; ++t) {
-        if (t < ng) {
-          const float dot = fold_and_finish(acc[t], wrow, xs + t * I, I, bank == 0);
-          if (bank == 0 && row_ok) {
-            const float y = __fmul_rn(dot, S[row]);
-            bad |= !is_finite_f(y);
-            const int r = g0 + t;
-            if (a.contrib) {
-              const int tok = a.r_token[r], slot = a.r_slot[r];
-              a.contrib[((size_t)tok * a.K + slot) * H + row] = __fmul_rn(a.r_gate[r], y);
-            } else {
-              a.y[(size_t)r * H + row] = y;
-            }
-          }
-        }
-      }
+    if (a.contrib) {
+      good &= down_item<kVec>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item,
+                              a.seg_off[e], a.seg_off[e + 1], a.act, xs,
+                              [&](int r, int row, float y) {
+                                const int tok = a.r_token[r], slot = a.r_slot[r];
+                                a.contrib[((size_t)tok * a.K + slot) * a.H + row] =
+                                    __fmul_rn(a.r_gate[r], y);
+                              });
+    } else {
+      good &= down_item<kVec>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item,
+                              a.seg_off[e], a.seg_off[e + 1], a.act, xs,
+                              [&](int r, int row, float y) { a.y[(size_t)r * a.H + row] = y; });
     }
   }
-  if (bad) set_status(a.status, kStatusNonFinite);
+  if (!good) set_status(a.status, kStatusNonFinite);
 }
 
 int grid_for(int items, int sm_count) { return std::max(1, std::min(items, sm_count * 8)); }
@@ -273,7 +73,7 @@ void ensure_smem(K kernel, size_t smem) {
 }
 
 cudaError_t launch_gate_up(const GemvArgs &a, cudaStream_t s) {
-  const int nblk = (a.I + kGURows - 1) / kGURows;
+  const int nblk = (a.I + kGURowsPerWarp * 4 - 1) / (kGURowsPerWarp * 4);
   const int grid = grid_for(a.n_active_max * nblk, a.sm_count);
   const size_t smem = sizeof(float) * kTG * a.H;
   if (a.H % 8 == 0 && a.vec) {
@@ -287,7 +87,7 @@ cudaError_t launch_gate_up(const GemvArgs &a, cudaStream_t s) {
 }
 
 cudaError_t launch_down(const GemvArgs &a, cudaStream_t s) {
-  const int nblk = (a.H + kDNRows - 1) / kDNRows;
+  const int nblk = (a.H + kDNRowsPerWarp * 4 - 1) / (kDNRowsPerWarp * 4);
   const int grid = grid_for(a.n_active_max * nblk, a.sm_count);
   const size_t smem = sizeof(float) * kTG * a.I;
   if (a.I % 8 == 0 && a.vec) {

@@ -83,6 +83,46 @@ cudaError_t launch_combine(const float *contrib, const float *resid, float *out,
 cudaError_t launch_rmsnorm(const float *x, float *out, int T, int H, float eps,
                            uint32_t *status, cudaStream_t s);
 
+// Fused decode (decode_fused.cu): a whole layer, or a stack of layers with
+// RMSNorm + residual, in one cooperative launch for small T.
+constexpr int kFusedMaxRoutes = 1024;  // T * K per call
+constexpr int kFusedMaxH = 2048;       // router staging holds 8 rows of H floats
+
+struct FusedLayer {
+  const int8_t *const *w_ptr;
+  const float *const *s_ptr;
+  const void *router;
+  int router_dtype;   // RouterDtype of the stored router
+  int prefetch_ok;    // expert bases 16-byte aligned, H and I multiples of 16
+};
+
+struct FusedArgs {
+  int T, H, I, E, K, norm, route_mode;
+  int n_layers;              // layers in this launch
+  int stacked;               // 1: x <- x + MoE(RMSNorm(x)) per layer, x in `out`
+  const FusedLayer *layers;  // device array [n_layers]
+  const float *h_in;         // single layer: MoE input [T, H]
+  const float *resid;        // single layer: residual [T, H] or null
+  float *out;                // single layer: output; stacked: x, updated in place
+  float *hbuf;               // stacked: normalized input [T, H]
+  float eps;
+  float *logits;             // [T, E]
+  uint32_t *ids;             // [T, K]
+  float *gates;              // [T, K]
+  float *act;                // [T*K, I]
+  float *contrib;            // [T, K, H]
+  uint32_t *ids_out;         // optional copies of the routing (single layer)
+  float *gates_out;
+  uint32_t *tok_cnt;         // [T] arrival counters, zero between calls
+  uint32_t *bar;             // grid barrier counter (zeroed by the launcher)
+  uint32_t *status;
+  int router_async;          // routers of every layer are 16-byte aligned f32 rows
+  unsigned long long *phase_ts;  // optional [5] phase timestamps (profiling)
+};
+bool fused_decode_supported(int T, int H, int I, int E, int K);
+cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint32_t *bar,
+                                cudaStream_t s);
+
 // Seeded synthetic expert weights, bit-identical to the host-side generator.
 cudaError_t launch_synth_expert(uint64_t seed, int layer, int expert, int H, int I, int8_t *w,
                                 float *sc, cudaStream_t s);

@@ -329,6 +329,14 @@ struct moe_handle {
   uint32_t *act_amax = nullptr;
   int32_t *tile_expert = nullptr, *tile_row0 = nullptr, *tile_rows = nullptr, *n_tiles = nullptr;
   CUtensorMap map_x64{}, map_x128{}, map_a64{}, map_a128{};  // digit planes, box 64/128 rows
+  // fused decode
+  FusedLayer *d_flayers = nullptr;  // [num_layers]
+  std::vector<FusedLayer> flayers;
+  std::vector<int> layer_vec;
+  uint32_t *tok_cnt = nullptr, *fbar = nullptr;
+  std::vector<int> layer_async;            // router rows are 16-byte aligned f32
+  unsigned long long *phase_ts = nullptr;  // [5] fused-kernel phase stamps
+  bool phase_pending = false;
 };
 
 namespace {
@@ -342,7 +350,8 @@ void free_handle(moe_handle *h) {
                   h->io_in,   h->io_out,    h->io_resid,  h->ids,       h->status,  h->seg_off,
                   h->active,  h->n_active,  h->r_token,   h->r_slot,    h->r_pos,   h->xq,
                   h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
-                  h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles};
+                  h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles, h->d_flayers,
+                  h->tok_cnt, h->fbar, h->phase_ts};
   for (void *p : ptrs) cudaFree(p);
   cudaFreeHost(h->h_pin_in);
   cudaFreeHost(h->h_pin_out);
@@ -425,8 +434,37 @@ moe_status check_layer(moe_handle *h, int layer, int T) {
 bool use_tensor_path(const moe_handle *h, const LayerSlot &L, int T, const float *d_h) {
   const bool avail = h->tc_ok && L.tc_ok && ((uintptr_t)d_h & 15) == 0;
   if (h->path == MOE_PATH_TENSOR) return avail;
-  if (h->path == MOE_PATH_GEMV) return false;
+  if (h->path == MOE_PATH_GEMV || h->path == MOE_PATH_GEMV_PHASED) return false;
   return avail && T >= kTcMinTokens;
+}
+
+bool use_fused(const moe_handle *h, int T) {
+  return h->path != MOE_PATH_GEMV_PHASED &&
+         fused_decode_supported(T, h->d.hidden, h->d.intermediate, h->d.num_experts,
+                                h->d.top_k);
+}
+
+FusedArgs fused_args(moe_handle *h, int T) {
+  FusedArgs f{};
+  f.T = T;
+  f.H = h->d.hidden;
+  f.I = h->d.intermediate;
+  f.E = h->d.num_experts;
+  f.K = h->d.top_k;
+  f.norm = h->d.norm_topk_prob;
+  f.route_mode = h->route_mode;
+  f.logits = h->logits;
+  f.ids = h->ids;
+  f.gates = h->gates;
+  f.act = h->act;
+  f.contrib = h->contrib;
+  f.tok_cnt = h->tok_cnt;
+  f.status = h->status;
+  if (h->prof.on) {
+    f.phase_ts = h->phase_ts;
+    h->phase_pending = true;
+  }
+  return f;
 }
 
 // Experts on the tensor cores: digit planes of the routed inputs, gate/up
@@ -502,6 +540,30 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
     set_err(h->err, "tensor-core path unavailable for layer %d (needs the packed expert layout, "
             "H and I multiples of 16, 16-byte aligned inputs)", layer);
     return MOE_ERR_STATE;
+  }
+  if (!use_tensor_path(h, L, T, d_h) && use_fused(h, T)) {
+    FusedArgs f = fused_args(h, T);
+    f.n_layers = 1;
+    f.stacked = 0;
+    f.layers = h->d_flayers + layer;
+    f.h_in = d_h;
+    f.resid = d_resid;
+    f.out = d_out;
+    f.ids_out = d_ids;
+    f.gates_out = d_gates;
+    if (!d_ids || !d_gates) f.ids_out = nullptr;
+    const int vec = h->layer_vec[layer] && ((uintptr_t)d_h & 15) == 0;
+    f.router_async = h->layer_async[layer] && ((uintptr_t)d_h & 15) == 0;
+    cudaEvent_t p0 = h->prof.begin(s);
+    cudaError_t e = launch_fused_decode(f, vec, h->sm_count, h->fbar, s);
+    h->prof.end("fused_decode", p0, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "fused decode launch");
+    h->last_launches += 1;
+    if (d_ids && !d_gates) cudaMemcpyAsync(d_ids, h->ids, (size_t)T * h->d.top_k * 4,
+                                           cudaMemcpyDeviceToDevice, s);
+    if (d_gates && !d_ids) cudaMemcpyAsync(d_gates, h->gates, (size_t)T * h->d.top_k * 4,
+                                           cudaMemcpyDeviceToDevice, s);
+    return MOE_OK;
   }
   moe_status st = run_route(h, L, d_h, T, ids, gates, nullptr, s, true);
   if (st != MOE_OK) return st;
@@ -595,6 +657,13 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && dalloc(&h->tile_row0, h->max_tiles) == cudaSuccess;
   ok = ok && dalloc(&h->tile_rows, h->max_tiles) == cudaSuccess;
   ok = ok && dalloc(&h->n_tiles, 1) == cudaSuccess;
+  ok = ok && dalloc(&h->d_flayers, d.num_layers) == cudaSuccess;
+  ok = ok && dalloc(&h->tok_cnt, T) == cudaSuccess && dalloc(&h->fbar, 1) == cudaSuccess;
+  ok = ok && cudaMemset(h->tok_cnt, 0, T * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && dalloc(&h->phase_ts, 8) == cudaSuccess;
+  h->flayers.assign(d.num_layers, FusedLayer{});
+  h->layer_vec.assign(d.num_layers, 0);
+  h->layer_async.assign(d.num_layers, 0);
   if (!ok) {
     free_handle(h);
     delete h;
@@ -639,7 +708,7 @@ extern "C" moe_status moe_set_route_mode(moe_handle *h, int mode) {
 }
 
 extern "C" moe_status moe_set_path(moe_handle *h, int path) {
-  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_TENSOR) return MOE_ERR_INVALID;
+  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_GEMV_PHASED) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
   h->path = path;
   return MOE_OK;
@@ -685,6 +754,20 @@ extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const 
   L.tc_ok = packed && h->tc_ok &&
             tc::encode_map3d(&L.map_gu, wb, H, 2 * I, E, H, 3 * I * H, 128) &&
             tc::encode_map3d(&L.map_dn, wb + 2 * I * H, I, H, E, I, 3 * I * H, 128);
+  bool align16 = true;
+  for (int e = 0; e < E; ++e) align16 = align16 && ((uintptr_t)d_weights[e] & 15) == 0;
+  FusedLayer &F = h->flayers[layer];
+  F.w_ptr = L.d_wptr;
+  F.s_ptr = L.d_sptr;
+  F.router = d_router;
+  F.router_dtype = router_dtype;
+  F.prefetch_ok = align16 && H % 16 == 0 && I % 16 == 0;
+  h->layer_vec[layer] = vec;
+  h->layer_async[layer] = router_dtype == MOE_ROUTER_F32 && ((uintptr_t)d_router & 15) == 0 &&
+                          H % 4 == 0;
+  const cudaError_t e3 =
+      cudaMemcpy(h->d_flayers + layer, &F, sizeof(FusedLayer), cudaMemcpyHostToDevice);
+  if (e3 != cudaSuccess) return cuda_fail(h, e3, "set_layer");
   L.set = true;
   return MOE_OK;
 }
@@ -758,6 +841,26 @@ extern "C" moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_la
   DeviceGuard g(h->device);
   cudaStream_t s = pick(h, stream);
   h->last_launches = 0;
+  bool vec_all = ((uintptr_t)d_x & 15) == 0;
+  for (int l = first_layer; l < first_layer + n_layers; ++l) vec_all = vec_all && h->layer_vec[l];
+  if (h->path != MOE_PATH_TENSOR && use_fused(h, T)) {
+    FusedArgs f = fused_args(h, T);
+    f.n_layers = n_layers;
+    f.stacked = 1;
+    f.layers = h->d_flayers + first_layer;
+    f.out = d_x;
+    f.hbuf = h->hbuf;
+    f.eps = rms_eps;
+    f.router_async = 1;
+    for (int l = first_layer; l < first_layer + n_layers; ++l)
+      f.router_async = f.router_async && h->layer_async[l];
+    cudaEvent_t p0 = h->prof.begin(s);
+    cudaError_t e = launch_fused_decode(f, vec_all ? 1 : 0, h->sm_count, h->fbar, s);
+    h->prof.end("fused_decode", p0, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "fused decode launch");
+    h->last_launches += 1;
+    return MOE_OK;
+  }
   for (int l = first_layer; l < first_layer + n_layers; ++l) {
     cudaEvent_t p0 = h->prof.begin(s);
     cudaError_t e = launch_rmsnorm(d_x, h->hbuf, T, h->d.hidden, rms_eps, h->status, s);
@@ -876,6 +979,22 @@ extern "C" moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int 
   }
   h->prof.recs.clear();
   h->prof.used = 0;
+  if (h->phase_pending) {
+    // phases of the most recent profiled fused launch (first layer; the
+    // last entry runs to the end of the launch)
+    unsigned long long ts[5] = {0, 0, 0, 0, 0};
+    if (cudaMemcpy(ts, h->phase_ts, sizeof ts, cudaMemcpyDeviceToHost) == cudaSuccess) {
+      const char *names[4] = {"fused:router", "fused:gate_up", "fused:down", "fused:rest"};
+      for (int i = 0; i < 4; ++i) {
+        moe_kernel_time k{};
+        snprintf(k.name, sizeof k.name, "%s", names[i]);
+        k.launches = 1;
+        k.total_ms = ts[i + 1] > ts[i] ? (float)((ts[i + 1] - ts[i]) * 1e-6) : 0.0f;
+        acc.push_back(k);
+      }
+    }
+    h->phase_pending = false;
+  }
   const int n = std::min<int>((int)acc.size(), max_entries);
   for (int i = 0; i < n; ++i) out[i] = acc[i];
   *n_entries = (int)acc.size();

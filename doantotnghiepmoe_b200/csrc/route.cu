@@ -15,19 +15,12 @@
 // logits, probabilities, ids and gates are bit-identical to the CPU path.
 #include "common.cuh"
 #include "kernels.h"
+#include "route_core.cuh"
 
 namespace moe {
 namespace {
 
 constexpr int kRouteThreads = 256;
-
-__device__ __forceinline__ float load_w(const void *W, int dtype, size_t idx) {
-  if (dtype == kRouterBF16) {
-    const uint16_t v = reinterpret_cast<const uint16_t *>(W)[idx];
-    return __uint_as_float((uint32_t)v << 16);
-  }
-  return reinterpret_cast<const float *>(W)[idx];
-}
 
 // Small T (decode): one CTA per (token, 4 experts).  The token row and the 4
 // router rows are staged into shared memory in one shot -- every thread
@@ -192,120 +185,15 @@ __global__ void __launch_bounds__(256) route_logits_tiled_kernel(RouteArgs a) {
     }
 }
 
-// One warp per token: softmax over all E in index order, then K rounds of a
-// warp-wide argmax on (total_cmp key, lower index first).
+// One warp per token (the selection itself is route_core.cuh select_token).
 __global__ void __launch_bounds__(256) route_select_kernel(RouteArgs a) {
-  __shared__ float ex_s[8][kMaxExperts];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ SelectScratch scratch[8];
+  const int warp = threadIdx.x >> 5;
   const int t = blockIdx.x * 8 + warp;
   if (t >= a.T) return;
-  const int E = a.E, K = a.K;
-  constexpr int kPer = kMaxExperts / 32;
-  float v[kPer];
-  const float *lg = a.logits + (size_t)t * E;
-#pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int e = lane + 32 * j;
-    v[j] = e < E ? lg[e] : __int_as_float(0xff800000);  // -inf pad
-  }
-  if (a.mode == kRouteSoftmaxTopk) {
-    float mx = __int_as_float(0xff800000);
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) mx = fmaxf(mx, v[j]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E) {
-        v[j] = expf_ref(__fsub_rn(v[j], mx));
-        ex_s[warp][e] = v[j];
-      }
-    }
-    __syncwarp();
-    float sum = 0.0f;
-    if (lane == 0) {
-      sum = -0.0f;
-      for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, ex_s[warp][e]);
-    }
-    sum = __shfl_sync(0xffffffffu, sum, 0);
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E) {
-        v[j] = __fdiv_rn(v[j], sum);
-        if (a.probs) a.probs[(size_t)t * E + e] = v[j];
-      }
-    }
-  } else {
-    // partial_cmp treats -0.0 == +0.0; canonicalise zero so the total-order
-    // key ties them (and the lower index wins, as in the reference sort).
-#pragma unroll
-    for (int j = 0; j < kPer; ++j)
-      if (v[j] == 0.0f) v[j] = 0.0f;
-  }
-  // K rounds of argmax.  Key: order-preserving bits of the value, then the
-  // complement of the index so that equal values prefer the lower index.
-  __shared__ float sel_v[8][kMaxTopK];
-  __shared__ uint32_t sel_i[8][kMaxTopK];
-  uint32_t taken = 0;  // bit j set when candidate j of this lane was selected
-  for (int k = 0; k < K; ++k) {
-    unsigned long long best = 0;
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E && !(taken & (1u << j))) {
-        const unsigned long long key =
-            ((unsigned long long)total_order_u32(v[j]) << 32) | (uint32_t)(0xFFFFFFFFu - e);
-        best = key > best ? key : best;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-      best = other > best ? other : best;
-    }
-    const uint32_t e = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
-    if ((int)(e & 31) == lane) {
-      const int j = (int)(e >> 5);
-      taken |= 1u << j;
-      float val = 0.0f;
-#pragma unroll
-      for (int jj = 0; jj < kPer; ++jj)
-        if (jj == j) val = v[jj];
-      sel_v[warp][k] = val;
-      sel_i[warp][k] = e;
-    }
-    __syncwarp();
-  }
-  if (lane == 0) {
-    uint32_t *ids = a.ids + (size_t)t * K;
-    float *gates = a.gates + (size_t)t * K;
-    if (a.mode == kRouteSoftmaxTopk) {
-      float norm = 1.0f;
-      if (a.norm_topk_prob) {
-        norm = -0.0f;
-        for (int k = 0; k < K; ++k) norm = __fadd_rn(norm, sel_v[warp][k]);
-      }
-      for (int k = 0; k < K; ++k) {
-        ids[k] = sel_i[warp][k];
-        gates[k] = __fdiv_rn(sel_v[warp][k], norm);
-        if (sel_i[warp][k] >= (uint32_t)E) set_status(a.status, kStatusBadRoute);
-      }
-    } else {
-      const float mx = sel_v[warp][0];
-      float total = -0.0f;
-      float ex[kMaxTopK];
-      for (int k = 0; k < K; ++k) {
-        ex[k] = expf_ref(__fsub_rn(sel_v[warp][k], mx));
-        total = __fadd_rn(total, ex[k]);
-      }
-      for (int k = 0; k < K; ++k) {
-        ids[k] = sel_i[warp][k];
-        gates[k] = __fdiv_rn(ex[k], total);
-      }
-    }
-  }
+  select_token(a.logits + (size_t)t * a.E, a.E, a.K, a.norm_topk_prob, a.mode,
+               a.ids + (size_t)t * a.K, a.gates + (size_t)t * a.K,
+               a.probs ? a.probs + (size_t)t * a.E : nullptr, scratch[warp], a.status);
 }
 
 // Single-CTA stable counting sort of the T*K routes by expert.

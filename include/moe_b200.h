@@ -101,9 +101,11 @@ enum {
 
 /* Expert GEMM back-end for a layer call. */
 enum {
-  MOE_PATH_AUTO = 0,   /* GEMV for small T, tensor cores for large T */
-  MOE_PATH_GEMV = 1,   /* exact-order INT8 GEMV (bit-identical to the CPU path) */
-  MOE_PATH_TENSOR = 2  /* tcgen05 grouped GEMM (within the 1e-3 tolerance) */
+  MOE_PATH_AUTO = 0,        /* GEMV for small T, tensor cores for large T */
+  MOE_PATH_GEMV = 1,        /* exact-order INT8 GEMV (bit-identical to the CPU path); for
+                               small T the whole layer runs as one fused launch */
+  MOE_PATH_TENSOR = 2,      /* tcgen05 grouped GEMM (within the 1e-3 tolerance) */
+  MOE_PATH_GEMV_PHASED = 3  /* exact-order GEMV, one launch per phase (no fusion) */
 };
 
 moe_status moe_create(int device, const moe_dims *dims, moe_handle **out);
