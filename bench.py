@@ -48,8 +48,8 @@ CONFIGS = {
                workload="olmoe_16layer_decode_T8"),
     "c3": dict(H=2048, I=768, E=128, K=8, norm=True, T=64, stack=48,
                workload="qwen3_48layer_decode_T64"),
-    "c4": dict(H=2048, I=768, E=128, K=8, norm=True, T=4096, stack=1,
-               workload="qwen3_layer_prefill_T4096"),
+    "c4": dict(H=2048, I=768, E=128, K=8, norm=True, T=4096, stack=1, zipf=True,
+               strong=True, workload="qwen3_layer_prefill_T4096_zipf1.1"),
 }
 SEED = 20261201
 
@@ -218,13 +218,15 @@ def main():
     import torch
     import torch.distributed as dist
     import doantotnghiepmoe_b200 as M
-    from doantotnghiepmoe_b200 import _lib
+    from doantotnghiepmoe_b200 import synthetic
 
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+    if world > 1:
+        return run_ep(args, cfg, rank, world, local)
     H, I, E, K, T = cfg["H"], cfg["I"], cfg["E"], cfg["K"], cfg["T"]
     n_stack = cfg["stack"]
     layer_bytes = E * (3 * I * H + 4 * (2 * I + H))
@@ -243,13 +245,12 @@ def main():
             sc = torch.empty((E, 2 * I + H), dtype=torch.float32, device="cuda")
             for e in range(E):
                 M.synth_expert(SEED, l, e, H, I, ex[e], sc[e], stream=stream)
-            rt = torch.from_numpy(M.synth_normal(SEED, M.layer.KIND_ROUTER, l, E * H, 0.02)
-                                  .reshape(E, H)).cuda()
+            rt = torch.from_numpy(synthetic.router(SEED, l, E, H, cfg.get("zipf", False))).cuda()
             eng.set_layer_packed(l, ex, sc, rt)
             keep.append((ex, sc, rt))
         n_inputs = n_layers if n_stack == 1 else 2
-        hs = [torch.from_numpy(M.synth_normal(SEED + rank, M.layer.KIND_HIDDEN, i, T * H, 1.0)
-                               .reshape(T, H)).cuda() for i in range(n_inputs)]
+        hs = [torch.from_numpy(synthetic.hidden(SEED, i, T, H, cfg.get("zipf", False))).cuda()
+              for i in range(n_inputs)]
         outs = [torch.empty((T, H), dtype=torch.float32, device="cuda") for _ in range(2)]
         ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
     stream.synchronize()
@@ -270,6 +271,7 @@ def main():
             stream.synchronize()
             Ds.append(len(np.unique(ids.cpu().numpy())))
     D = float(np.mean(Ds))
+    shares = np.bincount(ids.cpu().numpy().ravel(), minlength=E) / ids.numel()
     eng.sync_status(stream)
 
     with torch.cuda.stream(stream):
@@ -374,8 +376,11 @@ def main():
                            "distinct_experts_per_layer": D,
                            "l2": f"weights rotate over {n_layers} layers "
                                  f"({layer_bytes * n_layers / 1e9:.1f} GB) > 126 MB L2",
-                           "parallelism": f"replicas{world}" if world > 1 else "single",
-                           "path": args.path},
+                           "parallelism": "single",
+                           "path": args.path,
+                           "expert_share_top5": [round(float(x), 4) for x in
+                                                 np.sort(shares)[::-1][:5]],
+                           "expert_share_max_over_mean": round(float(shares.max() * E), 2)},
                 "layer_hbm_gbs": layer_gbs,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches, "clocks": clk}
@@ -383,6 +388,134 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_ep(args, cfg, rank, world, local):
+    """Expert parallelism over `world` GPUs (one process each): experts are
+    split evenly (balanced by expected load), every rank routes its own
+    tokens; NCCL dispatch/combine inside the library.  Tokens per rank: the
+    config's T (weak scaling), or T / world for the strong-scaling config."""
+    import torch
+    import torch.distributed as dist
+
+    import doantotnghiepmoe_b200 as M
+    from doantotnghiepmoe_b200 import placement, synthetic
+
+    H, I, E, K = cfg["H"], cfg["I"], cfg["E"], cfg["K"]
+    strong = cfg.get("strong", False)
+    T = cfg["T"] // world if strong else cfg["T"]
+    zipf = cfg.get("zipf", False)
+    if zipf:
+        w, _ = synthetic.zipf_weights(E, SEED)
+        owner = placement.balanced_owner(np.minimum(w, 1.0 / K), world)
+    else:
+        owner = placement.contiguous_owner(E, world)
+    loc = placement.local_experts(owner, rank)
+    EL = len(loc)
+    layer_bytes_local = EL * (3 * I * H + 4 * (2 * I + H))
+    n_layers = max(2, int(np.ceil(3 * 126e6 / max(1, layer_bytes_local))) + 1)
+    eng = M.MoeLayerEngine(M.MoeConfig(H, I, E, K, cfg["norm"], T, n_layers), device=local)
+    stream = torch.cuda.Stream()
+    eng.set_stream(stream)
+    uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid = torch.tensor(list(M.layer.ep_unique_id()), dtype=torch.uint8, device="cuda")
+    dist.broadcast(uid, 0)
+    eng.ep_init(rank, world, bytes(uid.cpu().tolist()), owner)
+    keep = []
+    with torch.cuda.stream(stream):
+        for l in range(n_layers):
+            ex = torch.empty((max(EL, 1), 3 * I * H), dtype=torch.int8, device="cuda")
+            sc = torch.empty((max(EL, 1), 2 * I + H), dtype=torch.float32, device="cuda")
+            for j, e in enumerate(loc):
+                M.synth_expert(SEED, l, int(e), H, I, ex[j], sc[j], stream=stream)
+            rt = torch.from_numpy(synthetic.router(SEED, l, E, H, zipf)).cuda()
+            eng.ep_set_layer(l, ex, sc, rt)
+            keep.append((ex, sc, rt))
+        hs = [torch.from_numpy(synthetic.hidden(SEED, 1000 * rank + i, T, H, zipf)).cuda()
+              for i in range(2)]
+        outs = [torch.empty((T, H), dtype=torch.float32, device="cuda") for _ in range(2)]
+    stream.synchronize()
+
+    def step(i):
+        eng.ep_forward(i % n_layers, hs[i % 2], outs[i % 2], stream=stream)
+
+    for i in range(args.warmup):
+        step(i)
+    stream.synchronize()
+    eng.sync_status(stream)
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    eng.profile_read()
+    eng.profile(True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+        launches += eng.last_launch_count()
+    ev1.record(stream)
+    ev1.synchronize()
+    eng.profile(False)
+    prof = eng.profile_read()
+    dist.barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    tokens = T * world
+    value = tokens / (ms_max / 1e3)
+    # e2e: host hidden states in (pinned), layer, host outputs back, per step
+    h_host = [hs[i].cpu().pin_memory() for i in range(2)]
+    o_host = [torch.empty((T, H), dtype=torch.float32).pin_memory() for _ in range(2)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            hs[i % 2].copy_(h_host[i % 2], non_blocking=True)
+            step(i)
+            o_host[i % 2].copy_(outs[i % 2], non_blocking=True)
+    e1.record(stream)
+    e1.synchronize()
+    e_t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device="cuda")
+    dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    e2e = {"value": tokens / (float(e_t.item()) / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4}
+    eng.sync_status(stream)
+    hbm_peak, _, peak_kind = measured_peaks()
+    top = max(prof.items(), key=lambda kv: kv[1][1]) if prof else ("none", (1, 0.0))
+    kname, (klaunch, kms) = top
+    tot = max(1e-9, sum(v[1] for v in prof.values()))
+    # local weight bytes streamed per step (every local expert is active)
+    local_gbs = layer_bytes_local / (ms_max / 1e3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "ep_layer", "achieved": local_gbs, "peak": hbm_peak,
+                "unit": "GB/s", "frac": local_gbs / hbm_peak, "traffic": None,
+                "peak_kind": peak_kind, "alg_bytes_per_launch": layer_bytes_local,
+                "mean_launch_ms": ms_max, "top_kernel": kname,
+                "kernel_share": {k: round(v[1] / tot, 4) for k, v in prof.items()}}
+    if rank == 0:
+        line = {"metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": ms_max, "higher_is_better": True,
+                "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic",
+                "config": {"workload": cfg["workload"], "hidden": H, "intermediate": I,
+                           "experts": E, "top_k": K, "norm_topk_prob": cfg["norm"],
+                           "tokens_per_rank": T, "experts_per_rank": EL,
+                           "parallelism": f"ep{world}",
+                           "placement": "balanced" if zipf else "contiguous",
+                           "l2": f"weights rotate over {n_layers} layers > 126 MB L2"},
+                "roofline": roofline, "cpu_baseline": None, "e2e": e2e,
+                "gpu_launches": launches, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    eng.ep_finalize()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -74,6 +74,11 @@ SIGNATURES = {
     "moe_synth_normal_host": (I32, [U64, U32, U32, SZ, F32, P]),
     "moe_layer_forward_noalloc": (I32, [ctypes.POINTER(MoeDims), P, P, P, I32, P, P, P, I32,
                                         P, ctypes.c_char_p, SZ]),
+    "moe_ep_unique_id": (I32, [P]),
+    "moe_ep_init": (I32, [P, I32, I32, P, P]),
+    "moe_ep_set_layer": (I32, [P, I32, P, P, P, I32]),
+    "moe_ep_layer_forward": (I32, [P, I32, P, P, P, I32, P]),
+    "moe_ep_finalize": (I32, [P]),
 }
 
 _lib = None

@@ -25,7 +25,7 @@
 // kStatusTimeout, stops issuing work, waits (bounded) for its in-flight
 // copies, frees its TMEM and returns.
 //
-// No TMA multicast is used anywhere.
+// Every tensor load targets this CTA's own shared memory only.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

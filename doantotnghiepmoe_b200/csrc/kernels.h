@@ -123,6 +123,25 @@ bool fused_decode_supported(int T, int H, int I, int E, int K);
 cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint32_t *bar,
                                 cudaStream_t s);
 
+// Expert parallelism (ep.cu): one route on the wire = two int8 digit planes
+// of its token row + {s1, s2, gate, destination-local expert id}.
+__host__ __device__ inline size_t ep_row_bytes(int H) { return (size_t)2 * H + 16; }
+cudaError_t launch_ep_dest(const uint32_t *ids, const int32_t *owner, int R, int E,
+                           uint32_t *dest, uint32_t *status, cudaStream_t s);
+cudaError_t launch_ep_pack(const float *x, const int32_t *r_token, const int32_t *r_slot,
+                           const float *r_gate, const uint32_t *ids, const int32_t *local_of,
+                           int R, int K, int H, uint8_t *send, cudaStream_t s);
+cudaError_t launch_ep_unpack_meta(const uint8_t *recv, int R, int H, int E_local,
+                                  uint32_t *ids_local, float *gates, uint32_t *status,
+                                  cudaStream_t s);
+cudaError_t launch_ep_unpack_digits(const uint8_t *recv, const int32_t *src, int R, int H,
+                                    int8_t *xq, size_t plane, float *s1, float *s2,
+                                    uint32_t *amax_reset, cudaStream_t s);
+cudaError_t launch_seg_counts(const int32_t *seg, int n, int32_t *cnt, cudaStream_t s);
+cudaError_t launch_ep_gather_combine(const float *ret, const int32_t *pos, const float *resid,
+                                     float *out, int T, int K, int H, uint32_t *status,
+                                     cudaStream_t s);
+
 // Seeded synthetic expert weights, bit-identical to the host-side generator.
 cudaError_t launch_synth_expert(uint64_t seed, int layer, int expert, int H, int I, int8_t *w,
                                 float *sc, cudaStream_t s);

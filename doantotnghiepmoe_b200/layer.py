@@ -135,6 +135,29 @@ class MoeLayerEngine:
     def last_launch_count(self) -> int:
         return int(lib().moe_last_launch_count(self._h))
 
+    # -- expert parallelism (one process per GPU) -------------------------
+    def ep_init(self, rank: int, nranks: int, unique_id: bytes, owner):
+        owner = np.ascontiguousarray(owner, np.int32)
+        assert owner.size == self.cfg.num_experts
+        uid = (ctypes.c_ubyte * 128).from_buffer_copy(unique_id)
+        self._check(lib().moe_ep_init(self._h, rank, nranks, uid, owner.ctypes.data))
+
+    def ep_set_layer(self, layer: int, experts_local, scales_local, router):
+        """experts_local / scales_local: this rank's experts packed in ascending
+        global id order; router: the full [E, H] router."""
+        import torch
+        dtype = MOE_ROUTER_F32 if router.dtype == torch.float32 else MOE_ROUTER_BF16
+        self._keep[("ep", layer)] = (experts_local, scales_local, router)
+        self._check(lib().moe_ep_set_layer(self._h, layer, _ptr(experts_local),
+                                           _ptr(scales_local), router.data_ptr(), dtype))
+
+    def ep_forward(self, layer: int, h, out, resid=None, stream=None):
+        self._check(lib().moe_ep_layer_forward(self._h, layer, h.data_ptr(), _ptr(resid),
+                                               out.data_ptr(), h.shape[0], _stream(stream)))
+
+    def ep_finalize(self):
+        self._check(lib().moe_ep_finalize(self._h))
+
     def profile(self, enable: bool):
         self._check(lib().moe_profile_enable(self._h, int(enable)))
 
@@ -157,6 +180,14 @@ def synth_normal(seed: int, kind: int, layer: int, n: int, std: float) -> np.nda
 
 
 KIND_ROUTER, KIND_HIDDEN = 3, 4
+
+
+def ep_unique_id() -> bytes:
+    buf = (ctypes.c_ubyte * 128)()
+    st = lib().moe_ep_unique_id(buf)
+    if st != MOE_OK:
+        raise MoeError(st, "moe_ep_unique_id failed (NCCL unavailable?)")
+    return bytes(buf)
 
 
 def synth_expert(seed: int, layer: int, expert: int, H: int, I: int, w, s, stream=None):

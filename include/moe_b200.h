@@ -188,6 +188,30 @@ moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8_t *d_exper
                                      size_t err_len);
 
 /* ------------------------------------------------------------------------
+ * 2b. Expert parallelism (no counterpart in the reference, which runs on one
+ *     device, src/gpu.rs:457-460).  One process per GPU; experts are owned by
+ *     ranks, tokens stay on the rank that routes them.  Dispatch and combine
+ *     are NCCL point-to-point exchanges inside moe_ep_layer_forward; results
+ *     equal the single-GPU tensor-core path bit for bit.
+ * ---------------------------------------------------------------------- */
+/* 128-byte NCCL unique id; rank 0 creates it and the host shares it. */
+moe_status moe_ep_unique_id(unsigned char id_out[128]);
+/* Join the expert-parallel group.  expert_owner[e] = rank that holds expert
+ * e (E entries, every rank the same table).  Must precede moe_ep_set_layer. */
+moe_status moe_ep_init(moe_handle *h, int rank, int nranks, const unsigned char id[128],
+                       const int32_t *expert_owner);
+/* This rank's experts of a layer, packed in ascending global id order
+ * (3*I*H int8 and 2*I+H f32 each), plus the full [E,H] router. */
+moe_status moe_ep_set_layer(moe_handle *h, int layer, const int8_t *d_experts_local,
+                            const float *d_scales_local, const void *d_router, int router_dtype);
+/* One MoE layer over this rank's T_local tokens (device [T_local,H]); every
+ * rank must call it with the same layer, in the same order. */
+moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float *d_h, const float *d_resid,
+                                float *d_out, int T_local, void *stream);
+/* Leave the group (destroys the communicator; also done by moe_destroy). */
+moe_status moe_ep_finalize(moe_handle *h);
+
+/* ------------------------------------------------------------------------
  * 3. Utilities for tests and benchmarks (no reference counterpart).
  * ---------------------------------------------------------------------- */
 /* Per-kernel device timing: when enabled, every kernel the handle launches is
