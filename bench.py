@@ -206,7 +206,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tensor"])
+    ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tensor", "gemv_fused",
+                                                          "gemv_stream"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
@@ -237,7 +238,8 @@ def main():
     eng = M.MoeLayerEngine(M.MoeConfig(H, I, E, K, cfg["norm"], T, n_layers), device=local)
     stream = torch.cuda.Stream()
     eng.set_stream(stream)
-    eng.set_path({"auto": 0, "gemv": 1, "tensor": 2}[args.path])
+    eng.set_path({"auto": 0, "gemv": 1, "tensor": 2, "gemv_fused": 4,
+                  "gemv_stream": 5}[args.path])
     keep = []
     with torch.cuda.stream(stream):
         for l in range(n_layers):
@@ -333,6 +335,7 @@ def main():
     hbm_peak, _, peak_kind = measured_peaks()
     alg = algorithmic_bytes(cfg, D, T)
     alg["fused_decode"] = alg["layer"] * n_stack  # one launch runs the whole step
+    alg["stream_decode"] = alg["layer"] * n_stack
     phases = {k: v for k, v in prof.items() if ":" in k}
     prof = {k: v for k, v in prof.items() if ":" not in k}
     top = max(prof.items(), key=lambda kv: kv[1][1]) if prof else ("none", (1, 0.0))

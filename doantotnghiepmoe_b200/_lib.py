@@ -26,6 +26,8 @@ STATUS_NAMES = {0: "OK", 1: "INVALID", 2: "NONFINITE", 3: "CUDA", 4: "NCCL", 5: 
 MOE_ROUTER_F32, MOE_ROUTER_BF16 = 0, 1
 MOE_ROUTE_SOFTMAX_TOPK, MOE_ROUTE_TOPK_SOFTMAX = 0, 1
 MOE_PATH_AUTO, MOE_PATH_GEMV, MOE_PATH_TENSOR, MOE_PATH_GEMV_PHASED = 0, 1, 2, 3
+MOE_PATH_GEMV_FUSED = 4
+MOE_PATH_GEMV_STREAM = 5
 
 # Every symbol the header declares, with (restype, argtypes).
 P, SZ, I32, U32, U64, F32 = (ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32,

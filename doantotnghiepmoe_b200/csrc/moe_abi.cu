@@ -410,9 +410,12 @@ struct moe_handle {
   std::vector<FusedLayer> flayers;
   std::vector<int> layer_vec;
   uint32_t *tok_cnt = nullptr, *fbar = nullptr;
+  uint32_t *sctr = nullptr;                // streaming decode: 2 counter sets
+  uint32_t sctr_parity = 0;                // set used by the next launch
   std::vector<int> layer_async;            // router rows are 16-byte aligned f32
-  unsigned long long *phase_ts = nullptr;  // [5] fused-kernel phase stamps
+  unsigned long long *phase_ts = nullptr;  // [8] single-launch kernel phase stamps
   bool phase_pending = false;
+  int phase_kind = 0;                      // 0: register-prefetch kernel, 1: streaming
   EpState ep;
 };
 
@@ -442,7 +445,7 @@ void free_handle(moe_handle *h) {
                   h->active,  h->n_active,  h->r_token,   h->r_slot,    h->r_pos,   h->xq,
                   h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
                   h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles, h->d_flayers,
-                  h->tok_cnt, h->fbar, h->phase_ts};
+                  h->tok_cnt, h->fbar, h->phase_ts, h->sctr};
   for (void *p : ptrs) cudaFree(p);
   cudaFreeHost(h->h_pin_in);
   cudaFreeHost(h->h_pin_out);
@@ -525,7 +528,9 @@ moe_status check_layer(moe_handle *h, int layer, int T) {
 bool use_tensor_path(const moe_handle *h, const LayerSlot &L, int T, const float *d_h) {
   const bool avail = h->tc_ok && L.tc_ok && ((uintptr_t)d_h & 15) == 0;
   if (h->path == MOE_PATH_TENSOR) return avail;
-  if (h->path == MOE_PATH_GEMV || h->path == MOE_PATH_GEMV_PHASED) return false;
+  if (h->path == MOE_PATH_GEMV || h->path == MOE_PATH_GEMV_PHASED ||
+      h->path == MOE_PATH_GEMV_FUSED || h->path == MOE_PATH_GEMV_STREAM)
+    return false;
   return avail && T >= kTcMinTokens;
 }
 
@@ -533,6 +538,29 @@ bool use_fused(const moe_handle *h, int T) {
   return h->path != MOE_PATH_GEMV_PHASED &&
          fused_decode_supported(T, h->d.hidden, h->d.intermediate, h->d.num_experts,
                                 h->d.top_k);
+}
+
+// The streaming decode kernel: every layer's experts 16-byte aligned (bulk
+// copies), f32 routers in 16-byte rows or bf16, aligned f32 activations.
+bool use_stream(const moe_handle *h, int T, int first_layer, int n_layers, const void *d_x) {
+  if (h->path != MOE_PATH_GEMV_STREAM) return false;
+  if (((uintptr_t)d_x & 15) != 0) return false;
+  if (!stream_decode_supported(T, h->d.hidden, h->d.intermediate, h->d.num_experts, h->d.top_k))
+    return false;
+  for (int l = first_layer; l < first_layer + n_layers; ++l)
+    if (!h->flayers[l].prefetch_ok) return false;
+  return true;
+}
+
+// Launch the streaming decode kernel with the handle's next counter set.
+cudaError_t launch_stream(moe_handle *h, FusedArgs f, cudaStream_t s) {
+  if (f.phase_ts) cudaMemsetAsync(f.phase_ts, 0, 16 * sizeof(unsigned long long), s);
+  f.ctr = h->sctr + (size_t)h->sctr_parity * kStreamCtrWords;
+  f.ctr_next = h->sctr + (size_t)(h->sctr_parity ^ 1u) * kStreamCtrWords;
+  const cudaError_t e = launch_stream_decode(f, h->sm_count, s);
+  if (e == cudaSuccess) h->sctr_parity ^= 1u;
+  else fprintf(stderr, "moe_b200: %s: %s\n", cudaGetErrorString(e), stream_decode_diag());
+  return e;
 }
 
 FusedArgs fused_args(moe_handle *h, int T) {
@@ -645,9 +673,13 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
     if (!d_ids || !d_gates) f.ids_out = nullptr;
     const int vec = h->layer_vec[layer] && ((uintptr_t)d_h & 15) == 0;
     f.router_async = h->layer_async[layer] && ((uintptr_t)d_h & 15) == 0;
+    const bool stream = use_stream(h, T, layer, 1, d_h) &&
+                        (!d_resid || ((uintptr_t)d_resid & 15) == 0);
+    h->phase_kind = stream ? 1 : 0;
     cudaEvent_t p0 = h->prof.begin(s);
-    cudaError_t e = launch_fused_decode(f, vec, h->sm_count, h->fbar, s);
-    h->prof.end("fused_decode", p0, s);
+    cudaError_t e = stream ? launch_stream(h, f, s)
+                           : launch_fused_decode(f, vec, h->sm_count, h->fbar, s);
+    h->prof.end(stream ? "stream_decode" : "fused_decode", p0, s);
     if (e != cudaSuccess) return cuda_fail(h, e, "fused decode launch");
     h->last_launches += 1;
     if (d_ids && !d_gates) cudaMemcpyAsync(d_ids, h->ids, (size_t)T * h->d.top_k * 4,
@@ -751,7 +783,9 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && dalloc(&h->d_flayers, d.num_layers) == cudaSuccess;
   ok = ok && dalloc(&h->tok_cnt, T) == cudaSuccess && dalloc(&h->fbar, 1) == cudaSuccess;
   ok = ok && cudaMemset(h->tok_cnt, 0, T * sizeof(uint32_t)) == cudaSuccess;
-  ok = ok && dalloc(&h->phase_ts, 8) == cudaSuccess;
+  ok = ok && dalloc(&h->phase_ts, 16) == cudaSuccess;
+  ok = ok && dalloc(&h->sctr, 2 * kStreamCtrWords) == cudaSuccess;
+  ok = ok && cudaMemset(h->sctr, 0, 2 * kStreamCtrWords * sizeof(uint32_t)) == cudaSuccess;
   h->flayers.assign(d.num_layers, FusedLayer{});
   h->layer_vec.assign(d.num_layers, 0);
   h->layer_async.assign(d.num_layers, 0);
@@ -799,7 +833,7 @@ extern "C" moe_status moe_set_route_mode(moe_handle *h, int mode) {
 }
 
 extern "C" moe_status moe_set_path(moe_handle *h, int path) {
-  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_GEMV_PHASED) return MOE_ERR_INVALID;
+  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_GEMV_STREAM) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
   h->path = path;
   return MOE_OK;
@@ -945,9 +979,12 @@ extern "C" moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_la
     f.router_async = 1;
     for (int l = first_layer; l < first_layer + n_layers; ++l)
       f.router_async = f.router_async && h->layer_async[l];
+    const bool stream = use_stream(h, T, first_layer, n_layers, d_x);
+    h->phase_kind = stream ? 1 : 0;
     cudaEvent_t p0 = h->prof.begin(s);
-    cudaError_t e = launch_fused_decode(f, vec_all ? 1 : 0, h->sm_count, h->fbar, s);
-    h->prof.end("fused_decode", p0, s);
+    cudaError_t e = stream ? launch_stream(h, f, s)
+                           : launch_fused_decode(f, vec_all ? 1 : 0, h->sm_count, h->fbar, s);
+    h->prof.end(stream ? "stream_decode" : "fused_decode", p0, s);
     if (e != cudaSuccess) return cuda_fail(h, e, "fused decode launch");
     h->last_launches += 1;
     return MOE_OK;
@@ -1073,16 +1110,39 @@ extern "C" moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int 
   if (h->phase_pending) {
     // phases of the most recent profiled fused launch (first layer; the
     // last entry runs to the end of the launch)
-    unsigned long long ts[5] = {0, 0, 0, 0, 0};
+    unsigned long long ts[16] = {};
     if (cudaMemcpy(ts, h->phase_ts, sizeof ts, cudaMemcpyDeviceToHost) == cudaSuccess) {
-      const char *names[4] = {"fused:router", "fused:gate_up", "fused:down", "fused:rest"};
-      for (int i = 0; i < 4; ++i) {
+      static const char *names_f[4] = {"fused:router", "fused:gate_up", "fused:down",
+                                       "fused:rest"};
+      static const char *names_s[6] = {"fused:route_task", "fused:route_wait", "fused:select",
+                                       "fused:gate_up",    "fused:down",       "fused:rest"};
+      const char *const *names = h->phase_kind ? names_s : names_f;
+      const int nph = h->phase_kind ? 6 : 4;
+      for (int i = 0; i < nph; ++i) {
         moe_kernel_time k{};
         snprintf(k.name, sizeof k.name, "%s", names[i]);
         k.launches = 1;
         k.total_ms = ts[i + 1] > ts[i] ? (float)((ts[i + 1] - ts[i]) * 1e-6) : 0.0f;
         acc.push_back(k);
       }
+      // selection alone (streaming kernel): stamp 7 follows the top-k
+      if (h->phase_kind && ts[7] > ts[2]) {
+        moe_kernel_time k{};
+        snprintf(k.name, sizeof k.name, "fused:select_topk");
+        k.launches = 1;
+        k.total_ms = (float)((ts[7] - ts[2]) * 1e-6);
+        acc.push_back(k);
+      }
+      // second layer of a stack (streaming kernel), stamps 8..13
+      if (h->phase_kind && ts[8] != 0)
+        for (int i = 0; i < 5; ++i) {
+          moe_kernel_time k{};
+          snprintf(k.name, sizeof k.name, "%s1", names[i]);
+          k.launches = 1;
+          k.total_ms =
+              ts[9 + i] > ts[8 + i] ? (float)((ts[9 + i] - ts[8 + i]) * 1e-6) : 0.0f;
+          acc.push_back(k);
+        }
     }
     h->phase_pending = false;
   }

@@ -27,11 +27,13 @@ struct SelectScratch {
 // raw scores (kRouteTopkSoftmax), then K rounds of a warp-wide argmax on
 // (f32::total_cmp key, lower index first).  Called by all 32 lanes of a warp.
 // lg may live in global memory written by other CTAs: it is read through L2.
-__device__ __forceinline__ void select_token(const float *lg, int E, int K, int norm_topk_prob,
-                                             int mode, uint32_t *ids, float *gates, float *probs,
-                                             SelectScratch &sc, uint32_t *status) {
+// kPer = candidates per lane (E <= 32 * kPer); select_token below picks it.
+template <int kPer>
+__device__ __forceinline__ void select_token_t(const float *lg, int E, int K, int norm_topk_prob,
+                                               int mode, uint32_t *ids, float *gates,
+                                               float *probs, SelectScratch &sc,
+                                               uint32_t *status) {
   const int lane = threadIdx.x & 31;
-  constexpr int kPer = kMaxExperts / 32;
   float v[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
@@ -55,8 +57,17 @@ __device__ __forceinline__ void select_token(const float *lg, int E, int K, int 
     __syncwarp();
     float sum = 0.0f;
     if (lane == 0) {
+      // sequential in index order; loads batched ahead of the dependent adds
       sum = -0.0f;
-      for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, sc.ex[e]);
+      int e = 0;
+      for (; e + 8 <= E; e += 8) {
+        float v8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v8[j] = sc.ex[e + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sum = __fadd_rn(sum, v8[j]);
+      }
+      for (; e < E; ++e) sum = __fadd_rn(sum, sc.ex[e]);
     }
     sum = __shfl_sync(0xffffffffu, sum, 0);
 #pragma unroll
@@ -74,24 +85,28 @@ __device__ __forceinline__ void select_token(const float *lg, int E, int K, int 
     for (int j = 0; j < kPer; ++j)
       if (v[j] == 0.0f) v[j] = 0.0f;
   }
+  // Each round: every lane takes its best remaining candidate (its candidates
+  // run in ascending expert order, so a strict '>' keeps the lower index on a
+  // tie), one warp max-reduction finds the winning key, one min-reduction
+  // picks the lowest expert index among the lanes holding it.
   uint32_t taken = 0;  // bit j set when candidate j of this lane was selected
   for (int k = 0; k < K; ++k) {
-    unsigned long long best = 0;
+    uint32_t bk = 0;
+    int bj = -1;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
       const int e = lane + 32 * j;
       if (e < E && !(taken & (1u << j))) {
-        const unsigned long long key =
-            ((unsigned long long)total_order_u32(v[j]) << 32) | (uint32_t)(0xFFFFFFFFu - e);
-        best = key > best ? key : best;
+        const uint32_t key = total_order_u32(v[j]);
+        if (bj < 0 || key > bk) {
+          bk = key;
+          bj = j;
+        }
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-      best = other > best ? other : best;
-    }
-    const uint32_t e = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
+    const uint32_t mx = __reduce_max_sync(0xffffffffu, bj >= 0 ? bk : 0u);
+    const uint32_t cand = (bj >= 0 && bk == mx) ? (uint32_t)(lane + 32 * bj) : 0xFFFFFFFFu;
+    const uint32_t e = __reduce_min_sync(0xffffffffu, cand);
     if ((int)(e & 31) == lane) {
       const int j = (int)(e >> 5);
       taken |= 1u << j;
@@ -131,6 +146,18 @@ __device__ __forceinline__ void select_token(const float *lg, int E, int K, int 
     }
   }
   __syncwarp();
+}
+
+__device__ __forceinline__ void select_token(const float *lg, int E, int K, int norm_topk_prob,
+                                             int mode, uint32_t *ids, float *gates, float *probs,
+                                             SelectScratch &sc, uint32_t *status) {
+  if (E <= 64)
+    select_token_t<2>(lg, E, K, norm_topk_prob, mode, ids, gates, probs, sc, status);
+  else if (E <= 128)
+    select_token_t<4>(lg, E, K, norm_topk_prob, mode, ids, gates, probs, sc, status);
+  else
+    select_token_t<kMaxExperts / 32>(lg, E, K, norm_topk_prob, mode, ids, gates, probs, sc,
+                                     status);
 }
 
 }  // namespace moe

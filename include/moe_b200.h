@@ -103,9 +103,14 @@ enum {
 enum {
   MOE_PATH_AUTO = 0,        /* GEMV for small T, tensor cores for large T */
   MOE_PATH_GEMV = 1,        /* exact-order INT8 GEMV (bit-identical to the CPU path); for
-                               small T the whole layer runs as one fused launch */
+                               small T the whole layer runs as one cooperative launch */
   MOE_PATH_TENSOR = 2,      /* tcgen05 grouped GEMM (within the 1e-3 tolerance) */
-  MOE_PATH_GEMV_PHASED = 3  /* exact-order GEMV, one launch per phase (no fusion) */
+  MOE_PATH_GEMV_PHASED = 3, /* exact-order GEMV, one launch per phase (no fusion) */
+  MOE_PATH_GEMV_FUSED = 4,  /* same as MOE_PATH_GEMV: the register-prefetch single launch */
+  MOE_PATH_GEMV_STREAM = 5  /* exact-order GEMV, one launch, weights staged through a
+                               shared-memory ring with cp.async (needs 16-byte aligned
+                               experts, H and I multiples of 32); falls back to the
+                               register-prefetch launch otherwise */
 };
 
 moe_status moe_create(int device, const moe_dims *dims, moe_handle **out);

@@ -1,6 +1,8 @@
-"""GPU tests of the fused decode launch (one cooperative kernel per layer or
-per stack).  Same arithmetic as the phased kernels, so everything is compared
-bit for bit: against the oracle and against MOE_PATH_GEMV_PHASED."""
+"""GPU tests of the single-launch decode kernels: the register-prefetch kernel
+(MOE_PATH_GEMV, the default) and the streaming kernel (weights staged through
+a shared-memory ring, MOE_PATH_GEMV_STREAM).  Both use the phased kernels' arithmetic, so
+everything is compared bit for bit: against the oracle and against
+MOE_PATH_GEMV_PHASED."""
 import numpy as np
 import pytest
 
@@ -12,6 +14,8 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 import doantotnghiepmoe_b200 as M  # noqa: E402
 from doantotnghiepmoe_b200 import _lib  # noqa: E402
+
+KERNELS = [(_lib.MOE_PATH_GEMV_STREAM, "stream_decode"), (_lib.MOE_PATH_GEMV, "fused_decode")]
 
 
 def bits(a):
@@ -33,49 +37,126 @@ def layer_out(eng, h, path, resid=None):
     return out.cpu().numpy(), ids.cpu().numpy().astype(np.uint32), gates.cpu().numpy(), prof
 
 
+def check_layer(lw, h, resid, path, kernel, cfg):
+    ref = O.layer_forward(lw, h, resid=resid)
+    eng = M.MoeLayerEngine(cfg)
+    t = helpers.to_device(lw)
+    eng.set_layer_packed(0, *t)
+    of, idf, gf, pf = layer_out(eng, h, path, resid)
+    assert kernel in pf, pf
+    assert np.array_equal(idf, ref.ids)
+    assert np.array_equal(bits(gf), bits(ref.gates))
+    assert np.array_equal(bits(of), bits(ref.out))
+    return eng, of
+
+
+@pytest.mark.parametrize("path,kernel", KERNELS)
 @pytest.mark.parametrize("T", [1, 5, 16])
-def test_fused_equals_phased_and_oracle(T):
+def test_single_launch_equals_phased_and_oracle(T, path, kernel):
     lw = O.synth_layer(201, 0, 2048, 1024, 64, 8, T == 5)
     h = O.synth_hidden(201, T, 2048)
     resid = O.synth_hidden(202, T, 2048) if T == 16 else None
-    ref = O.layer_forward(lw, h, resid=resid)
-    eng = M.MoeLayerEngine(M.MoeConfig(2048, 1024, 64, 8, T == 5, T, 1))
-    ex, sc, rt = helpers.to_device(lw)
-    eng.set_layer_packed(0, ex, sc, rt)
-    of, idf, gf, pf = layer_out(eng, h, _lib.MOE_PATH_GEMV, resid)
-    op, idp, gp, pp = layer_out(eng, h, _lib.MOE_PATH_GEMV_PHASED, resid)
-    assert "fused_decode" in pf and "fused_decode" not in pp
-    assert np.array_equal(idf, ref.ids) and np.array_equal(idp, ref.ids)
-    assert np.array_equal(bits(gf), bits(ref.gates))
-    assert np.array_equal(bits(of), bits(ref.out))
-    assert np.array_equal(bits(op), bits(ref.out))
+    cfg = M.MoeConfig(2048, 1024, 64, 8, T == 5, T, 1)
+    eng, of = check_layer(lw, h, resid, path, kernel, cfg)
+    op, _, _, pp = layer_out(eng, h, _lib.MOE_PATH_GEMV_PHASED, resid)
+    assert "fused_decode" not in pp and "stream_decode" not in pp
+    assert np.array_equal(bits(of), bits(op))
 
 
-def test_fused_qwen3_stack_t64():
+_QWEN = {}
+
+
+def qwen_stack():
+    if not _QWEN:
+        layers = [O.synth_layer(211, l, 2048, 768, 128, 8, True) for l in range(2)]
+        x0 = O.synth_hidden(211, 64, 2048)
+        ref_x, _, _ = O.stack_forward(layers, x0, nthreads=8)
+        _QWEN.update(layers=layers, x0=x0, ref=ref_x)
+    return _QWEN
+
+
+@pytest.mark.parametrize("path,kernel", KERNELS)
+def test_qwen3_stack_t64(path, kernel):
     """Qwen3-shaped decode (H=2048, I=768, E=128, K=8, normalized), T=64, two
     stacked layers with RMSNorm + residual: bit-exact after both layers."""
-    layers = [O.synth_layer(211, l, 2048, 768, 128, 8, True) for l in range(2)]
-    x0 = O.synth_hidden(211, 64, 2048)
-    ref_x, ref_ids, _ = O.stack_forward(layers, x0, nthreads=8)
+    q = qwen_stack()
     eng = M.MoeLayerEngine(M.MoeConfig(2048, 768, 128, 8, True, 64, 2))
     keep = []
-    for l, lw in enumerate(layers):
+    for l, lw in enumerate(q["layers"]):
         t = helpers.to_device(lw)
         keep.append(t)
         eng.set_layer_packed(l, *t)
-    x = torch.from_numpy(x0).cuda()
+    eng.set_path(path)
+    x = torch.from_numpy(q["x0"]).cuda()
     eng.profile(True)
     eng.stack_forward(0, 2, x, 1e-5)
     eng.sync_status()
-    assert "fused_decode" in eng.profile_read()
+    assert kernel in eng.profile_read()
     xg = x.cpu().numpy()
-    assert helpers.rel_err(xg, ref_x) < 1e-3
-    assert np.array_equal(bits(xg), bits(ref_x))
+    assert helpers.rel_err(xg, q["ref"]) < 1e-3
+    assert np.array_equal(bits(xg), bits(q["ref"]))
 
 
-def test_fused_router_variant_and_repeat_calls():
-    """Router::select_top_k semantics through the fused kernel, and repeated
-    calls (the per-token arrival counters must reset themselves)."""
+@pytest.mark.parametrize("T", [1, 8, 32])
+def test_stream_olmoe_stack(T):
+    """Config-2 shapes (OLMoE layers, RMSNorm + residual between them) through
+    one streaming launch per stack of three layers; repeated twice so the
+    alternating counter sets are both exercised."""
+    layers = [O.synth_layer(231, l, 2048, 1024, 64, 8, False) for l in range(3)]
+    x0 = O.synth_hidden(231, T, 2048)
+    ref_x, ref_ids, _ = O.stack_forward(layers, x0, nthreads=8)
+    eng = M.MoeLayerEngine(M.MoeConfig(2048, 1024, 64, 8, False, T, 3))
+    keep = [helpers.to_device(lw) for lw in layers]
+    for l, t in enumerate(keep):
+        eng.set_layer_packed(l, *t)
+    eng.set_path(_lib.MOE_PATH_GEMV_STREAM)
+    for _ in range(2):
+        x = torch.from_numpy(x0).cuda()
+        eng.profile(True)
+        eng.stack_forward(0, 3, x, 1e-5)
+        eng.sync_status()
+        assert "stream_decode" in eng.profile_read()
+        assert np.array_equal(bits(x.cpu().numpy()), bits(ref_x))
+
+
+def test_stream_many_routes_per_expert():
+    """Few experts, many tokens: experts hold more routes than one segment
+    (4), and windows straddle two segments with up to eight staged token
+    rows."""
+    H, I, E, K, T = 512, 256, 8, 2, 24
+    lw = O.synth_layer(241, 0, H, I, E, K, True)
+    h = O.synth_hidden(241, T, H)
+    resid = O.synth_hidden(242, T, H)
+    check_layer(lw, h, resid, _lib.MOE_PATH_GEMV_STREAM, "stream_decode",
+                M.MoeConfig(H, I, E, K, True, T, 1))
+
+
+def test_stream_bf16_router():
+    """A bf16 router (rows staged with scalar loads) through the streaming
+    kernel."""
+    H, I, E, K, T = 512, 256, 32, 4, 3
+    lw = O.synth_layer(251, 0, H, I, E, K, False)
+    rb = (lw.router.view(np.uint32) >> 16).astype(np.uint16)
+    lw = O.LayerWeights(H, I, E, K, False, rb, lw.experts, lw.scales, router_bf16=True)
+    h = O.synth_hidden(251, T, H)
+    check_layer(lw, h, None, _lib.MOE_PATH_GEMV_STREAM, "stream_decode",
+                M.MoeConfig(H, I, E, K, False, T, 1))
+
+
+def test_stream_falls_back_on_odd_shapes():
+    """I not a multiple of 32: the streaming kernel declines and the
+    register-prefetch kernel runs instead, still bit-exact."""
+    H, I, E, K, T = 256, 200, 16, 4, 2
+    lw = O.synth_layer(261, 0, H, I, E, K, True)
+    h = O.synth_hidden(261, T, H)
+    check_layer(lw, h, None, _lib.MOE_PATH_GEMV_STREAM, "fused_decode",
+                M.MoeConfig(H, I, E, K, True, T, 1))
+
+
+@pytest.mark.parametrize("path,kernel", KERNELS)
+def test_router_variant_and_repeat_calls(path, kernel):
+    """Router::select_top_k semantics through the single-launch kernels, and
+    repeated calls (counters must come back clean)."""
     lw = O.synth_layer(221, 0, 256, 128, 16, 4, True)
     eng = M.MoeLayerEngine(M.MoeConfig(256, 128, 16, 4, True, 8, 1))
     ex, sc, rt = helpers.to_device(lw)
@@ -83,8 +164,8 @@ def test_fused_router_variant_and_repeat_calls():
     eng.set_route_mode(_lib.MOE_ROUTE_TOPK_SOFTMAX)
     for rep in range(3):
         h = O.synth_hidden(222 + rep, 8, 256)
-        _, ids, gates, prof = layer_out(eng, h, _lib.MOE_PATH_GEMV)
-        assert "fused_decode" in prof
+        _, ids, gates, prof = layer_out(eng, h, path)
+        assert kernel in prof
         for t in range(8):
             scores = np.array([O.lib().oracle_dot_seq(lw.router[e].ctypes.data,
                                                       h[t].ctypes.data, 256)
