@@ -511,6 +511,7 @@ def run_ep(args, cfg, rank, world, local):
                            "experts": E, "top_k": K, "norm_topk_prob": cfg["norm"],
                            "tokens_per_rank": T, "experts_per_rank": EL,
                            "parallelism": f"ep{world}",
+                           "transport": eng.ep_transport(),
                            "placement": "balanced" if zipf else "contiguous",
                            "l2": f"weights rotate over {n_layers} layers > 126 MB L2"},
                 "roofline": roofline, "cpu_baseline": None, "e2e": e2e,

@@ -81,6 +81,7 @@ SIGNATURES = {
     "moe_ep_set_layer": (I32, [P, I32, P, P, P, I32]),
     "moe_ep_layer_forward": (I32, [P, I32, P, P, P, I32, P]),
     "moe_ep_finalize": (I32, [P]),
+    "moe_ep_transport": (I32, [P]),
 }
 
 _lib = None

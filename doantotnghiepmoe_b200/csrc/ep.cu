@@ -194,3 +194,286 @@ cudaError_t launch_seg_counts(const int32_t *seg, int n, int32_t *cnt, cudaStrea
   return cudaGetLastError();
 }
 }  // namespace moe
+
+// ---------------------------------------------------------------------------
+// Device-driven exchange over NVLink peer memory (CUDA IPC).  Every rank owns
+// one region, mapped by all peers at the same offsets (EpP2P).  No host
+// synchronisation and no collective library on the data path:
+//   1. publish: this rank's per-expert route counts go into every peer's
+//      count matrix, then flag A;
+//   2. dispatch: after every rank's counts are in, each route is quantized
+//      and written straight into its owner's expert-sorted tensor-core input
+//      (digit planes, scales, gate, source rank/token/slot); the last CTA
+//      raises flag B on every peer;
+//   3. receive: the owner waits for flag B from every rank and derives its
+//      expert segments from the count matrix;
+//   4. the down GEMM's epilogue writes gate * y straight into the source
+//      rank's [T, K, H] contribution buffer; flag C follows;
+//   5. combine: the source waits for flag C from every rank and sums the
+//      contributions in slot order.
+// Flags carry the call's epoch (monotonic), so nothing is ever reset.  Every
+// wait is bounded; on expiry the kernel records kStatusTimeout and moves on.
+// ---------------------------------------------------------------------------
+namespace moe {
+namespace {
+
+constexpr long long kEpWaitCycles = 4000000000LL;  // ~2 s
+
+__device__ __forceinline__ bool ep_wait_flags(const uint32_t *flags, int n, uint32_t epoch) {
+  const long long t0 = clock64();
+  for (int q = 0; q < n; ++q) {
+    const volatile uint32_t *f = flags + q;
+    while (*f < epoch)
+      if (clock64() - t0 > kEpWaitCycles) return false;
+  }
+  __threadfence_system();
+  return true;
+}
+
+__device__ __forceinline__ uint8_t *peer_at(const EpP2P &p, int rank, size_t off) {
+  return p.base[rank] + off;
+}
+
+__global__ void ep_publish_kernel(const int32_t *__restrict__ seg_off, int E, EpP2P p,
+                                  uint32_t epoch) {
+  const int par = epoch & 1;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int32_t c = seg_off[e + 1] - seg_off[e];
+    for (int q = 0; q < p.nranks; ++q) {
+      int32_t *cm = reinterpret_cast<int32_t *>(peer_at(p, q, p.off_counts));
+      cm[((size_t)par * p.nranks + p.rank) * E + e] = c;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int q = 0; q < p.nranks; ++q)
+      reinterpret_cast<volatile uint32_t *>(peer_at(p, q, p.off_flags))[0 * kEpMaxRanks + p.rank] =
+          epoch;
+  }
+}
+
+// dest_base[e]: first position, in the owner's expert-sorted receive buffer,
+// of this rank's routes to expert e = (routes of the owner's earlier local
+// experts, all sources) + (routes to e from lower ranks).
+__device__ void ep_dest_bases(const int32_t *cm, const int32_t *owner, int E, int me, int N,
+                              int32_t *tot, int32_t *base) {
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int t = 0, before = 0;
+    for (int q = 0; q < N; ++q) {
+      const int c = cm[(size_t)q * E + e];
+      t += c;
+      if (q < me) before += c;
+    }
+    tot[e] = t;
+    base[e] = before;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int o = owner[e];
+    int s = 0;
+    for (int e2 = 0; e2 < e; ++e2)
+      if (owner[e2] == o) s += tot[e2];
+    base[e] += s;
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(
+    const float *__restrict__ x, const int32_t *__restrict__ seg_off,
+    const int32_t *__restrict__ r_token, const int32_t *__restrict__ r_slot,
+    const float *__restrict__ r_gate, const int32_t *__restrict__ owner, int E, int R, int H,
+    EpP2P p, uint32_t epoch, uint32_t *done, uint32_t *status) {
+  __shared__ int32_t tot[kMaxExperts], base[kMaxExperts], segs[kMaxExperts + 1];
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
+                           0 * kEpMaxRanks,
+                       p.nranks, epoch);
+    if (!ok) set_status(status, kStatusTimeout);
+  }
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) segs[e] = seg_off[e];
+  __syncthreads();
+  const int par = epoch & 1;
+  if (ok) {
+    const int32_t *cm =
+        reinterpret_cast<const int32_t *>(p.base[p.rank] + p.off_counts) + (size_t)par * p.nranks * E;
+    ep_dest_bases(cm, owner, E, p.rank, p.nranks, tot, base);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * 8 + warp; r < R; r += gridDim.x * 8) {
+      int lo = 0, hi = E - 1;  // expert of permuted route r: last e with segs[e] <= r
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (segs[mid] <= r) lo = mid; else hi = mid - 1;
+      }
+      const int e = lo, q = owner[e];
+      const size_t pos = (size_t)base[e] + (r - segs[e]);
+      const int t = r_token[r];
+      const float *xr = x + (size_t)t * H;
+      // the single-GPU tensor path's two-digit quantization of the row
+      float amax = 0.0f;
+      for (int c = lane * 4; c < H; c += 128) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+      const float inv = 1.0f / s;
+      uint8_t *qbase = peer_at(p, q, p.off_xq);
+      uint8_t *d1 = qbase + pos * H, *d2 = qbase + p.plane + pos * H;
+      for (int c = lane * 4; c < H; c += 128) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        const float in[4] = {v.x, v.y, v.z, v.w};
+        uint32_t p1 = 0, p2 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float qv = in[k] * inv;
+          const float a1 = fminf(fmaxf(rintf(qv), -127.0f), 127.0f);
+          const float a2 = fminf(fmaxf(rintf((qv - a1) * 254.0f), -127.0f), 127.0f);
+          p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
+          p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
+        }
+        *reinterpret_cast<uint32_t *>(d1 + c) = p1;
+        *reinterpret_cast<uint32_t *>(d2 + c) = p2;
+      }
+      if (lane == 0) {
+        reinterpret_cast<float *>(peer_at(p, q, p.off_s1))[pos] = s;
+        reinterpret_cast<float *>(peer_at(p, q, p.off_s2))[pos] = s / 254.0f;
+        reinterpret_cast<float *>(peer_at(p, q, p.off_gate))[pos] = r_gate[r];
+        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_rank))[pos] = p.rank;
+        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_tok))[pos] = t;
+        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_slot))[pos] = r_slot[r];
+        reinterpret_cast<uint32_t *>(peer_at(p, q, p.off_amax))[pos] = 0u;
+      }
+    }
+  }
+  // the last CTA to finish raises flag B on every peer
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t prev = atomicAdd(done, 1u);
+    if (prev + 1 == epoch * gridDim.x) {
+      __threadfence_system();
+      for (int q = 0; q < p.nranks; ++q)
+        reinterpret_cast<volatile uint32_t *>(peer_at(p, q, p.off_flags))[1 * kEpMaxRanks + p.rank] =
+            epoch;
+    }
+  }
+}
+
+// One CTA: wait for every rank's routes, then this rank's expert segments
+// (local expert order) from the count matrix.
+__global__ void __launch_bounds__(256) ep_recv_prep_kernel(const int32_t *__restrict__ owner,
+                                                           int E, EpP2P p, uint32_t epoch,
+                                                           int32_t *seg_l, int32_t *active_l,
+                                                           int32_t *n_active_l,
+                                                           int32_t *n_recv, uint32_t *status) {
+  __shared__ int ok;
+  __shared__ int32_t tot[kMaxExperts];
+  if (threadIdx.x == 0) {
+    ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
+                           1 * kEpMaxRanks,
+                       p.nranks, epoch);
+    if (!ok) set_status(status, kStatusTimeout);
+  }
+  __syncthreads();
+  const int par = epoch & 1;
+  const int32_t *cm =
+      reinterpret_cast<const int32_t *>(p.base[p.rank] + p.off_counts) + (size_t)par * p.nranks * E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int t = 0;
+    if (ok)
+      for (int q = 0; q < p.nranks; ++q) t += cm[(size_t)q * E + e];
+    tot[e] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0, el = 0, na = 0;
+    for (int e = 0; e < E; ++e) {
+      if (owner[e] != p.rank) continue;
+      seg_l[el] = acc;
+      if (tot[e] > 0) active_l[na++] = el;
+      acc += tot[e];
+      ++el;
+    }
+    seg_l[el] = acc;
+    *n_active_l = na;
+    *n_recv = acc;
+  }
+}
+
+__global__ void ep_signal_kernel(EpP2P p, uint32_t epoch) {
+  __threadfence_system();
+  for (int q = 0; q < p.nranks; ++q)
+    reinterpret_cast<volatile uint32_t *>(peer_at(p, q, p.off_flags))[2 * kEpMaxRanks + p.rank] =
+        epoch;
+}
+
+// out[t] = resid[t] (or 0) + contrib[t, 0] + ... + contrib[t, K-1], slot
+// order, once every rank's contributions are in.
+__global__ void ep_wait_combine_kernel(EpP2P p, uint32_t epoch, const float *__restrict__ resid,
+                                       float *__restrict__ out, int T, int K, int H,
+                                       uint32_t *status) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
+                           2 * kEpMaxRanks,
+                       p.nranks, epoch);
+    if (!ok) set_status(status, kStatusTimeout);
+  }
+  __syncthreads();
+  if (!ok) return;
+  const float *contrib = reinterpret_cast<const float *>(p.base[p.rank] + p.off_contrib);
+  bool bad = false;
+  const size_t n = (size_t)T * H;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t t = i / H, j = i % H;
+    float acc = resid ? resid[i] : 0.0f;
+    for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __ldcg(contrib + (t * K + k) * H + j));
+    bad |= !is_finite_f(acc);
+    out[i] = acc;
+  }
+  if (bad) set_status(status, kStatusNonFinite);
+}
+
+}  // namespace
+
+cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uint32_t epoch,
+                              cudaStream_t s) {
+  ep_publish_kernel<<<1, 256, 0, s>>>(seg_off, E, p, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const int32_t *r_token,
+                               const int32_t *r_slot, const float *r_gate, const int32_t *owner,
+                               int E, int R, int H, const EpP2P &p, uint32_t epoch,
+                               uint32_t *done, int grid, uint32_t *status, cudaStream_t s) {
+  ep_dispatch_kernel<<<grid, 256, 0, s>>>(x, seg_off, r_token, r_slot, r_gate, owner, E, R, H, p,
+                                          epoch, done, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p, uint32_t epoch,
+                                int32_t *seg_l, int32_t *active_l, int32_t *n_active_l,
+                                int32_t *n_recv, uint32_t *status, cudaStream_t s) {
+  ep_recv_prep_kernel<<<1, 256, 0, s>>>(owner, E, p, epoch, seg_l, active_l, n_active_l, n_recv,
+                                        status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_signal(const EpP2P &p, uint32_t epoch, cudaStream_t s) {
+  ep_signal_kernel<<<1, 1, 0, s>>>(p, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait_combine(const EpP2P &p, uint32_t epoch, const float *resid, float *out,
+                                   int T, int K, int H, uint32_t *status, cudaStream_t s) {
+  const size_t n = (size_t)T * H;
+  const int blocks = (int)std::max<size_t>(1, std::min<size_t>((n + 255) / 256, 148 * 8));
+  ep_wait_combine_kernel<<<blocks, 256, 0, s>>>(p, epoch, resid, out, T, K, H, status);
+  return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -268,7 +268,7 @@ __device__ __forceinline__ void teardown(Pipe &pp, uint32_t ncols, uint32_t *sta
 // Dynamic smem: [Pipe | per-route epilogue table | pad | tiles (1024-aligned)].
 struct RouteTab {
   float s1[128], s2[128], gate[128];
-  int32_t tok[128], slot[128];
+  int32_t tok[128], slot[128], rank[128];
 };
 constexpr size_t smem_bytes(int na, int nb, int bn, int stages) {
   return 1024 + sizeof(Pipe) + sizeof(RouteTab) + 1024 +
@@ -381,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
       tab.gate[c] = a.r_gate[r];
       tab.tok[c] = a.r_token[r];
       tab.slot[c] = a.r_slot[r];
+      tab.rank[c] = a.r_rank ? a.r_rank[r] : 0;
     }
     const int q = warp & 3;
     const int j = m0 + 32 * q + lane;  // output row (hidden index)
@@ -405,8 +406,10 @@ __global__ void __launch_bounds__(kThreads, MINB)
           if (c < nr && j < a.H) {
             const float y = fmaf(tab.s1[c], (float)v[0][jj], tab.s2[c] * (float)v[1][jj]) * sd;
             bad |= !is_finite_f(y);
-            a.contrib[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + j] =
-                __fmul_rn(tab.gate[c], y);
+            // expert parallelism: the row goes straight to the source rank's
+            // contribution buffer (peer memory over NVLink)
+            float *dst = a.r_rank ? a.peer_contrib[tab.rank[c]] : a.contrib;
+            dst[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + j] = __fmul_rn(tab.gate[c], y);
           }
         }
       }
@@ -458,12 +461,13 @@ __global__ void __launch_bounds__(256) build_tiles_kernel(const int32_t *seg_off
 // src rows are gathered through `rows` (null = identity).  Also resets the
 // per-row amax used by the next stage when `amax_reset` is given.
 __global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_t *__restrict__ rows,
-                                     const uint32_t *__restrict__ amax_in, int R, int n,
+                                     const uint32_t *__restrict__ amax_in, int R,
+                                     const int32_t *__restrict__ R_dev, int n,
                                      int8_t *__restrict__ q, size_t plane, float *__restrict__ s1,
                                      float *__restrict__ s2, uint32_t *__restrict__ amax_reset) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= R) return;
+  if (warp >= R || (R_dev && warp >= *R_dev)) return;
   const int row = rows ? rows[warp] : warp;
   const float *x = src + (size_t)row * n;
   float amax;
@@ -546,10 +550,10 @@ cudaError_t launch_build_tiles(const int32_t *seg_off, const int32_t *active,
 
 cudaError_t launch_quantize_rows(const float *src, const int32_t *rows, const uint32_t *amax_in,
                                  int R, int n, int8_t *q, size_t plane, float *s1, float *s2,
-                                 uint32_t *amax_reset, cudaStream_t s) {
+                                 uint32_t *amax_reset, cudaStream_t s, const int32_t *R_dev) {
   if (R <= 0) return cudaSuccess;
-  quantize_rows_kernel<<<(R + 7) / 8, 256, 0, s>>>(src, rows, amax_in, R, n, q, plane, s1, s2,
-                                                   amax_reset);
+  quantize_rows_kernel<<<(R + 7) / 8, 256, 0, s>>>(src, rows, amax_in, R, R_dev, n, q, plane, s1,
+                                                   s2, amax_reset);
   return cudaGetLastError();
 }
 

@@ -28,6 +28,10 @@ struct TcArgs {
   const int32_t *r_token, *r_slot;
   const float *r_gate;
   float *contrib;              // [T, K, H]
+  // expert parallelism over peer memory: when r_rank is set, route r's row
+  // goes to peer_contrib[r_rank[r]] (the source rank's [T, K, H] buffer)
+  const int32_t *r_rank;
+  float *peer_contrib[8];
   uint32_t *status;
 };
 
@@ -40,9 +44,11 @@ cudaError_t launch_build_tiles(const int32_t *seg_off, const int32_t *active,
                                int32_t *tile_row0, int32_t *tile_rows, int32_t *n_tiles,
                                int max_tiles, cudaStream_t s);
 
+// R rows (grid size); when R_dev is given, rows at or past *R_dev are skipped.
 cudaError_t launch_quantize_rows(const float *src, const int32_t *rows, const uint32_t *amax_in,
                                  int R, int n, int8_t *q, size_t plane, float *s1, float *s2,
-                                 uint32_t *amax_reset, cudaStream_t s);
+                                 uint32_t *amax_reset, cudaStream_t s,
+                                 const int32_t *R_dev = nullptr);
 
 cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
                               int bn, int max_tiles, cudaStream_t s);

@@ -45,7 +45,12 @@ struct PermuteArgs {
   float *r_gate;        // [T*K] permuted position -> gate (may be null)
   int32_t *r_pos;       // [T*K] (t*K + slot) -> permuted position (may be null)
   uint32_t *status;
+  // optional scratch for the multi-CTA sort (large T*K); without it, or too
+  // small, one CTA sorts everything
+  int32_t *scratch;
+  size_t scratch_words;
 };
+size_t permute_scratch_words(int R, int E);
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t s);
 
 // Grouped INT8 GEMV over expert segments (expert_gemv.cu), in the exact
@@ -156,6 +161,31 @@ cudaError_t launch_seg_counts(const int32_t *seg, int n, int32_t *cnt, cudaStrea
 cudaError_t launch_ep_gather_combine(const float *ret, const int32_t *pos, const float *resid,
                                      float *out, int T, int K, int H, uint32_t *status,
                                      cudaStream_t s);
+
+// Expert parallelism over NVLink peer memory: one region per rank, mapped by
+// every peer (CUDA IPC) at the same offsets.
+constexpr int kEpMaxRanks = 8;
+struct EpP2P {
+  uint8_t *base[kEpMaxRanks];  // region of each rank, as mapped in this process
+  int rank, nranks;
+  size_t off_flags;            // uint32 [3][kEpMaxRanks]: A counts, B routes, C outputs
+  size_t off_counts;           // int32 [2][nranks][E] route counts by source rank
+  size_t off_xq, plane;        // int8 [2][RR][H] digit planes (plane = RR * H)
+  size_t off_s1, off_s2, off_gate, off_rank, off_tok, off_slot, off_amax;  // [RR]
+  size_t off_contrib;          // f32 [T, K, H] outputs of this rank's routes
+};
+cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uint32_t epoch,
+                              cudaStream_t s);
+cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const int32_t *r_token,
+                               const int32_t *r_slot, const float *r_gate, const int32_t *owner,
+                               int E, int R, int H, const EpP2P &p, uint32_t epoch,
+                               uint32_t *done, int grid, uint32_t *status, cudaStream_t s);
+cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p, uint32_t epoch,
+                                int32_t *seg_l, int32_t *active_l, int32_t *n_active_l,
+                                int32_t *n_recv, uint32_t *status, cudaStream_t s);
+cudaError_t launch_ep_signal(const EpP2P &p, uint32_t epoch, cudaStream_t s);
+cudaError_t launch_ep_wait_combine(const EpP2P &p, uint32_t epoch, const float *resid, float *out,
+                                   int T, int K, int H, uint32_t *status, cudaStream_t s);
 
 // Seeded synthetic expert weights, bit-identical to the host-side generator.
 cudaError_t launch_synth_expert(uint64_t seed, int layer, int expert, int H, int I, int8_t *w,

@@ -374,6 +374,16 @@ struct EpState {
   int32_t *tile_expert = nullptr, *tile_row0 = nullptr, *tile_rows = nullptr, *n_tiles = nullptr;
   CUtensorMap map_x64{}, map_x128{}, map_a64{}, map_a128{};
   std::vector<void *> allocs;
+  // device-driven exchange over NVLink peer memory (CUDA IPC)
+  bool p2p = false;
+  std::string transport_note;       // why the collective-library path is in use
+  void *region = nullptr;           // this rank's peer-visible region
+  std::vector<void *> peer_maps;    // opened peer regions (closed at finalize)
+  EpP2P P{};
+  uint32_t epoch = 0;               // calls so far (flag values)
+  uint32_t *done = nullptr;         // dispatch completion counter (monotonic)
+  int32_t *n_recv = nullptr;        // device count of received routes
+  int dispatch_grid = 0;
 };
 }  // namespace
 
@@ -411,6 +421,8 @@ struct moe_handle {
   std::vector<int> layer_vec;
   uint32_t *tok_cnt = nullptr, *fbar = nullptr;
   uint32_t *sctr = nullptr;                // streaming decode: 2 counter sets
+  int32_t *perm_scratch = nullptr;         // multi-CTA permutation
+  size_t perm_scratch_words = 0;
   uint32_t sctr_parity = 0;                // set used by the next launch
   std::vector<int> layer_async;            // router rows are 16-byte aligned f32
   unsigned long long *phase_ts = nullptr;  // [8] single-launch kernel phase stamps
@@ -423,6 +435,11 @@ namespace {
 
 void free_ep(moe_handle *h) {
   EpState &ep = h->ep;
+  for (void *m : ep.peer_maps) cudaIpcCloseMemHandle(m);
+  ep.peer_maps.clear();
+  if (ep.region) cudaFree(ep.region);
+  ep.region = nullptr;
+  ep.p2p = false;
   if (ep.comm && nccl().ok) nccl().comm_destroy(ep.comm);
   ep.comm = nullptr;
   for (auto &l : ep.layers) cudaFree(l.d_sptr);
@@ -445,7 +462,7 @@ void free_handle(moe_handle *h) {
                   h->active,  h->n_active,  h->r_token,   h->r_slot,    h->r_pos,   h->xq,
                   h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
                   h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles, h->d_flayers,
-                  h->tok_cnt, h->fbar, h->phase_ts, h->sctr};
+                  h->tok_cnt, h->fbar, h->phase_ts, h->sctr, h->perm_scratch};
   for (void *p : ptrs) cudaFree(p);
   cudaFreeHost(h->h_pin_in);
   cudaFreeHost(h->h_pin_out);
@@ -501,6 +518,8 @@ moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T,
   pa.r_gate = h->r_gate;
   pa.r_pos = h->r_pos;
   pa.status = h->status;
+  pa.scratch = h->perm_scratch;
+  pa.scratch_words = h->perm_scratch_words;
   p0 = h->prof.begin(s);
   e = launch_permute(pa, s);
   h->prof.end("permute", p0, s);
@@ -785,6 +804,8 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && cudaMemset(h->tok_cnt, 0, T * sizeof(uint32_t)) == cudaSuccess;
   ok = ok && dalloc(&h->phase_ts, 16) == cudaSuccess;
   ok = ok && dalloc(&h->sctr, 2 * kStreamCtrWords) == cudaSuccess;
+  h->perm_scratch_words = permute_scratch_words((int)(T * K), (int)E);
+  ok = ok && dalloc(&h->perm_scratch, h->perm_scratch_words) == cudaSuccess;
   ok = ok && cudaMemset(h->sctr, 0, 2 * kStreamCtrWords * sizeof(uint32_t)) == cudaSuccess;
   h->flayers.assign(d.num_layers, FusedLayer{});
   h->layer_vec.assign(d.num_layers, 0);
@@ -1193,6 +1214,117 @@ moe_status nccl_fail(moe_handle *h, ncclResult_t r, const char *what) {
 }
 }  // namespace
 
+namespace {
+size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
+// Peer-memory transport: one region per rank holding everything peers write
+// (flags, count matrix, the expert-sorted receive side of the tensor-core
+// input, the [T, K, H] contribution buffer), shared through CUDA IPC handles
+// that are exchanged once over the communicator.  On any failure the
+// collective-library transport stays in use and the reason is kept.
+void ep_setup_p2p(moe_handle *h, size_t Tm) {
+  EpState &ep = h->ep;
+  const int N = ep.nranks, E = h->d.num_experts, H = h->d.hidden, K = h->d.top_k;
+  const char *env = getenv("MOE_EP_TRANSPORT");
+  if (env && strcmp(env, "nccl") == 0) {
+    ep.transport_note = "MOE_EP_TRANSPORT=nccl";
+    return;
+  }
+  if (N > kEpMaxRanks) {
+    ep.transport_note = "more ranks than the peer-memory transport supports";
+    return;
+  }
+  const size_t RR = ep.r_recv_cap;
+  EpP2P P{};
+  size_t off = 0;
+  P.off_flags = off;   off = align_up(off + 3 * kEpMaxRanks * 4, 1024);
+  P.off_counts = off;  off = align_up(off + (size_t)2 * N * E * 4, 1024);
+  P.off_xq = off;      P.plane = RR * H; off = align_up(off + 2 * RR * H, 1024);
+  P.off_s1 = off;      off = align_up(off + RR * 4, 1024);
+  P.off_s2 = off;      off = align_up(off + RR * 4, 1024);
+  P.off_gate = off;    off = align_up(off + RR * 4, 1024);
+  P.off_rank = off;    off = align_up(off + RR * 4, 1024);
+  P.off_tok = off;     off = align_up(off + RR * 4, 1024);
+  P.off_slot = off;    off = align_up(off + RR * 4, 1024);
+  P.off_amax = off;    off = align_up(off + RR * 4, 1024);
+  P.off_contrib = off; off = align_up(off + Tm * K * H * 4, 1024);
+  P.rank = ep.rank;
+  P.nranks = N;
+  void *region = nullptr;
+  if (cudaMalloc(&region, off) != cudaSuccess || cudaMemset(region, 0, off) != cudaSuccess) {
+    cudaGetLastError();
+    if (region) cudaFree(region);
+    ep.transport_note = "peer region allocation failed";
+    return;
+  }
+  cudaIpcMemHandle_t mine{};
+  if (cudaIpcGetMemHandle(&mine, region) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(region);
+    ep.transport_note = "cudaIpcGetMemHandle failed";
+    return;
+  }
+  // exchange the handles: every rank sends its 64 bytes to every other rank
+  const size_t HB = sizeof(cudaIpcMemHandle_t);
+  uint8_t *dh = nullptr;
+  std::vector<uint8_t> all(N * HB);
+  bool ok = cudaMalloc(&dh, N * HB) == cudaSuccess &&
+            cudaMemcpy(dh + ep.rank * HB, &mine, HB, cudaMemcpyHostToDevice) == cudaSuccess;
+  cudaStream_t s = h->stream;
+  if (ok) {
+    const NcclApi &api = nccl();
+    ncclResult_t nr = api.group_start();
+    for (int q = 0; q < N && nr == ncclSuccess; ++q) {
+      if (q == ep.rank) continue;
+      nr = api.send(dh + ep.rank * HB, HB, ncclUint8, q, ep.comm, s);
+      if (nr == ncclSuccess) nr = api.recv(dh + q * HB, HB, ncclUint8, q, ep.comm, s);
+    }
+    const ncclResult_t ng = api.group_end();
+    ok = nr == ncclSuccess && ng == ncclSuccess && cudaStreamSynchronize(s) == cudaSuccess &&
+         cudaMemcpy(all.data(), dh, N * HB, cudaMemcpyDeviceToHost) == cudaSuccess;
+  }
+  if (dh) cudaFree(dh);
+  std::vector<void *> maps;
+  for (int q = 0; q < N && ok; ++q) {
+    if (q == ep.rank) {
+      P.base[q] = (uint8_t *)region;
+      continue;
+    }
+    cudaIpcMemHandle_t hq;
+    memcpy(&hq, all.data() + q * HB, HB);
+    void *ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, hq, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = false;
+      break;
+    }
+    maps.push_back(ptr);
+    P.base[q] = (uint8_t *)ptr;
+  }
+  // the tensor-core input maps now point at the region's receive side
+  uint8_t *xq = (uint8_t *)region + P.off_xq;
+  ok = ok && tc::encode_map3d(&ep.map_x64, xq, H, RR, 2, H, RR * H, 64) &&
+       tc::encode_map3d(&ep.map_x128, xq, H, RR, 2, H, RR * H, 128) &&
+       ep_alloc(ep, &ep.done, 1) && ep_alloc(ep, &ep.n_recv, 1) &&
+       cudaMemset(ep.done, 0, 4) == cudaSuccess;
+  if (!ok) {
+    for (void *m : maps) cudaIpcCloseMemHandle(m);
+    cudaFree(region);
+    ep.transport_note = "CUDA IPC handle exchange / mapping failed";
+    // restore the collective-library path's maps
+    tc::encode_map3d(&ep.map_x64, ep.xq, H, RR, 2, H, RR * H, 64);
+    tc::encode_map3d(&ep.map_x128, ep.xq, H, RR, 2, H, RR * H, 128);
+    return;
+  }
+  ep.region = region;
+  ep.peer_maps = maps;
+  ep.P = P;
+  ep.p2p = true;
+  ep.dispatch_grid = 2 * h->sm_count;
+  ep.transport_note.clear();
+}
+}  // namespace
+
 extern "C" moe_status moe_ep_unique_id(unsigned char id_out[128]) {
   if (!id_out) return MOE_ERR_INVALID;
   if (!nccl().ok) return MOE_ERR_NCCL;
@@ -1281,7 +1413,13 @@ extern "C" moe_status moe_ep_init(moe_handle *h, int rank, int nranks,
   }
   ep.layers.assign(h->d.num_layers, EpLayer{});
   ep.on = true;
+  ep_setup_p2p(h, Tm);
   return MOE_OK;
+}
+
+extern "C" int moe_ep_transport(const moe_handle *h) {
+  if (!h || !h->ep.on) return -1;
+  return h->ep.p2p ? 1 : 0;
 }
 
 extern "C" moe_status moe_ep_finalize(moe_handle *h) {
@@ -1332,6 +1470,117 @@ extern "C" moe_status moe_ep_set_layer(moe_handle *h, int layer, const int8_t *d
   return MOE_OK;
 }
 
+namespace {
+// One layer over the peer-memory transport; see ep.cu for the protocol.
+moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const float *d_resid,
+                          float *d_out, int T, cudaStream_t s) {
+  EpState &ep = h->ep;
+  const int H = h->d.hidden, I = h->d.intermediate, K = h->d.top_k, E = h->d.num_experts;
+  const int R = T * K;
+  const size_t RR = ep.r_recv_cap;
+  const LayerSlot &LS = h->layers[layer];
+  const EpLayer &EL = ep.layers[layer];
+  const EpP2P &P = ep.P;
+  const uint32_t epoch = ++ep.epoch;
+  cudaError_t e = cudaSuccess;
+  // 1. route and bucket the local routes by global expert
+  cudaEvent_t p0 = nullptr;
+  if (T > 0) {
+    moe_status st = run_route(h, LS, d_h, T, h->ids, h->gates, nullptr, s, false);
+    if (st != MOE_OK) return st;
+    p0 = h->prof.begin(s);
+    PermuteArgs pa{};
+    pa.ids = h->ids;
+    pa.gates = h->gates;
+    pa.T = T;
+    pa.K = K;
+    pa.E = E;
+    pa.seg_off = h->seg_off;
+    pa.active = h->active;
+    pa.n_active = h->n_active;
+    pa.r_token = h->r_token;
+    pa.r_slot = h->r_slot;
+    pa.r_gate = h->r_gate;
+    pa.r_pos = nullptr;
+    pa.status = h->status;
+    pa.scratch = h->perm_scratch;
+    pa.scratch_words = h->perm_scratch_words;
+    e = launch_permute(pa, s);
+    h->prof.end("permute", p0, s);
+  } else {
+    e = cudaMemsetAsync(h->seg_off, 0, (E + 1) * sizeof(int32_t), s);
+  }
+  // 2. counts to every peer, 3. routes straight into the owners' buffers
+  cudaEvent_t p1 = h->prof.begin(s);
+  if (e == cudaSuccess) e = launch_ep_publish(h->seg_off, E, P, epoch, s);
+  if (e == cudaSuccess)
+    e = launch_ep_dispatch(d_h, h->seg_off, h->r_token, h->r_slot, h->r_gate, ep.d_owner, E, R,
+                           H, P, epoch, ep.done, ep.dispatch_grid, h->status, s);
+  h->prof.end("ep_dispatch", p1, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "ep dispatch");
+  // 4. wait for every rank's routes; expert segments from the count matrix
+  cudaEvent_t p2 = h->prof.begin(s);
+  e = launch_ep_recv_prep(ep.d_owner, E, P, epoch, ep.seg_l, ep.active_l, ep.n_active_l,
+                          ep.n_recv, h->status, s);
+  const int bn = tc::tc_block_n(std::max(R, 1), std::max(ep.E_local, 1));
+  if (e == cudaSuccess && ep.E_local > 0)
+    e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, bn, ep.tile_expert,
+                               ep.tile_row0, ep.tile_rows, ep.n_tiles, ep.max_tiles, s);
+  h->prof.end("ep_recv", p2, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "ep receive");
+  // 5. experts; the down epilogue writes each output row to its source rank
+  if (ep.E_local > 0) {
+    uint8_t *me = P.base[P.rank];
+    tc::TcArgs a{};
+    a.H = H;
+    a.I = I;
+    a.K = K;
+    a.tile_expert = ep.tile_expert;
+    a.tile_row0 = ep.tile_row0;
+    a.tile_rows = ep.tile_rows;
+    a.n_tiles = ep.n_tiles;
+    a.s_ptr = EL.d_sptr;
+    a.xs1 = (const float *)(me + P.off_s1);
+    a.xs2 = (const float *)(me + P.off_s2);
+    a.act = ep.act;
+    a.act_amax = (uint32_t *)(me + P.off_amax);
+    a.as1 = ep.as1;
+    a.as2 = ep.as2;
+    a.r_token = (const int32_t *)(me + P.off_tok);
+    a.r_slot = (const int32_t *)(me + P.off_slot);
+    a.r_gate = (const float *)(me + P.off_gate);
+    a.r_rank = (const int32_t *)(me + P.off_rank);
+    for (int q = 0; q < P.nranks; ++q) a.peer_contrib[q] = (float *)(P.base[q] + P.off_contrib);
+    a.contrib = a.peer_contrib[P.rank];
+    a.status = h->status;
+    cudaEvent_t p3 = h->prof.begin(s);
+    e = tc::launch_gate_up_tc(EL.map_gu, bn == 64 ? ep.map_x64 : ep.map_x128, a, bn,
+                              ep.max_tiles, s);
+    h->prof.end("gate_up_tc", p3, s);
+    p3 = h->prof.begin(s);
+    if (e == cudaSuccess)
+      e = tc::launch_quantize_rows(ep.act, nullptr, a.act_amax, (int)RR, I, ep.aq, RR * I,
+                                   ep.as1, ep.as2, nullptr, s, ep.n_recv);
+    h->prof.end("tc_act_digits", p3, s);
+    p3 = h->prof.begin(s);
+    if (e == cudaSuccess)
+      e = tc::launch_down_tc(EL.map_dn, bn == 64 ? ep.map_a64 : ep.map_a128, a, bn,
+                             ep.max_tiles, s);
+    h->prof.end("down_tc", p3, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "ep experts");
+  }
+  // 6. outputs are in: signal the sources; 7. combine this rank's tokens
+  cudaEvent_t p4 = h->prof.begin(s);
+  e = launch_ep_signal(P, epoch, s);
+  if (e == cudaSuccess)
+    e = launch_ep_wait_combine(P, epoch, d_resid, d_out, T, K, H, h->status, s);
+  h->prof.end("ep_combine", p4, s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "ep combine");
+  h->last_launches += 11;
+  return MOE_OK;
+}
+}  // namespace
+
 extern "C" moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float *d_h,
                                            const float *d_resid, float *d_out, int T,
                                            void *stream) {
@@ -1356,6 +1605,7 @@ extern "C" moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float
   const EpLayer &EL = ep.layers[layer];
   cudaError_t e = cudaSuccess;
   moe_status st = MOE_OK;
+  if (ep.p2p) return ep_forward_p2p(h, layer, d_h, d_resid, d_out, T, s);
   // 1. route the local tokens and bucket the routes by owner rank
   if (T > 0) {
     st = run_route(h, LS, d_h, T, h->ids, h->gates, nullptr, s, false);
@@ -1375,6 +1625,8 @@ extern "C" moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float
     pa.r_gate = ep.sgate;
     pa.r_pos = ep.spos;
     pa.status = h->status;
+    pa.scratch = h->perm_scratch;
+    pa.scratch_words = h->perm_scratch_words;
     cudaEvent_t p0 = h->prof.begin(s);
     if (e == cudaSuccess) e = launch_permute(pa, s);
     if (e == cudaSuccess)

@@ -262,7 +262,92 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(PermuteArgs a) {
   }
 }
 
+// Multi-CTA stable counting sort for large route counts: (1) per tile of
+// 1024 routes, the per-expert counts and each route's rank inside its tile
+// (warp match mask + earlier warps' counts); (2) one CTA turns the tile
+// counts into per-tile offsets and the expert segments; (3) every route is
+// scattered to seg_off[e] + tile offset + rank in tile.  Same order as the
+// single-CTA kernel: experts ascending, routes (tokens) ascending inside.
+constexpr int kPermTile = 1024;
+
+__global__ void __launch_bounds__(kPermTile) perm_hist_kernel(PermuteArgs a, int32_t *tilecnt,
+                                                              int32_t *intra) {
+  __shared__ int32_t wcnt[kPermTile / 32][kMaxExperts];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int E = a.E, R = a.T * a.K;
+  for (int i = tid; i < (kPermTile / 32) * kMaxExperts; i += kPermTile) (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  const int r = blockIdx.x * kPermTile + tid;
+  const bool valid = r < R;
+  const uint32_t e = valid ? a.ids[r] : 0xFFFFFFFFu;
+  const bool ok = valid && e < (uint32_t)E;
+  if (valid && !ok) set_status(a.status, kStatusBadRoute);
+  const unsigned mask = __match_any_sync(0xffffffffu, ok ? e : 0xFFFFFFFFu);
+  const int in_warp = __popc(mask & ((1u << lane) - 1u));
+  if (ok && in_warp == 0) wcnt[warp][e] = __popc(mask);
+  __syncthreads();
+  if (ok) {
+    int rank = in_warp;
+    for (int w = 0; w < warp; ++w) rank += wcnt[w][e];
+    intra[r] = rank;
+  }
+  for (int ee = tid; ee < E; ee += kPermTile) {
+    int tot = 0;
+    for (int w = 0; w < kPermTile / 32; ++w) tot += wcnt[w][ee];
+    tilecnt[(size_t)blockIdx.x * E + ee] = tot;
+  }
+}
+
+__global__ void __launch_bounds__(kMaxExperts) perm_scan_kernel(PermuteArgs a, int32_t *tilecnt,
+                                                                int ntiles) {
+  __shared__ int32_t tot[kMaxExperts], act[kMaxExperts];
+  const int e = threadIdx.x, E = a.E;
+  int run = 0;
+  if (e < E)
+    for (int t = 0; t < ntiles; ++t) {
+      const int c = tilecnt[(size_t)t * E + e];
+      tilecnt[(size_t)t * E + e] = run;
+      run += c;
+    }
+  tot[e] = e < E ? run : 0;
+  act[e] = (e < E && run > 0) ? 1 : 0;
+  __syncthreads();
+  for (int o = 1; o < kMaxExperts; o <<= 1) {  // inclusive scans
+    const int v = e >= o ? tot[e - o] : 0, w = e >= o ? act[e - o] : 0;
+    __syncthreads();
+    tot[e] += v;
+    act[e] += w;
+    __syncthreads();
+  }
+  if (e < E) {
+    a.seg_off[e] = tot[e] - run;
+    if (run > 0) a.active[act[e] - 1] = e;
+  }
+  if (e == kMaxExperts - 1) {
+    a.seg_off[E] = tot[e];
+    *a.n_active = act[e];
+  }
+}
+
+__global__ void perm_scatter_kernel(PermuteArgs a, const int32_t *tilecnt,
+                                    const int32_t *intra) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  const int R = a.T * a.K;
+  if (r >= R) return;
+  const uint32_t e = a.ids[r];
+  if (e >= (uint32_t)a.E) return;
+  const int pos = a.seg_off[e] + tilecnt[(size_t)(r / kPermTile) * a.E + e] + intra[r];
+  a.r_token[pos] = r / a.K;
+  a.r_slot[pos] = r % a.K;
+  if (a.r_gate) a.r_gate[pos] = a.gates[r];
+  if (a.r_pos) a.r_pos[r] = pos;
+}
+
 }  // namespace
+
+size_t permute_scratch_words(int R, int E) {
+  return (size_t)((R + kPermTile - 1) / kPermTile) * E + (size_t)R;
+}
 
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
@@ -284,7 +369,16 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t s) {
 }
 
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t s) {
-  permute_kernel<<<1, kPermThreads, 0, s>>>(a);
+  const int R = a.T * a.K;
+  if (R <= 2 * kPermTile || !a.scratch || a.scratch_words < permute_scratch_words(R, a.E)) {
+    permute_kernel<<<1, kPermThreads, 0, s>>>(a);
+    return cudaGetLastError();
+  }
+  const int ntiles = (R + kPermTile - 1) / kPermTile;
+  int32_t *tilecnt = a.scratch, *intra = a.scratch + (size_t)ntiles * a.E;
+  perm_hist_kernel<<<ntiles, kPermTile, 0, s>>>(a, tilecnt, intra);
+  perm_scan_kernel<<<1, kMaxExperts, 0, s>>>(a, tilecnt, ntiles);
+  perm_scatter_kernel<<<(R + 255) / 256, 256, 0, s>>>(a, tilecnt, intra);
   return cudaGetLastError();
 }
 

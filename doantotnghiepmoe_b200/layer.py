@@ -158,6 +158,10 @@ class MoeLayerEngine:
     def ep_finalize(self):
         self._check(lib().moe_ep_finalize(self._h))
 
+    def ep_transport(self) -> str:
+        """'p2p' (kernels write into peer memory), 'nccl' or 'none'."""
+        return {1: "p2p", 0: "nccl"}.get(lib().moe_ep_transport(self._h), "none")
+
     def profile(self, enable: bool):
         self._check(lib().moe_profile_enable(self._h, int(enable)))
 

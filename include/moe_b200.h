@@ -196,8 +196,12 @@ moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8_t *d_exper
  * 2b. Expert parallelism (no counterpart in the reference, which runs on one
  *     device, src/gpu.rs:457-460).  One process per GPU; experts are owned by
  *     ranks, tokens stay on the rank that routes them.  Dispatch and combine
- *     are NCCL point-to-point exchanges inside moe_ep_layer_forward; results
- *     equal the single-GPU tensor-core path bit for bit.
+ *     run inside moe_ep_layer_forward: by default the kernels write straight
+ *     into peer memory over NVLink (CUDA IPC, handles exchanged once at
+ *     moe_ep_init; no host synchronisation per layer); without peer mappings,
+ *     or with MOE_EP_TRANSPORT=nccl in the environment, as NCCL
+ *     point-to-point exchanges.  Either way the results equal the single-GPU
+ *     tensor-core path bit for bit.
  * ---------------------------------------------------------------------- */
 /* 128-byte NCCL unique id; rank 0 creates it and the host shares it. */
 moe_status moe_ep_unique_id(unsigned char id_out[128]);
@@ -215,6 +219,8 @@ moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float *d_h, cons
                                 float *d_out, int T_local, void *stream);
 /* Leave the group (destroys the communicator; also done by moe_destroy). */
 moe_status moe_ep_finalize(moe_handle *h);
+/* Transport in use: 1 = peer memory, 0 = NCCL point-to-point, -1 = no group. */
+int moe_ep_transport(const moe_handle *h);
 
 /* ------------------------------------------------------------------------
  * 3. Utilities for tests and benchmarks (no reference counterpart).

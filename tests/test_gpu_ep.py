@@ -1,6 +1,6 @@
 """Expert parallelism on 2 GPUs (skipped with fewer): experts split over two
-processes, tokens split over two processes, NCCL dispatch/combine inside the
-library.  Each rank's output rows must equal, bit for bit, the single-GPU
+processes, tokens split over two processes, dispatch/combine inside the
+library over both transports (kernels writing into peer memory, and NCCL).  Each rank's output rows must equal, bit for bit, the single-GPU
 tensor-core path run on the same rank with all experts resident; routing must
 equal the CPU oracle's."""
 import os
@@ -21,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, transport):
     import datetime
 
     import torch.distributed as dist
@@ -32,6 +32,8 @@ def _worker(rank, world, port, outdir):
     from tests import helpers
 
     torch.cuda.set_device(rank)
+    if transport == "nccl":
+        os.environ["MOE_EP_TRANSPORT"] = "nccl"
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world, timeout=datetime.timedelta(seconds=120))
     H, I, E, K, T = 2048, 768, 16, 4, 96
@@ -45,6 +47,7 @@ def _worker(rank, world, port, outdir):
     dist.broadcast(uid, 0)
     eng = M.MoeLayerEngine(M.MoeConfig(H, I, E, K, True, T, 1), device=rank)
     eng.ep_init(rank, world, bytes(uid.tolist()), owner)
+    assert eng.ep_transport() == transport, eng.ep_transport()
     loc = placement.local_experts(owner, rank)
     ex = torch.from_numpy(np.ascontiguousarray(lw.experts[loc])).cuda()
     sc = torch.from_numpy(np.ascontiguousarray(lw.scales[loc])).cuda()
@@ -52,7 +55,7 @@ def _worker(rank, world, port, outdir):
     eng.ep_set_layer(0, ex, sc, rt)
     hd = torch.from_numpy(h).cuda()
     out = torch.empty_like(hd)
-    for _ in range(2):  # twice: buffers are reused across calls
+    for _ in range(3):  # buffers and flags are reused across calls
         eng.ep_forward(0, hd, out)
         eng.sync_status()
     ep_out = out.cpu().numpy()
@@ -73,7 +76,8 @@ def _worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
-def test_expert_parallel_two_gpus_bit_exact():
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
+def test_expert_parallel_two_gpus_bit_exact(transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -81,7 +85,7 @@ def test_expert_parallel_two_gpus_bit_exact():
     from tests import helpers
     world = 2
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_worker, args=(world, _free_port(), d), nprocs=world,
+        mp.start_processes(_worker, args=(world, _free_port(), d, transport), nprocs=world,
                            start_method="spawn", join=True)
         lw = O.synth_layer(301, 0, 2048, 768, 16, 4, True)
         h_all = O.synth_hidden(302, 96 * world, 2048)

@@ -307,3 +307,28 @@ def test_route_tiled_ragged_shapes(bf16):
         assert np.array_equal(bits(probs.cpu().numpy()[t]), bits(p)), t
         assert np.array_equal(ids.cpu().numpy()[t].astype(np.uint32), rid), t
         assert np.array_equal(bits(gates.cpu().numpy()[t]), bits(rg)), t
+
+
+@pytest.mark.parametrize("T,E,K", [(600, 128, 8), (2100, 64, 4)])
+def test_route_permute_large_multi_cta(T, E, K):
+    """Route counts above 2048 take the multi-CTA permutation (tile
+    histograms, per-expert scan, scatter): same segments and the same
+    token-ascending order inside each expert as the oracle's expert_uses."""
+    lw = O.synth_layer(41, 0, 256, 128, E, K, False)
+    h = O.synth_hidden(41, T, 256)
+    ref = O.layer_forward(lw, h, nthreads=8)
+    eng = engine_for(lw, T)
+    ex, sc, rt = helpers.to_device(lw)
+    eng.set_layer_packed(0, ex, sc, rt)
+    hd = torch.from_numpy(h).cuda()
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    gates = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    seg = torch.empty(E + 1, dtype=torch.int32, device="cuda")
+    rtok = torch.empty(T * K, dtype=torch.int32, device="cuda")
+    rslot = torch.empty(T * K, dtype=torch.int32, device="cuda")
+    eng.route_permute(0, hd, ids, gates, seg, rtok, rslot)
+    torch.cuda.synchronize()
+    assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ref.ids)
+    assert np.array_equal(seg.cpu().numpy(), ref.seg_off)
+    assert np.array_equal(rtok.cpu().numpy(), ref.use_token)
+    assert np.array_equal(rslot.cpu().numpy(), ref.use_slot)
