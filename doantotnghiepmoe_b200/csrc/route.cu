@@ -89,13 +89,16 @@ __global__ void __launch_bounds__(kRouteThreads) route_logits_small_kernel(Route
   }
 }
 
-// Register-tiled logits for larger T.  A CTA covers 32 tokens x 16 experts;
-// thread (lane l, token group, expert group) owns lane l of the 8-lane chain
-// of 4 x 4 (token, expert) pairs, so each shared-memory load feeds four
-// multiply-adds and every chain still runs in chunk order.
-constexpr int kTT = 32, kTE = 16, kCW = 128;  // tokens, experts, columns per pass
-constexpr int kHStride = kCW + 2;             // padding: conflict-free token rows
+// Register-tiled logits for larger T.  A CTA covers kTT (32 or 16) tokens x
+// 16 experts; thread (lane l, token group, expert group) owns lane l of the
+// 8-lane chain of (kTT / 8) x 4 (token, expert) pairs, so each shared-memory
+// load feeds several multiply-adds and every chain still runs in chunk order.
+// The 16-token tile doubles the grid when 32-token tiles would leave SMs idle.
+constexpr int kTE = 16, kCW = 128;  // experts, columns per pass
+constexpr int kHStride = kCW + 2;   // padding: conflict-free token rows
+template <int kTT>
 __global__ void __launch_bounds__(256) route_logits_tiled_kernel(RouteArgs a) {
+  constexpr int kTG = kTT / 8;      // tokens per thread
   __shared__ float hs[kTT][kHStride];
   __shared__ float ws[kTE][kCW];
   const int tid = threadIdx.x;
@@ -103,9 +106,9 @@ __global__ void __launch_bounds__(256) route_logits_tiled_kernel(RouteArgs a) {
   const int tg = st & 7, eg = st >> 3;  // 8 token groups x 4 expert groups
   const int t0 = blockIdx.y * kTT, e0 = blockIdx.x * kTE;
   const int H = a.H, full = H / 8;
-  float acc[4][4];
+  float acc[kTG][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < kTG; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
   bool bad_input = false;
@@ -147,13 +150,13 @@ __global__ void __launch_bounds__(256) route_logits_tiled_kernel(RouteArgs a) {
     const int nchunk = ncol / 8;
 #pragma unroll 4
     for (int c = 0; c < nchunk; ++c) {
-      float hv[4], wv[4];
+      float hv[kTG], wv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) hv[i] = hs[4 * tg + i][8 * c + l];
+      for (int i = 0; i < kTG; ++i) hv[i] = hs[kTG * tg + i][8 * c + l];
 #pragma unroll
       for (int j = 0; j < 4; ++j) wv[j] = ws[4 * eg + j][8 * c + l];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < kTG; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[j], hv[i]));
     }
@@ -168,13 +171,13 @@ __global__ void __launch_bounds__(256) route_logits_tiled_kernel(RouteArgs a) {
   if (bad_input) set_status(a.status, kStatusNonFinite);
   const int base = (tid & 31) & ~7;
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < kTG; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float s = -0.0f;
 #pragma unroll
       for (int k = 0; k < 8; ++k) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc[i][j], base + k));
-      const int t = t0 + 4 * tg + i, e = e0 + 4 * eg + j;
+      const int t = t0 + kTG * tg + i, e = e0 + 4 * eg + j;
       if (l == 0 && t < a.T && e < a.E) {
         for (int c = full * 8; c < H; ++c)
           s = __fadd_rn(s, __fmul_rn(load_w(a.router, a.router_dtype, (size_t)e * H + c),
@@ -353,8 +356,12 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t s) {
   if (a.T <= 0) return cudaSuccess;
   const size_t small_smem = sizeof(float) * (size_t)(1 + kSmallTE) * a.H;
   if (a.T >= 16 && a.router_dtype != kRouterF32Seq) {
-    dim3 grid((a.E + kTE - 1) / kTE, (a.T + kTT - 1) / kTT);
-    route_logits_tiled_kernel<<<grid, 256, 0, s>>>(a);
+    const int ne = (a.E + kTE - 1) / kTE;
+    if ((long long)ne * ((a.T + 31) / 32) >= 2 * 148) {
+      route_logits_tiled_kernel<32><<<dim3(ne, (a.T + 31) / 32), 256, 0, s>>>(a);
+    } else {
+      route_logits_tiled_kernel<16><<<dim3(ne, (a.T + 15) / 16), 256, 0, s>>>(a);
+    }
   } else {
     if (small_smem > 48 * 1024)
       cudaFuncSetAttribute(route_logits_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
