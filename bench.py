@@ -276,8 +276,12 @@ def main():
     shares = np.bincount(ids.cpu().numpy().ravel(), minlength=E) / ids.numel()
     eng.sync_status(stream)
 
+    # warm-up: W steps, then one untimed pass over the timed steps' inputs so
+    # that every (layer, buffers) combination has its launch graph captured
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
+            step(i)
+        for i in range(args.steps):
             step(i)
     stream.synchronize()
     if world > 1:
@@ -286,8 +290,7 @@ def main():
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    eng.profile_read()
-    eng.profile(True)
+    eng.profile(False)
     launches = 0
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -297,12 +300,22 @@ def main():
             launches += eng.last_launch_count()
         ev1.record(stream)
     ev1.synchronize()
-    eng.profile(False)
-    prof = eng.profile_read()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
+    # kernel breakdown: the same steps again with CUDA events between the
+    # kernels (direct launches), for kernel_share and the roofline
+    eng.profile_read()
+    eng.profile(True)
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            step(i)
+    stream.synchronize()
+    eng.profile(False)
+    prof = eng.profile_read()
+    if world > 1:
+        dist.barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
     ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if world > 1:
@@ -443,7 +456,10 @@ def run_ep(args, cfg, rank, world, local):
     def step(i):
         eng.ep_forward(i % n_layers, hs[i % 2], outs[i % 2], stream=stream)
 
+    # warm-up, plus one untimed pass over the timed steps (launch graphs)
     for i in range(args.warmup):
+        step(i)
+    for i in range(args.steps):
         step(i)
     stream.synchronize()
     eng.sync_status(stream)
@@ -452,8 +468,7 @@ def run_ep(args, cfg, rank, world, local):
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    eng.profile_read()
-    eng.profile(True)
+    eng.profile(False)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches = 0
     ev0.record(stream)
@@ -462,10 +477,20 @@ def run_ep(args, cfg, rank, world, local):
         launches += eng.last_launch_count()
     ev1.record(stream)
     ev1.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    # kernel breakdown: the same steps with CUDA events between the kernels
+    # (all ranks start together, so no rank's first wait absorbs the skew)
+    torch.cuda.synchronize()
+    dist.barrier()
+    eng.profile_read()
+    eng.profile(True)
+    for i in range(args.steps):
+        step(i)
+    stream.synchronize()
     eng.profile(False)
     prof = eng.profile_read()
     dist.barrier()
-    clk = clocks.stop()
     ms = ev0.elapsed_time(ev1) / args.steps
     ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)

@@ -82,6 +82,7 @@ SIGNATURES = {
     "moe_ep_layer_forward": (I32, [P, I32, P, P, P, I32, P]),
     "moe_ep_finalize": (I32, [P]),
     "moe_ep_transport": (I32, [P]),
+    "moe_set_graphs": (I32, [P, I32]),
 }
 
 _lib = None

@@ -211,8 +211,10 @@ cudaError_t launch_seg_counts(const int32_t *seg, int n, int32_t *cnt, cudaStrea
 //      rank's [T, K, H] contribution buffer; flag C follows;
 //   5. combine: the source waits for flag C from every rank and sums the
 //      contributions in slot order.
-// Flags carry the call's epoch (monotonic), so nothing is ever reset.  Every
-// wait is bounded; on expiry the kernel records kStatusTimeout and moves on.
+// Flags carry the call's epoch (monotonic), so nothing is ever reset.  The
+// epoch lives in device memory and the publish kernel advances it, so a
+// captured sequence of these launches replays correctly.  Every wait is
+// bounded; on expiry the kernel records kStatusTimeout and moves on.
 // ---------------------------------------------------------------------------
 namespace moe {
 namespace {
@@ -235,7 +237,14 @@ __device__ __forceinline__ uint8_t *peer_at(const EpP2P &p, int rank, size_t off
 }
 
 __global__ void ep_publish_kernel(const int32_t *__restrict__ seg_off, int E, EpP2P p,
-                                  uint32_t epoch) {
+                                  uint32_t *epoch_p) {
+  __shared__ uint32_t ep_now;
+  if (threadIdx.x == 0) {
+    ep_now = *epoch_p + 1;
+    *epoch_p = ep_now;
+  }
+  __syncthreads();
+  const uint32_t epoch = ep_now;
   const int par = epoch & 1;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int32_t c = seg_off[e + 1] - seg_off[e];
@@ -283,9 +292,10 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const float *__restrict__ x, const int32_t *__restrict__ seg_off,
     const int32_t *__restrict__ r_token, const int32_t *__restrict__ r_slot,
     const float *__restrict__ r_gate, const int32_t *__restrict__ owner, int E, int R, int H,
-    EpP2P p, uint32_t epoch, uint32_t *done, uint32_t *status) {
+    EpP2P p, const uint32_t *epoch_p, uint32_t *done, uint32_t *status) {
   __shared__ int32_t tot[kMaxExperts], base[kMaxExperts], segs[kMaxExperts + 1];
   __shared__ int ok;
+  const uint32_t epoch = *epoch_p;
   if (threadIdx.x == 0) {
     ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
                            0 * kEpMaxRanks,
@@ -365,11 +375,13 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
 // One CTA: wait for every rank's routes, then this rank's expert segments
 // (local expert order) from the count matrix.
 __global__ void __launch_bounds__(256) ep_recv_prep_kernel(const int32_t *__restrict__ owner,
-                                                           int E, EpP2P p, uint32_t epoch,
+                                                           int E, EpP2P p,
+                                                           const uint32_t *epoch_p,
                                                            int32_t *seg_l, int32_t *active_l,
                                                            int32_t *n_active_l,
                                                            int32_t *n_recv, uint32_t *status) {
   __shared__ int ok;
+  const uint32_t epoch = *epoch_p;
   __shared__ int32_t tot[kMaxExperts];
   if (threadIdx.x == 0) {
     ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
@@ -403,7 +415,8 @@ __global__ void __launch_bounds__(256) ep_recv_prep_kernel(const int32_t *__rest
   }
 }
 
-__global__ void ep_signal_kernel(EpP2P p, uint32_t epoch) {
+__global__ void ep_signal_kernel(EpP2P p, const uint32_t *epoch_p) {
+  const uint32_t epoch = *epoch_p;
   __threadfence_system();
   for (int q = 0; q < p.nranks; ++q)
     reinterpret_cast<volatile uint32_t *>(peer_at(p, q, p.off_flags))[2 * kEpMaxRanks + p.rank] =
@@ -412,10 +425,11 @@ __global__ void ep_signal_kernel(EpP2P p, uint32_t epoch) {
 
 // out[t] = resid[t] (or 0) + contrib[t, 0] + ... + contrib[t, K-1], slot
 // order, once every rank's contributions are in.
-__global__ void ep_wait_combine_kernel(EpP2P p, uint32_t epoch, const float *__restrict__ resid,
-                                       float *__restrict__ out, int T, int K, int H,
-                                       uint32_t *status) {
+__global__ void ep_wait_combine_kernel(EpP2P p, const uint32_t *epoch_p,
+                                       const float *__restrict__ resid, float *__restrict__ out,
+                                       int T, int K, int H, uint32_t *status) {
   __shared__ int ok;
+  const uint32_t epoch = *epoch_p;
   if (threadIdx.x == 0) {
     ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
                            2 * kEpMaxRanks,
@@ -440,7 +454,7 @@ __global__ void ep_wait_combine_kernel(EpP2P p, uint32_t epoch, const float *__r
 
 }  // namespace
 
-cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uint32_t epoch,
+cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uint32_t *epoch,
                               cudaStream_t s) {
   ep_publish_kernel<<<1, 256, 0, s>>>(seg_off, E, p, epoch);
   return cudaGetLastError();
@@ -448,28 +462,29 @@ cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uin
 
 cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const int32_t *r_token,
                                const int32_t *r_slot, const float *r_gate, const int32_t *owner,
-                               int E, int R, int H, const EpP2P &p, uint32_t epoch,
+                               int E, int R, int H, const EpP2P &p, const uint32_t *epoch,
                                uint32_t *done, int grid, uint32_t *status, cudaStream_t s) {
   ep_dispatch_kernel<<<grid, 256, 0, s>>>(x, seg_off, r_token, r_slot, r_gate, owner, E, R, H, p,
                                           epoch, done, status);
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p, uint32_t epoch,
-                                int32_t *seg_l, int32_t *active_l, int32_t *n_active_l,
+cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p,
+                                const uint32_t *epoch, int32_t *seg_l, int32_t *active_l, int32_t *n_active_l,
                                 int32_t *n_recv, uint32_t *status, cudaStream_t s) {
   ep_recv_prep_kernel<<<1, 256, 0, s>>>(owner, E, p, epoch, seg_l, active_l, n_active_l, n_recv,
                                         status);
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_signal(const EpP2P &p, uint32_t epoch, cudaStream_t s) {
+cudaError_t launch_ep_signal(const EpP2P &p, const uint32_t *epoch, cudaStream_t s) {
   ep_signal_kernel<<<1, 1, 0, s>>>(p, epoch);
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_wait_combine(const EpP2P &p, uint32_t epoch, const float *resid, float *out,
-                                   int T, int K, int H, uint32_t *status, cudaStream_t s) {
+cudaError_t launch_ep_wait_combine(const EpP2P &p, const uint32_t *epoch, const float *resid,
+                                   float *out, int T, int K, int H, uint32_t *status,
+                                   cudaStream_t s) {
   const size_t n = (size_t)T * H;
   const int blocks = (int)std::max<size_t>(1, std::min<size_t>((n + 255) / 256, 148 * 8));
   ep_wait_combine_kernel<<<blocks, 256, 0, s>>>(p, epoch, resid, out, T, K, H, status);

@@ -174,18 +174,22 @@ struct EpP2P {
   size_t off_s1, off_s2, off_gate, off_rank, off_tok, off_slot, off_amax;  // [RR]
   size_t off_contrib;          // f32 [T, K, H] outputs of this rank's routes
 };
-cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uint32_t epoch,
+// epoch: this rank's call counter in device memory; the publish kernel
+// advances it, every later kernel of the call reads it.
+cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uint32_t *epoch,
                               cudaStream_t s);
 cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const int32_t *r_token,
                                const int32_t *r_slot, const float *r_gate, const int32_t *owner,
-                               int E, int R, int H, const EpP2P &p, uint32_t epoch,
+                               int E, int R, int H, const EpP2P &p, const uint32_t *epoch,
                                uint32_t *done, int grid, uint32_t *status, cudaStream_t s);
-cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p, uint32_t epoch,
-                                int32_t *seg_l, int32_t *active_l, int32_t *n_active_l,
-                                int32_t *n_recv, uint32_t *status, cudaStream_t s);
-cudaError_t launch_ep_signal(const EpP2P &p, uint32_t epoch, cudaStream_t s);
-cudaError_t launch_ep_wait_combine(const EpP2P &p, uint32_t epoch, const float *resid, float *out,
-                                   int T, int K, int H, uint32_t *status, cudaStream_t s);
+cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p,
+                                const uint32_t *epoch, int32_t *seg_l, int32_t *active_l,
+                                int32_t *n_active_l, int32_t *n_recv, uint32_t *status,
+                                cudaStream_t s);
+cudaError_t launch_ep_signal(const EpP2P &p, const uint32_t *epoch, cudaStream_t s);
+cudaError_t launch_ep_wait_combine(const EpP2P &p, const uint32_t *epoch, const float *resid,
+                                   float *out, int T, int K, int H, uint32_t *status,
+                                   cudaStream_t s);
 
 // Seeded synthetic expert weights, bit-identical to the host-side generator.
 cudaError_t launch_synth_expert(uint64_t seed, int layer, int expert, int H, int I, int8_t *w,

@@ -380,7 +380,7 @@ struct EpState {
   void *region = nullptr;           // this rank's peer-visible region
   std::vector<void *> peer_maps;    // opened peer regions (closed at finalize)
   EpP2P P{};
-  uint32_t epoch = 0;               // calls so far (flag values)
+  uint32_t *epoch = nullptr;        // device: calls so far (flag values)
   uint32_t *done = nullptr;         // dispatch completion counter (monotonic)
   int32_t *n_recv = nullptr;        // device count of received routes
   int dispatch_grid = 0;
@@ -428,6 +428,16 @@ struct moe_handle {
   unsigned long long *phase_ts = nullptr;  // [8] single-launch kernel phase stamps
   bool phase_pending = false;
   int phase_kind = 0;                      // 0: register-prefetch kernel, 1: streaming
+  // replayed launch sequences (see graphed())
+  struct GraphEntry {
+    uint64_t key[10];
+    cudaGraphExec_t exec;
+    int launches;
+    uint64_t last_use;
+  };
+  std::vector<GraphEntry> graphs;
+  uint64_t graph_clock = 0;
+  bool graphs_on = true;
   EpState ep;
 };
 
@@ -451,7 +461,13 @@ void free_ep(moe_handle *h) {
   ep.on = false;
 }
 
+void drop_graphs(moe_handle *h) {
+  for (auto &g : h->graphs) cudaGraphExecDestroy(g.exec);
+  h->graphs.clear();
+}
+
 void free_handle(moe_handle *h) {
+  drop_graphs(h);
   free_ep(h);
   for (auto &l : h->layers) {
     cudaFree(l.d_wptr);
@@ -476,6 +492,60 @@ cudaStream_t pick(moe_handle *h, void *stream) {
 moe_status cuda_fail(moe_handle *h, cudaError_t e, const char *what) {
   set_err(h->err, "%s: %s", what, cudaGetErrorString(e));
   return MOE_ERR_CUDA;
+}
+
+// Replay a call's launch sequence as a CUDA graph.  The sequence is captured
+// once per key (call kind, layer, token count, buffers, stream, path) and
+// replayed afterwards, which removes the host launch cost and most of the
+// gaps between the kernels.  Captures are only kept when every launch in the
+// sequence takes its sizes from device memory or from the key; the cache is
+// dropped whenever weights, path or routing mode change.  Profiling (events
+// between kernels) and a caller's own stream capture use direct launches.
+template <typename F>
+moe_status graphed(moe_handle *h, const uint64_t (&key)[10], cudaStream_t s, F &&launch_all) {
+  if (!h->graphs_on || h->prof.on) return launch_all();
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return launch_all();
+  }
+  for (auto &g : h->graphs) {
+    if (memcmp(g.key, key, sizeof key) != 0) continue;
+    g.last_use = ++h->graph_clock;
+    h->last_launches = g.launches;
+    const cudaError_t e = cudaGraphLaunch(g.exec, s);
+    return e == cudaSuccess ? MOE_OK : cuda_fail(h, e, "graph launch");
+  }
+  if (cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed) != cudaSuccess) {
+    cudaGetLastError();
+    return launch_all();
+  }
+  const moe_status st = launch_all();
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ec = cudaStreamEndCapture(s, &graph);
+  cudaGraphExec_t exec = nullptr;
+  const bool ok = st == MOE_OK && ec == cudaSuccess && graph &&
+                  cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+  if (graph) cudaGraphDestroy(graph);
+  if (!ok) {
+    cudaGetLastError();
+    if (st != MOE_OK) return st;
+    return launch_all();  // nothing ran during the failed capture
+  }
+  if (h->graphs.size() >= 32) {
+    auto old = std::min_element(h->graphs.begin(), h->graphs.end(),
+                                [](const auto &a, const auto &b) { return a.last_use < b.last_use; });
+    cudaGraphExecDestroy(old->exec);
+    h->graphs.erase(old);
+  }
+  moe_handle::GraphEntry g{};
+  memcpy(g.key, key, sizeof key);
+  g.exec = exec;
+  g.launches = h->last_launches;
+  g.last_use = ++h->graph_clock;
+  h->graphs.push_back(g);
+  const cudaError_t e = cudaGraphLaunch(exec, s);
+  return e == cudaSuccess ? MOE_OK : cuda_fail(h, e, "graph launch");
 }
 
 // Router + top-k + permutation for T tokens of `layer`.
@@ -845,6 +915,15 @@ extern "C" moe_status moe_set_stream(moe_handle *h, void *cuda_stream) {
   return MOE_OK;
 }
 
+extern "C" moe_status moe_set_graphs(moe_handle *h, int enable) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  DeviceGuard g(h->device);
+  drop_graphs(h);
+  h->graphs_on = enable != 0;
+  return MOE_OK;
+}
+
 extern "C" moe_status moe_set_route_mode(moe_handle *h, int mode) {
   if (!h || (mode != MOE_ROUTE_SOFTMAX_TOPK && mode != MOE_ROUTE_TOPK_SOFTMAX))
     return MOE_ERR_INVALID;
@@ -865,6 +944,7 @@ extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const 
                                     int router_dtype) {
   if (!h) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
+  drop_graphs(h);
   if (layer < 0 || layer >= (int)h->layers.size() || !d_weights || !d_scales || !d_router ||
       (router_dtype != MOE_ROUTER_F32 && router_dtype != MOE_ROUTER_BF16)) {
     set_err(h->err, "moe_set_layer: invalid argument");
@@ -935,6 +1015,7 @@ extern "C" moe_status moe_route(moe_handle *h, int layer, const float *d_h, int 
                                 uint32_t *d_ids, float *d_gates, float *d_probs, void *stream) {
   if (!h || !d_h || !d_ids || !d_gates) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
+  drop_graphs(h);
   moe_status st = check_layer(h, layer, T);
   if (st != MOE_OK || T == 0) return st;
   DeviceGuard g(h->device);
@@ -972,8 +1053,21 @@ extern "C" moe_status moe_layer_forward(moe_handle *h, int layer, const float *d
   if (st != MOE_OK || T == 0) return st;
   DeviceGuard g(h->device);
   h->last_launches = 0;
-  return layer_forward_locked(h, layer, d_h, d_resid, d_out, T, d_ids, d_gates, pick(h, stream));
+  cudaStream_t s = pick(h, stream);
+  // the streaming decode kernel alternates counter sets from the host: direct launches
+  if (h->path == MOE_PATH_GEMV_STREAM)
+    return layer_forward_locked(h, layer, d_h, d_resid, d_out, T, d_ids, d_gates, s);
+  const uint64_t key[10] = {1, (uint64_t)layer, (uint64_t)T, (uint64_t)d_h, (uint64_t)d_resid,
+                            (uint64_t)d_out, (uint64_t)d_ids, (uint64_t)d_gates, (uint64_t)s,
+                            (uint64_t)(h->path * 16 + h->route_mode)};
+  return graphed(h, key, s, [&] {
+    h->last_launches = 0;
+    return layer_forward_locked(h, layer, d_h, d_resid, d_out, T, d_ids, d_gates, s);
+  });
 }
+
+moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, float *d_x, int T,
+                                float rms_eps, cudaStream_t s);
 
 extern "C" moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_layers, float *d_x,
                                         int T, float rms_eps, void *stream) {
@@ -987,6 +1081,21 @@ extern "C" moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_la
   DeviceGuard g(h->device);
   cudaStream_t s = pick(h, stream);
   h->last_launches = 0;
+  if (h->path == MOE_PATH_GEMV_STREAM)
+    return stack_forward_locked(h, first_layer, n_layers, d_x, T, rms_eps, s);
+  uint32_t eps_bits;
+  memcpy(&eps_bits, &rms_eps, 4);
+  const uint64_t key[10] = {2, (uint64_t)first_layer, (uint64_t)n_layers, (uint64_t)T,
+                            (uint64_t)d_x, eps_bits, (uint64_t)s,
+                            (uint64_t)(h->path * 16 + h->route_mode), 0, 0};
+  return graphed(h, key, s, [&] {
+    h->last_launches = 0;
+    return stack_forward_locked(h, first_layer, n_layers, d_x, T, rms_eps, s);
+  });
+}
+
+moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, float *d_x, int T,
+                                float rms_eps, cudaStream_t s) {
   bool vec_all = ((uintptr_t)d_x & 15) == 0;
   for (int l = first_layer; l < first_layer + n_layers; ++l) vec_all = vec_all && h->layer_vec[l];
   if (h->path != MOE_PATH_TENSOR && use_fused(h, T)) {
@@ -1306,7 +1415,8 @@ void ep_setup_p2p(moe_handle *h, size_t Tm) {
   ok = ok && tc::encode_map3d(&ep.map_x64, xq, H, RR, 2, H, RR * H, 64) &&
        tc::encode_map3d(&ep.map_x128, xq, H, RR, 2, H, RR * H, 128) &&
        ep_alloc(ep, &ep.done, 1) && ep_alloc(ep, &ep.n_recv, 1) &&
-       cudaMemset(ep.done, 0, 4) == cudaSuccess;
+       ep_alloc(ep, &ep.epoch, 1) && cudaMemset(ep.done, 0, 4) == cudaSuccess &&
+       cudaMemset(ep.epoch, 0, 4) == cudaSuccess;
   if (!ok) {
     for (void *m : maps) cudaIpcCloseMemHandle(m);
     cudaFree(region);
@@ -1339,6 +1449,7 @@ extern "C" moe_status moe_ep_init(moe_handle *h, int rank, int nranks,
   if (!h || !id || !expert_owner || nranks < 1 || rank < 0 || rank >= nranks)
     return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
+  drop_graphs(h);
   if (!nccl().ok) {
     set_err(h->err, "libnccl.so.2 not available");
     return MOE_ERR_NCCL;
@@ -1426,6 +1537,7 @@ extern "C" moe_status moe_ep_finalize(moe_handle *h) {
   if (!h) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
   DeviceGuard g(h->device);
+  drop_graphs(h);
   free_ep(h);
   return MOE_OK;
 }
@@ -1436,6 +1548,7 @@ extern "C" moe_status moe_ep_set_layer(moe_handle *h, int layer, const int8_t *d
   if (!h || !d_router || (router_dtype != MOE_ROUTER_F32 && router_dtype != MOE_ROUTER_BF16))
     return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
+  drop_graphs(h);
   EpState &ep = h->ep;
   if (!ep.on || layer < 0 || layer >= (int)ep.layers.size()) {
     set_err(h->err, "moe_ep_set_layer: call moe_ep_init first / layer out of range");
@@ -1481,7 +1594,7 @@ moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const floa
   const LayerSlot &LS = h->layers[layer];
   const EpLayer &EL = ep.layers[layer];
   const EpP2P &P = ep.P;
-  const uint32_t epoch = ++ep.epoch;
+  uint32_t *epoch = ep.epoch;  // advanced on the device by the publish kernel
   cudaError_t e = cudaSuccess;
   // 1. route and bucket the local routes by global expert
   cudaEvent_t p0 = nullptr;
@@ -1605,7 +1718,14 @@ extern "C" moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float
   const EpLayer &EL = ep.layers[layer];
   cudaError_t e = cudaSuccess;
   moe_status st = MOE_OK;
-  if (ep.p2p) return ep_forward_p2p(h, layer, d_h, d_resid, d_out, T, s);
+  if (ep.p2p) {
+    const uint64_t key[10] = {3, (uint64_t)layer, (uint64_t)T, (uint64_t)d_h, (uint64_t)d_resid,
+                              (uint64_t)d_out, (uint64_t)s, (uint64_t)h->route_mode, 0, 0};
+    return graphed(h, key, s, [&] {
+      h->last_launches = 0;
+      return ep_forward_p2p(h, layer, d_h, d_resid, d_out, T, s);
+    });
+  }
   // 1. route the local tokens and bucket the routes by owner rank
   if (T > 0) {
     st = run_route(h, LS, d_h, T, h->ids, h->gates, nullptr, s, false);

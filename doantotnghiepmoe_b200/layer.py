@@ -162,6 +162,10 @@ class MoeLayerEngine:
         """'p2p' (kernels write into peer memory), 'nccl' or 'none'."""
         return {1: "p2p", 0: "nccl"}.get(lib().moe_ep_transport(self._h), "none")
 
+    def set_graphs(self, enable: bool):
+        """Replay each call's launch sequence as a CUDA graph (default on)."""
+        self._check(lib().moe_set_graphs(self._h, int(enable)))
+
     def profile(self, enable: bool):
         self._check(lib().moe_profile_enable(self._h, int(enable)))
 

@@ -116,6 +116,12 @@ enum {
 moe_status moe_create(int device, const moe_dims *dims, moe_handle **out);
 void moe_destroy(moe_handle *h);
 const char *moe_last_error(const moe_handle *h);
+/* Replay each call's launch sequence as a CUDA graph (default on).  The
+ * sequence is captured once per (call, layer, token count, buffers, stream,
+ * path) and replayed afterwards; captures are dropped when weights, path or
+ * routing mode change.  Calls run with direct launches while profiling is on,
+ * inside a caller's own stream capture, and on MOE_PATH_GEMV_STREAM. */
+moe_status moe_set_graphs(moe_handle *h, int enable);
 /* Default stream for calls that pass stream == NULL. */
 moe_status moe_set_stream(moe_handle *h, void *cuda_stream);
 moe_status moe_set_route_mode(moe_handle *h, int route_mode);
