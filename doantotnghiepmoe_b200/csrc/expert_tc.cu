@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "expert_tc.h"
@@ -420,6 +421,303 @@ __global__ void __launch_bounds__(kThreads, MINB)
 }
 
 // ---------------------------------------------------------------------------
+// Persistent variants: one CTA per SM walks the work items (route tile g,
+// 128-row weight tile m) with a stride of gridDim.x.  The producer's TMA
+// stages run on across work items; the MMA thread alternates between two
+// TMEM accumulator buffers, so the epilogue of one item overlaps the
+// mainloop of the next.  64-route tiles (two buffers of 4 x 64 columns for
+// gate/up, 2 x 64 for down).
+// ---------------------------------------------------------------------------
+constexpr int PBN = 64;
+
+struct PPipe {
+  uint64_t full[8];
+  uint64_t empty[8];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t done;
+  uint32_t tmem_base;
+  int abort_flag;
+  int consumed;
+};
+
+// Barrier among the four epilogue warps that ORs a predicate over them, so
+// every epilogue thread leaves the tile loop at the same item on an abort.
+__device__ __forceinline__ bool epi_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive_plain(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void psetup(PPipe &pp, int stages, uint32_t ncols) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&pp.full[s], 1);
+      mbar_init(&pp.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pp.tfull[b], 1);
+      mbar_init(&pp.tempty[b], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(&pp.done, 1);
+    pp.abort_flag = 0;
+    pp.consumed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if ((threadIdx.x >> 5) == 1) tmem_alloc(&pp.tmem_base, ncols);
+  __syncthreads();
+  fence_after_sync();
+}
+
+// Producer (warp 0, one thread) and MMA issuer (warp 1, one thread) of the
+// persistent kernels.  NA weight tiles (rows arow(m, a)) x NB digit tiles
+// per stage; accumulator (a, b) of buffer buf at TMEM column
+// buf * NA * NB * PBN + (a * NB + b) * PBN.
+template <int NA, int NB, int S, typename ARow>
+__device__ __forceinline__ void pmain(PPipe &pp, uint8_t *tiles, const CUtensorMap *mapA,
+                                      const CUtensorMap *mapB, const TcArgs &a, int nwork,
+                                      int nM, int nk, ARow arow) {
+  constexpr uint32_t kBTile = PBN * BK;
+  constexpr uint32_t kStageBytes = NA * kTileBytes + NB * kBTile;
+  constexpr uint32_t kIdesc = idesc_i8<PBN>();
+  constexpr uint32_t kBufCols = NA * NB * PBN;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0 && lane == 0) {
+    int q = 0;
+    for (int w = blockIdx.x; w < nwork; w += gridDim.x) {
+      const int g = w / nM, m = w % nM;
+      const int e = a.tile_expert[g], r0 = a.tile_row0[g];
+      for (int kb = 0; kb < nk; ++kb, ++q) {
+        const int s = q % S, use = q / S;
+        if (use > 0 && !mbar_wait(&pp.empty[s], (use - 1) & 1, &pp.abort_flag)) {
+          pp.abort_flag = 1;
+          break;
+        }
+        uint8_t *st = tiles + s * kStageBytes;
+        mbar_expect_tx(&pp.full[s], kStageBytes);
+#pragma unroll
+        for (int x = 0; x < NA; ++x)
+          tma_load_3d(st + x * kTileBytes, mapA, &pp.full[s], kb * BK, arow(m, x), e);
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+          tma_load_3d(st + NA * kTileBytes + b * kBTile, mapB, &pp.full[s], kb * BK, r0, b);
+      }
+      if (pp.abort_flag) break;
+    }
+    if (pp.abort_flag) {  // issued stages must land before the CTA may exit
+      const int from = *(volatile int *)&pp.consumed;
+      for (int k = from; k < q; ++k) mbar_wait(&pp.full[k % S], (k / S) & 1, nullptr);
+    }
+  } else if (warp == 1 && lane == 0) {
+    int q = 0, j = 0;
+    for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++j) {
+      const int buf = j & 1;
+      if (j >= 2 && !mbar_wait(&pp.tempty[buf], ((j >> 1) - 1) & 1, &pp.abort_flag)) {
+        pp.abort_flag = 1;
+        break;
+      }
+      fence_after_sync();
+      const uint32_t tmem = pp.tmem_base + (uint32_t)(buf * kBufCols);
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb, ++q) {
+        const int s = q % S;
+        if (!mbar_wait(&pp.full[s], (q / S) & 1, &pp.abort_flag)) {
+          pp.abort_flag = 1;
+          ok = false;
+          break;
+        }
+        fence_after_sync();
+        const uint32_t base = su32(tiles + s * kStageBytes);
+#pragma unroll
+        for (int k = 0; k < BK / UK; ++k) {
+#pragma unroll
+          for (int x = 0; x < NA; ++x) {
+            const uint64_t ad = sw128_desc(base + x * kTileBytes + k * UK);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+              const uint64_t bd = sw128_desc(base + NA * kTileBytes + b * kBTile + k * UK);
+              mma_i8(tmem + (uint32_t)((x * NB + b) * PBN), ad, bd, kIdesc,
+                     (kb > 0 || k > 0) ? 1u : 0u);
+            }
+          }
+        }
+        mma_commit(&pp.empty[s]);
+        pp.consumed = q + 1;
+      }
+      if (!ok) break;
+      mma_commit(&pp.tfull[buf]);
+    }
+    mma_commit(&pp.done);  // every MMA issued by this CTA has completed
+  }
+}
+
+__device__ __forceinline__ void pteardown(PPipe &pp, uint32_t ncols, uint32_t *status) {
+  if (threadIdx.x == 32) mbar_wait(&pp.done, 0, nullptr);  // no MMA still writes TMEM
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && pp.abort_flag) set_status(status, kStatusTimeout);
+  if ((threadIdx.x >> 5) == 1) tmem_dealloc(pp.tmem_base, ncols);
+}
+
+constexpr size_t psmem_bytes(int na, int nb, int stages) {
+  return 1024 + sizeof(PPipe) + 2 * sizeof(RouteTab) + 1024 +
+         (size_t)stages * (na * kTileBytes + nb * PBN * BK);
+}
+
+template <int S>
+__global__ void __launch_bounds__(kThreads, 1)
+    gate_up_tc_pkernel(const __grid_constant__ CUtensorMap mapW,
+                       const __grid_constant__ CUtensorMap mapX, TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  PPipe &pp = *reinterpret_cast<PPipe *>(smem_raw);
+  RouteTab *tabs = reinterpret_cast<RouteTab *>(smem_raw + sizeof(PPipe));
+  uint8_t *tiles = align1024(smem_raw + sizeof(PPipe) + 2 * sizeof(RouteTab));
+  const int nM = (a.I + BM - 1) / BM, nwork = *a.n_tiles * nM, nk = (a.H + BK - 1) / BK;
+  constexpr uint32_t kCols = 2 * 4 * PBN;
+  psetup(pp, S, kCols);
+  const int I = a.I;
+  pmain<2, 2, S>(pp, tiles, &mapW, &mapX, a, nwork, nM, nk,
+                 [I](int m, int x) { return x * I + m * BM; });
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp >= 2) {
+    const int qd = warp & 3;
+    int j = 0;
+    for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++j) {
+      const int buf = j & 1, g = w / nM, m = w % nM;
+      const int e = a.tile_expert[g], r0 = a.tile_row0[g], nr = a.tile_rows[g];
+      RouteTab &tab = tabs[buf];
+      const int i = m * BM + 32 * qd + lane;  // weight row of this thread
+      const float *Sc = a.s_ptr[e];
+      const float sg = i < I ? Sc[i] : 0.0f, su = i < I ? Sc[I + i] : 0.0f;
+      epi_sync();  // every epilogue warp is past the item that last used tab[buf]
+      for (int c = threadIdx.x - 64; c < nr; c += 128) {
+        tab.s1[c] = a.xs1[r0 + c];
+        tab.s2[c] = a.xs2[r0 + c];
+      }
+      epi_sync();
+      const bool ok = mbar_wait(&pp.tfull[buf], (j >> 1) & 1, &pp.abort_flag);
+      if (epi_any(!ok)) {  // uniform over the epilogue warps
+        pp.abort_flag = 1;
+        break;
+      }
+      fence_after_sync();
+      const uint32_t trow =
+          pp.tmem_base + (uint32_t)(buf * 4 * PBN) + ((uint32_t)(32 * qd) << 16);
+      for (int c0 = 0; c0 < PBN; c0 += 16) {
+        if (c0 >= nr) break;  // warp-uniform
+        int32_t v[4][16];
+#pragma unroll
+        for (int acc = 0; acc < 4; ++acc) tmem_ld16(trow + acc * PBN + c0, v[acc]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int c = c0 + jj;
+          float act = 0.0f;
+          if (c < nr) {
+            const int r = r0 + c;
+            const float s1 = tab.s1[c], s2 = tab.s2[c];
+            const float gd = fmaf(s1, (float)v[0][jj], s2 * (float)v[1][jj]);
+            const float ud = fmaf(s1, (float)v[2][jj], s2 * (float)v[3][jj]);
+            const float gg = gd * sg, uu = ud * su;
+            // tolerance path: the hardware exp (the GEMV path keeps libm's)
+            act = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
+            if (i < I) a.act[(size_t)r * I + i] = act;
+          }
+          float mx = fabsf(act);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          if (lane == 0 && c < nr) atomicMax(&a.act_amax[r0 + c], __float_as_uint(mx));
+        }
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_plain(&pp.tempty[buf]);
+    }
+  }
+  pteardown(pp, kCols, a.status);
+}
+
+template <int S>
+__global__ void __launch_bounds__(kThreads, 1)
+    down_tc_pkernel(const __grid_constant__ CUtensorMap mapW,
+                    const __grid_constant__ CUtensorMap mapA, TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  PPipe &pp = *reinterpret_cast<PPipe *>(smem_raw);
+  RouteTab *tabs = reinterpret_cast<RouteTab *>(smem_raw + sizeof(PPipe));
+  uint8_t *tiles = align1024(smem_raw + sizeof(PPipe) + 2 * sizeof(RouteTab));
+  const int nM = (a.H + BM - 1) / BM, nwork = *a.n_tiles * nM, nk = (a.I + BK - 1) / BK;
+  constexpr uint32_t kCols = 2 * 2 * PBN;
+  psetup(pp, S, kCols);
+  pmain<1, 2, S>(pp, tiles, &mapW, &mapA, a, nwork, nM, nk,
+                 [](int m, int) { return m * BM; });
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp >= 2) {
+    const int qd = warp & 3;
+    bool bad = false;
+    int j = 0;
+    for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++j) {
+      const int buf = j & 1, g = w / nM, m = w % nM;
+      const int e = a.tile_expert[g], r0 = a.tile_row0[g], nr = a.tile_rows[g];
+      RouteTab &tab = tabs[buf];
+      const int jr = m * BM + 32 * qd + lane;  // output row (hidden index)
+      const float sd = jr < a.H ? a.s_ptr[e][2 * a.I + jr] : 0.0f;
+      epi_sync();
+      for (int c = threadIdx.x - 64; c < nr; c += 128) {
+        const int r = r0 + c;
+        tab.s1[c] = a.as1[r];
+        tab.s2[c] = a.as2[r];
+        tab.gate[c] = a.r_gate[r];
+        tab.tok[c] = a.r_token[r];
+        tab.slot[c] = a.r_slot[r];
+        tab.rank[c] = a.r_rank ? a.r_rank[r] : 0;
+      }
+      epi_sync();
+      const bool ok = mbar_wait(&pp.tfull[buf], (j >> 1) & 1, &pp.abort_flag);
+      if (epi_any(!ok)) {  // uniform over the epilogue warps
+        pp.abort_flag = 1;
+        break;
+      }
+      fence_after_sync();
+      const uint32_t trow =
+          pp.tmem_base + (uint32_t)(buf * 2 * PBN) + ((uint32_t)(32 * qd) << 16);
+      for (int c0 = 0; c0 < PBN; c0 += 16) {
+        if (c0 >= nr) break;
+        int32_t v[2][16];
+        tmem_ld16(trow + c0, v[0]);
+        tmem_ld16(trow + PBN + c0, v[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int c = c0 + jj;
+          if (c < nr && jr < a.H) {
+            const float y = fmaf(tab.s1[c], (float)v[0][jj], tab.s2[c] * (float)v[1][jj]) * sd;
+            bad |= !is_finite_f(y);
+            float *dst = a.r_rank ? a.peer_contrib[tab.rank[c]] : a.contrib;
+            dst[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + jr] = __fmul_rn(tab.gate[c], y);
+          }
+        }
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_plain(&pp.tempty[buf]);
+    }
+    if (bad) set_status(a.status, kStatusNonFinite);
+  }
+  pteardown(pp, kCols, a.status);
+}
+
+// ---------------------------------------------------------------------------
 // Tile table and activation digit planes
 // ---------------------------------------------------------------------------
 // Tile table: tile t of the layer covers routes [row0, row0 + rows) of one
@@ -557,6 +855,27 @@ cudaError_t launch_quantize_rows(const float *src, const int32_t *rows, const ui
   return cudaGetLastError();
 }
 
+// Persistent tile loop with double-buffered accumulators for 64-route tiles
+// (MOE_TC_PERSISTENT=1); by default one CTA per tile.
+bool persistent_tc() {
+  static int v = -1;
+  if (v < 0) {
+    const char *env = getenv("MOE_TC_PERSISTENT");
+    v = (env && env[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+int tc_bn_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char *env = getenv("MOE_TC_BN");
+    v = env ? atoi(env) : 0;
+    if (v != 64 && v != 128) v = 0;
+  }
+  return v;
+}
+
 // Tile configurations.  BN = 64: 2 CTAs per SM (TMEM 4*64 and 2*64 columns,
 // 96 KB of pipeline each).  BN = 128: gate/up one CTA per SM (512 TMEM
 // columns, 3 stages), down two per SM.
@@ -582,14 +901,46 @@ cudaError_t launch_dn(const CUtensorMap &mapW, const CUtensorMap &mapA, const Tc
   return cudaGetLastError();
 }
 
+// Persistent kernels: one CTA per SM (at most one per work item).
+int sm_count_cached() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+constexpr int kPStagesGU = 4, kPStagesDN = 6;
+
 cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
                               int bn, int max_tiles, cudaStream_t s) {
+  if (bn == PBN && persistent_tc()) {
+    const size_t smem = psmem_bytes(2, 2, kPStagesGU);
+    auto k = gate_up_tc_pkernel<kPStagesGU>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const long long work = (long long)max_tiles * ((a.I + BM - 1) / BM);
+    const int grid = (int)std::min<long long>(sm_count_cached(), std::max<long long>(work, 1));
+    k<<<grid, kThreads, smem, s>>>(mapW, mapX, a);
+    return cudaGetLastError();
+  }
   return bn == 64 ? launch_gu<64, 2, 2>(mapW, mapX, a, max_tiles, s)
                   : launch_gu<128, 3, 1>(mapW, mapX, a, max_tiles, s);
 }
 
 cudaError_t launch_down_tc(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
                            int bn, int max_tiles, cudaStream_t s) {
+  if (bn == PBN && persistent_tc()) {
+    const size_t smem = psmem_bytes(1, 2, kPStagesDN);
+    auto k = down_tc_pkernel<kPStagesDN>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const long long work = (long long)max_tiles * ((a.H + BM - 1) / BM);
+    const int grid = (int)std::min<long long>(sm_count_cached(), std::max<long long>(work, 1));
+    k<<<grid, kThreads, smem, s>>>(mapW, mapA, a);
+    return cudaGetLastError();
+  }
   return bn == 64 ? launch_dn<64, 3, 2>(mapW, mapA, a, max_tiles, s)
                   : launch_dn<128, 2, 2>(mapW, mapA, a, max_tiles, s);
 }

@@ -10,9 +10,20 @@
 namespace moe {
 namespace tc {
 
-// Routes per GEMM tile: 64 when experts average few routes (prefill of a
-// few hundred tokens), 128 otherwise.
-inline int tc_block_n(int routes, int experts) { return routes <= 96 * experts ? 64 : 128; }
+bool persistent_tc();
+int tc_bn_override();  // MOE_TC_BN (64 or 128), 0 when unset
+
+// Routes per GEMM tile: 64.  Measured on B200 (OLMoE T=512, Qwen3 T=4096),
+// 64-route tiles with two CTAs per SM beat 128-route tiles at both sizes:
+// two independent pipelines per SM overlap one CTA's epilogue with the
+// other's mainloop.  MOE_TC_BN=128 restores the wide tile.
+inline int tc_block_n(int routes, int experts) {
+  (void)routes;
+  (void)experts;
+  if (persistent_tc()) return 64;
+  if (const int o = tc_bn_override()) return o;
+  return 64;
+}
 
 struct TcArgs {
   int H, I, K;
