@@ -332,20 +332,28 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
       const float inv = 1.0f / s;
       uint8_t *qbase = peer_at(p, q, p.off_xq);
       uint8_t *d1 = qbase + pos * H, *d2 = qbase + p.plane + pos * H;
-      for (int c = lane * 4; c < H; c += 128) {
-        const float4 v = *reinterpret_cast<const float4 *>(xr + c);
-        const float in[4] = {v.x, v.y, v.z, v.w};
-        uint32_t p1 = 0, p2 = 0;
+      // 16 elements per lane per pass: 16-byte stores, 512 bytes per warp
+      // instruction on the link (H is a multiple of 16)
+      for (int c = lane * 16; c < H; c += 512) {
+        uint32_t p1[4], p2[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float qv = in[k] * inv;
-          const float a1 = fminf(fmaxf(rintf(qv), -127.0f), 127.0f);
-          const float a2 = fminf(fmaxf(rintf((qv - a1) * 254.0f), -127.0f), 127.0f);
-          p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
-          p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
+        for (int w4 = 0; w4 < 4; ++w4) {
+          const float4 v = *reinterpret_cast<const float4 *>(xr + c + 4 * w4);
+          const float in[4] = {v.x, v.y, v.z, v.w};
+          uint32_t b1 = 0, b2 = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float qv = in[k] * inv;
+            const float a1 = fminf(fmaxf(rintf(qv), -127.0f), 127.0f);
+            const float a2 = fminf(fmaxf(rintf((qv - a1) * 254.0f), -127.0f), 127.0f);
+            b1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
+            b2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
+          }
+          p1[w4] = b1;
+          p2[w4] = b2;
         }
-        *reinterpret_cast<uint32_t *>(d1 + c) = p1;
-        *reinterpret_cast<uint32_t *>(d2 + c) = p2;
+        *reinterpret_cast<uint4 *>(d1 + c) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+        *reinterpret_cast<uint4 *>(d2 + c) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
       }
       if (lane == 0) {
         reinterpret_cast<float *>(peer_at(p, q, p.off_s1))[pos] = s;

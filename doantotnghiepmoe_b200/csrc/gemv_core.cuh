@@ -26,12 +26,16 @@ constexpr int kTG = 4;              // tokens per pass
 constexpr int kGURowsPerWarp = 4;   // gate/up: 8 lanes per row (4 gate + 4 up banks)
 constexpr int kDNRowsPerWarp = 8;   // down: 4 lanes per row
 
-// Streaming 8-byte weight load: read once, never reused by this CTA.
+// Streaming 8-byte weight load: read once, never reused by this CTA, and
+// marked evict-first in L2 so the stream does not push the kernel's code,
+// the routers or the activations out of L2.
 __device__ __forceinline__ uint2 ldg_stream8(const int8_t *p) {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0, %1}, [%2], %3;"
                : "=r"(v.x), "=r"(v.y)
-               : "l"(p));
+               : "l"(p), "l"(pol));
   return v;
 }
 
