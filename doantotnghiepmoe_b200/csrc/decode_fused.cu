@@ -273,22 +273,41 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
   const int nseg = tb.n_active;
   const int nb_gu = (I + kGURowsItem - 1) / kGURowsItem;
   const int nb_dn = (H + kDNRowsItem - 1) / kDNRowsItem;
-  // Bulk L2 prefetch of every weight block this CTA will stream.
-  if (threadIdx.x == 0 && L.prefetch_ok) {
-    for (int item = blockIdx.x; item < nseg * nb_gu; item += G) {
-      const int e = tb.active[item / nb_gu], row0 = (item % nb_gu) * kGURowsItem;
-      const int rows = min(kGURowsItem, I - row0);
-      const int8_t *W = L.w_ptr[e];
-      prefetch_l2(W + (size_t)row0 * H, (uint32_t)rows * H);
-      prefetch_l2(W + (size_t)(I + row0) * H, (uint32_t)rows * H);
-    }
-    for (int item = blockIdx.x; item < nseg * nb_dn; item += G) {
-      const int e = tb.active[item / nb_dn], row0 = (item % nb_dn) * kDNRowsItem;
-      const int rows = min(kDNRowsItem, H - row0);
-      prefetch_l2(L.w_ptr[e] + (size_t)2 * I * H + (size_t)row0 * I, (uint32_t)rows * I);
-    }
+  // Bulk L2 prefetch of the weight blocks this CTA will stream: all of them
+  // up front when the layer's active experts fit comfortably in L2 (batch-1
+  // decode), otherwise two items ahead of use (larger batches would evict
+  // their own prefetches).
+  const bool all_up_front = (size_t)nseg * 3 * I * H <= ((size_t)64 << 20);
+  auto pf_gu = [&](int item) {
+    if (threadIdx.x != 0 || !L.prefetch_ok || item >= nseg * nb_gu) return;
+    const int e = tb.active[item / nb_gu], row0 = (item % nb_gu) * kGURowsItem;
+    const int rows = min(kGURowsItem, I - row0);
+    const int8_t *W = L.w_ptr[e];
+    prefetch_l2(W + (size_t)row0 * H, (uint32_t)rows * H);
+    prefetch_l2(W + (size_t)(I + row0) * H, (uint32_t)rows * H);
+  };
+  auto pf_dn = [&](int item) {
+    if (threadIdx.x != 0 || !L.prefetch_ok || item >= nseg * nb_dn) return;
+    const int e = tb.active[item / nb_dn], row0 = (item % nb_dn) * kDNRowsItem;
+    const int rows = min(kDNRowsItem, H - row0);
+    prefetch_l2(L.w_ptr[e] + (size_t)2 * I * H + (size_t)row0 * I, (uint32_t)rows * I);
+  };
+  if (all_up_front) {
+    for (int item = blockIdx.x; item < nseg * nb_gu; item += G) pf_gu(item);
+    for (int item = blockIdx.x; item < nseg * nb_dn; item += G) pf_dn(item);
+  } else {
+    pf_gu(blockIdx.x);
+    pf_gu(blockIdx.x + G);
   }
   for (int item = blockIdx.x; item < nseg * nb_gu; item += G) {
+    if (!all_up_front) {
+      pf_gu(item + 2 * G);
+      // the first down items of this CTA go out during its last gate/up item
+      if (item + G >= nseg * nb_gu) {
+        pf_dn(blockIdx.x);
+        pf_dn(blockIdx.x + G);
+      }
+    }
     const int e = tb.active[item / nb_gu];
     const int r0 = tb.seg_off[e], r1 = tb.seg_off[e + 1];
     const int row0 = (item % nb_gu) * kGURowsItem;
@@ -307,6 +326,7 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
   stamp(a, 2);
   bool good = true;
   for (int item = blockIdx.x; item < nseg * nb_dn; item += G) {
+    if (!all_up_front) pf_dn(item + 2 * G);
     const int e = tb.active[item / nb_dn];
     const int r0 = tb.seg_off[e], r1 = tb.seg_off[e + 1];
     const int row0 = (item % nb_dn) * kDNRowsItem;
