@@ -29,7 +29,8 @@ struct RouteArgs {
   float *probs;         // optional [T, E] post-softmax probabilities
   uint32_t *status;
 };
-cudaError_t launch_route(const RouteArgs &a, cudaStream_t s);
+// `launches` (optional) receives the number of kernels enqueued.
+cudaError_t launch_route(const RouteArgs &a, cudaStream_t s, int *launches = nullptr);
 
 // Stable bucket of routes by expert (src/olmoe.rs:3474-3480): experts in
 // ascending id, tokens ascending inside an expert.

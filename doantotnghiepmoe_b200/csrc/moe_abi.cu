@@ -405,6 +405,8 @@ struct moe_handle {
   int32_t *seg_off = nullptr, *active = nullptr, *n_active = nullptr, *r_token = nullptr,
           *r_slot = nullptr, *r_pos = nullptr;
   float *h_pin_in = nullptr, *h_pin_out = nullptr;
+  uint32_t *h_pin_status = nullptr;
+  cudaEvent_t stage_ev[16] = {};  // chunked staging of pageable host outputs
   int last_launches = 0;
   Profiler prof;
   // tensor-core path scratch
@@ -482,6 +484,9 @@ void free_handle(moe_handle *h) {
   for (void *p : ptrs) cudaFree(p);
   cudaFreeHost(h->h_pin_in);
   cudaFreeHost(h->h_pin_out);
+  cudaFreeHost(h->h_pin_status);
+  for (auto ev : h->stage_ev)
+    if (ev) cudaEventDestroy(ev);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
 }
 
@@ -569,10 +574,11 @@ moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T,
   ra.probs = probs;
   ra.status = h->status;
   cudaEvent_t p0 = h->prof.begin(s);
-  cudaError_t e = launch_route(ra, s);
+  int nl = 0;
+  cudaError_t e = launch_route(ra, s, &nl);
   h->prof.end("route", p0, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "route launch");
-  h->last_launches += 2;
+  h->last_launches += nl;
   if (!permute) return MOE_OK;
   PermuteArgs pa{};
   pa.ids = ids;
@@ -856,6 +862,7 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && dalloc(&h->status, 1) == cudaSuccess;
   ok = ok && cudaMallocHost(&h->h_pin_in, 2 * T * H * sizeof(float)) == cudaSuccess;
   ok = ok && cudaMallocHost(&h->h_pin_out, T * H * sizeof(float)) == cudaSuccess;
+  ok = ok && cudaMallocHost(&h->h_pin_status, 64) == cudaSuccess;
   ok = ok && cudaMemset(h->status, 0, 4) == cudaSuccess;
   // tensor-core path scratch and the activation-side tensor maps
   const size_t R = T * K;
@@ -1131,16 +1138,7 @@ moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, fl
   return MOE_OK;
 }
 
-extern "C" moe_status moe_sync_status(moe_handle *h, void *stream) {
-  if (!h) return MOE_ERR_INVALID;
-  std::lock_guard<std::mutex> lock(h->mu);
-  DeviceGuard g(h->device);
-  cudaStream_t s = pick(h, stream);
-  uint32_t st = 0;
-  cudaError_t e = cudaMemcpyAsync(&st, h->status, 4, cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return cuda_fail(h, e, "sync_status");
-  if (st) cudaMemsetAsync(h->status, 0, 4, s);
+static moe_status status_error(moe_handle *h, uint32_t st) {
   if (st & kStatusTimeout) {
     set_err(h->err, "device wait timed out");
     return MOE_ERR_TIMEOUT;
@@ -1156,6 +1154,54 @@ extern "C" moe_status moe_sync_status(moe_handle *h, void *stream) {
   return MOE_OK;
 }
 
+extern "C" moe_status moe_sync_status(moe_handle *h, void *stream) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  DeviceGuard g(h->device);
+  cudaStream_t s = pick(h, stream);
+  uint32_t st = 0;
+  cudaError_t e = cudaMemcpyAsync(&st, h->status, 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(h, e, "sync_status");
+  if (st) cudaMemsetAsync(h->status, 0, 4, s);
+  return status_error(h, st);
+}
+
+// Host memory that the CUDA driver has pinned (cudaHostAlloc, cudaHostRegister,
+// torch pin_memory) can be read and written by the copy engines directly.
+static bool host_is_pinned(const void *p) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return at.type == cudaMemoryTypeHost;
+}
+
+// Pageable buffers are staged through the handle's pinned buffers in chunks,
+// so the host copy of one chunk overlaps the DMA of the previous one.
+static constexpr size_t kStageChunk = 1u << 20;
+static constexpr int kStageEvents = 16;
+
+static size_t stage_chunk(size_t bytes) {
+  return std::max(kStageChunk, ((bytes + kStageEvents - 1) / kStageEvents + 255) & ~(size_t)255);
+}
+
+static void h2d(void *dst, const void *src, size_t bytes, void *pin, bool pinned,
+                cudaStream_t s) {
+  if (pinned) {
+    cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s);
+    return;
+  }
+  const size_t c = stage_chunk(bytes);
+  for (size_t o = 0; o < bytes; o += c) {
+    const size_t n = std::min(c, bytes - o);
+    memcpy(static_cast<char *>(pin) + o, static_cast<const char *>(src) + o, n);
+    cudaMemcpyAsync(static_cast<char *>(dst) + o, static_cast<char *>(pin) + o, n,
+                    cudaMemcpyHostToDevice, s);
+  }
+}
+
 extern "C" moe_status moe_layer_forward_host(moe_handle *h, int layer, const float *h_in,
                                              const float *h_resid, float *h_out, int T,
                                              uint32_t *h_ids, float *h_gates) {
@@ -1169,24 +1215,56 @@ extern "C" moe_status moe_layer_forward_host(moe_handle *h, int layer, const flo
     cudaStream_t s = h->stream;
     const size_t n = (size_t)T * h->d.hidden;
     const size_t R = (size_t)T * h->d.top_k;
-    memcpy(h->h_pin_in, h_in, n * sizeof(float));
-    cudaMemcpyAsync(h->io_in, h->h_pin_in, n * sizeof(float), cudaMemcpyHostToDevice, s);
-    if (h_resid) {
-      memcpy(h->h_pin_in + n, h_resid, n * sizeof(float));
-      cudaMemcpyAsync(h->io_resid, h->h_pin_in + n, n * sizeof(float), cudaMemcpyHostToDevice, s);
-    }
+    const size_t bytes = n * sizeof(float);
+    h2d(h->io_in, h_in, bytes, h->h_pin_in, host_is_pinned(h_in), s);
+    if (h_resid) h2d(h->io_resid, h_resid, bytes, h->h_pin_in + n, host_is_pinned(h_resid), s);
     h->last_launches = 0;
     st = layer_forward_locked(h, layer, h->io_in, h_resid ? h->io_resid : nullptr, h->io_out, T,
                               h->ids, h->gates, s);
     if (st != MOE_OK) return st;
-    cudaMemcpyAsync(h->h_pin_out, h->io_out, n * sizeof(float), cudaMemcpyDeviceToHost, s);
-    if (h_ids) cudaMemcpyAsync(h_ids, h->ids, R * 4, cudaMemcpyDeviceToHost, s);
-    if (h_gates) cudaMemcpyAsync(h_gates, h->gates, R * 4, cudaMemcpyDeviceToHost, s);
-    cudaError_t e = cudaStreamSynchronize(s);
+    // the status word travels back with the outputs and is cleared behind
+    // them, so the call needs one stream synchronisation
+    auto status_back = [&] {
+      cudaMemcpyAsync(h->h_pin_status, h->status, 4, cudaMemcpyDeviceToHost, s);
+      cudaMemsetAsync(h->status, 0, 4, s);
+    };
+    cudaError_t e = cudaSuccess;
+    if (host_is_pinned(h_out)) {
+      cudaMemcpyAsync(h_out, h->io_out, bytes, cudaMemcpyDeviceToHost, s);
+      if (h_ids) cudaMemcpyAsync(h_ids, h->ids, R * 4, cudaMemcpyDeviceToHost, s);
+      if (h_gates) cudaMemcpyAsync(h_gates, h->gates, R * 4, cudaMemcpyDeviceToHost, s);
+      status_back();
+      e = cudaStreamSynchronize(s);
+    } else {
+      // chunk i is copied out on the host while chunk i + 1 is in flight
+      if (!h->stage_ev[0])
+        for (auto &ev : h->stage_ev) cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+      const size_t c = stage_chunk(bytes);
+      int nc = 0;
+      for (size_t o = 0; o < bytes; o += c, ++nc) {
+        cudaMemcpyAsync(reinterpret_cast<char *>(h->h_pin_out) + o,
+                        reinterpret_cast<char *>(h->io_out) + o, std::min(c, bytes - o),
+                        cudaMemcpyDeviceToHost, s);
+        cudaEventRecord(h->stage_ev[nc], s);
+      }
+      status_back();
+      for (int i = 0; i < nc && e == cudaSuccess; ++i) {
+        e = cudaEventSynchronize(h->stage_ev[i]);
+        const size_t o = (size_t)i * c;
+        if (e == cudaSuccess)
+          memcpy(reinterpret_cast<char *>(h_out) + o,
+                 reinterpret_cast<char *>(h->h_pin_out) + o, std::min(c, bytes - o));
+      }
+      if (e == cudaSuccess && h_ids)
+        e = cudaMemcpyAsync(h_ids, h->ids, R * 4, cudaMemcpyDeviceToHost, s);
+      if (e == cudaSuccess && h_gates)
+        e = cudaMemcpyAsync(h_gates, h->gates, R * 4, cudaMemcpyDeviceToHost, s);
+      cudaError_t e2 = cudaStreamSynchronize(s);
+      if (e == cudaSuccess) e = e2;
+    }
     if (e != cudaSuccess) return cuda_fail(h, e, "layer_forward_host");
-    memcpy(h_out, h->h_pin_out, n * sizeof(float));
+    return status_error(h, *h->h_pin_status);
   }
-  return moe_sync_status(h, nullptr);
 }
 
 extern "C" int moe_last_launch_count(const moe_handle *h) { return h ? h->last_launches : 0; }

@@ -13,6 +13,8 @@
 //            ascending within an expert).
 // Every floating-point step is the same IEEE operation in the same order, so
 // logits, probabilities, ids and gates are bit-identical to the CPU path.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "route_core.cuh"
@@ -188,6 +190,181 @@ __global__ void __launch_bounds__(256) route_logits_tiled_kernel(RouteArgs a) {
     }
 }
 
+// Pipelined, register-blocked logits for f32 routers (H % 4 == 0, 16-byte
+// aligned rows).  A thread owns lane l of the 8-lane chain of a PT x PE block
+// of (token, expert) pairs, so each shared-memory word it loads feeds PE (or
+// PT) multiply-adds: at PT = PE = 8 the shared-memory traffic per
+// multiply-add is half that of a 4 x 4 block, and the FP32 pipe, not shared
+// memory, bounds the kernel.  The 32 groups of 8 threads form 8 token groups
+// x 4 expert groups; token (i, tg) is row 8 i + tg of the tile and expert
+// (j, ge) is row 4 j + ge, so the four groups of a warp read four adjacent
+// token rows (row stride = 8 words mod 32: no bank conflicts) and one shared
+// expert row (a broadcast).  Columns arrive in 64-wide stages through a
+// kStages-deep cp.async ring; columns past the last full chunk of 8 are zero
+// filled (0 * 0 added to a lane sum that cannot be -0.0 leaves it unchanged)
+// and folded after the chains, in the reference order.
+//
+// Non-finite input needs no separate scan: a non-finite h[t][c] makes the
+// product in its lane chain, and so the logit of every expert for token t,
+// non-finite, and the logit check below records it.
+template <int PT, int PE, int CW, int S, int NT>
+struct PipeTile {
+  static constexpr int GE = NT / 64;  // expert groups (8 token groups)
+  static constexpr int TT = 8 * PT, TE = GE * PE;
+  static constexpr int kStride = CW + 8;  // words per smem row (= 8 mod 32)
+  static constexpr int kStageWords = (TT + TE) * kStride;
+  static constexpr int kRedWords = TT * TE * 9;
+  static constexpr size_t kSmem =
+      sizeof(float) * (size_t)(kStageWords * S > kRedWords ? kStageWords * S : kRedWords);
+};
+
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const float *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+// CW columns per stage, an S-deep ring, NT threads: small blocks (little
+// compute per stage) take wider stages, a deeper ring and 128-thread CTAs so
+// that the copies in flight cover the memory latency and the grid covers
+// every SM.  Each thread's copy rows and column are fixed for the whole
+// kernel (row rb + k * (NT / (CW / 4)), column 4 * qc of every stage), so a
+// copy costs a pointer add and a predicate.
+template <int PT, int PE, int CW, int S, int NT>
+__global__ void __launch_bounds__(NT, PT * PE >= 64 ? 2 : 4)
+    route_logits_pipe_kernel(RouteArgs a) {
+  using Tile = PipeTile<PT, PE, CW, S, NT>;
+  constexpr int TT = Tile::TT, TE = Tile::TE, kStride = Tile::kStride;
+  constexpr int kQuads = CW / 4;               // 16-byte copies per row and stage
+  constexpr int kRowsPer = NT / kQuads;        // rows one pass of the CTA covers
+  constexpr int kNK = (TT + TE + kRowsPer - 1) / kRowsPer;
+  static_assert(NT % kQuads == 0, "copy layout");
+  extern __shared__ __align__(16) float psm[];
+  const int tid = threadIdx.x;
+  const int l = tid & 7, grp = tid >> 3;
+  const int tg = grp & 7, ge = grp >> 3;
+  const int t0 = blockIdx.y * TT, e0 = blockIdx.x * TE;
+  const int H = a.H, full = H / 8, ncols = full * 8;
+  const float *W = static_cast<const float *>(a.router);
+  const int nstage = (ncols + CW - 1) / CW;
+
+  const int rb = tid / kQuads, qc = tid % kQuads;
+  const float *src[kNK];
+  uint32_t rowok = 0;
+#pragma unroll
+  for (int k = 0; k < kNK; ++k) {
+    const int r = rb + k * kRowsPer;
+    bool ok;
+    if (r < TT) {
+      ok = t0 + r < a.T;
+      src[k] = a.h + (size_t)(ok ? t0 + r : 0) * H + 4 * qc;
+    } else {
+      ok = r < TT + TE && e0 + r - TT < a.E;
+      src[k] = W + (size_t)(ok ? e0 + r - TT : 0) * H + 4 * qc;
+    }
+    rowok |= (ok ? 1u : 0u) << k;
+  }
+  const uint32_t dst0 = (uint32_t)__cvta_generic_to_shared(psm) + 4u * (rb * kStride + 4 * qc);
+
+  auto issue = [&](int st) {
+    const uint32_t dst = dst0 + 4u * (st % S) * Tile::kStageWords;
+    const int c0 = st * CW;
+    const bool colok = c0 + 4 * qc < ncols;
+#pragma unroll
+    for (int k = 0; k < kNK; ++k) {
+      if (kNK * kRowsPer > TT + TE && rb + k * kRowsPer >= TT + TE) break;
+      const bool ok = colok && ((rowok >> k) & 1u);
+      cp_async16_zfill(dst + 4u * k * kRowsPer * kStride, ok ? src[k] + c0 : src[k], ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  float acc[PT][PE];
+#pragma unroll
+  for (int i = 0; i < PT; ++i)
+#pragma unroll
+    for (int j = 0; j < PE; ++j) acc[i][j] = 0.0f;  // `[0.0f32; 8]`, src/backend.rs:107
+
+#pragma unroll
+  for (int st = 0; st < S - 1; ++st) {
+    if (st < nstage) issue(st);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (int st = 0; st < nstage; ++st) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(S - 2) : "memory");
+    __syncthreads();  // stage st visible; stage st - 1 fully consumed
+    if (st + S - 1 < nstage) issue(st + S - 1);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    const float *hs = psm + (st % S) * Tile::kStageWords + tg * kStride + l;
+    const float *ws = psm + (st % S) * Tile::kStageWords + (TT + ge) * kStride + l;
+#pragma unroll
+    for (int c = 0; c < CW / 8; ++c) {
+      float hv[PT], wv[PE];
+#pragma unroll
+      for (int i = 0; i < PT; ++i) hv[i] = hs[8 * i * kStride + 8 * c];
+#pragma unroll
+      for (int j = 0; j < PE; ++j) wv[j] = ws[Tile::GE * j * kStride + 8 * c];
+#pragma unroll
+      for (int i = 0; i < PT; ++i)
+#pragma unroll
+        for (int j = 0; j < PE; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[j], hv[i]));
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // lane sums to shared memory, then each thread folds whole pairs
+  float *red = psm;
+#pragma unroll
+  for (int i = 0; i < PT; ++i)
+#pragma unroll
+    for (int j = 0; j < PE; ++j)
+      red[((8 * i + tg) * TE + Tile::GE * j + ge) * 9 + l] = acc[i][j];
+  __syncthreads();
+  for (int p = tid; p < TT * TE; p += NT) {
+    const int t = t0 + p / TE, e = e0 + p % TE;
+    if (t >= a.T || e >= a.E) continue;
+    float s = -0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s = __fadd_rn(s, red[p * 9 + k]);
+    for (int c = ncols; c < H; ++c)
+      s = __fadd_rn(s, __fmul_rn(W[(size_t)e * H + c], a.h[(size_t)t * H + c]));
+    a.logits[(size_t)t * a.E + e] = s;
+    if (!is_finite_f(s)) set_status(a.status, kStatusNonFinite);
+  }
+}
+
+// MOE_ROUTE_TILE=24|44 pins the block (PT, PE) for measurements; 1 selects
+// the 4 x 4 scalar-staged kernel.
+int route_tile_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char *env = getenv("MOE_ROUTE_TILE");
+    v = env ? atoi(env) : 0;
+    if (v != 1 && v != 24 && v != 44) v = 0;
+  }
+  return v;
+}
+
+template <int PT, int PE, int NT>
+int pipe_ctas(const RouteArgs &a) {
+  constexpr int TE = NT / 64 * PE, TT = 8 * PT;
+  return ((a.E + TE - 1) / TE) * ((a.T + TT - 1) / TT);
+}
+
+template <int PT, int PE, int CW, int S, int NT>
+cudaError_t launch_pipe(const RouteArgs &a, cudaStream_t s) {
+  using Tile = PipeTile<PT, PE, CW, S, NT>;
+  constexpr size_t smem = Tile::kSmem;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(route_logits_pipe_kernel<PT, PE, CW, S, NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid((a.E + Tile::TE - 1) / Tile::TE, (a.T + Tile::TT - 1) / Tile::TT);
+  route_logits_pipe_kernel<PT, PE, CW, S, NT><<<grid, NT, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
 // One warp per token (the selection itself is route_core.cuh select_token).
 __global__ void __launch_bounds__(256) route_select_kernel(RouteArgs a) {
   __shared__ SelectScratch scratch[8];
@@ -352,10 +529,24 @@ size_t permute_scratch_words(int R, int E) {
   return (size_t)((R + kPermTile - 1) / kPermTile) * E + (size_t)R;
 }
 
-cudaError_t launch_route(const RouteArgs &a, cudaStream_t s) {
+cudaError_t launch_route(const RouteArgs &a, cudaStream_t s, int *launches) {
+  if (launches) *launches = 0;
   if (a.T <= 0) return cudaSuccess;
   const size_t small_smem = sizeof(float) * (size_t)(1 + kSmallTE) * a.H;
-  if (a.T >= 16 && a.router_dtype != kRouterF32Seq) {
+  const bool aligned16 =
+      ((reinterpret_cast<uintptr_t>(a.h) | reinterpret_cast<uintptr_t>(a.router)) & 15) == 0;
+  if (a.T >= 16 && a.router_dtype == kRouterF32 && a.H % 4 == 0 && aligned16 &&
+      route_tile_override() != 1) {
+    // the largest block that still gives about 1.7 CTAs per SM
+    // 4 x 4 blocks while they still give about one CTA per SM, else 2 x 4
+    const int pin = route_tile_override();
+    cudaError_t e;
+    if (pin == 44 || (pin != 24 && pipe_ctas<4, 4, 256>(a) >= 128))
+      e = launch_pipe<4, 4, 64, 4, 256>(a, s);
+    else
+      e = launch_pipe<2, 4, 128, 4, 256>(a, s);
+    if (e != cudaSuccess) return e;
+  } else if (a.T >= 16 && a.router_dtype != kRouterF32Seq) {
     const int ne = (a.E + kTE - 1) / kTE;
     if ((long long)ne * ((a.T + 31) / 32) >= 2 * 148) {
       route_logits_tiled_kernel<32><<<dim3(ne, (a.T + 31) / 32), 256, 0, s>>>(a);
@@ -372,6 +563,7 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t s) {
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return err;
   route_select_kernel<<<(a.T + 7) / 8, 256, 0, s>>>(a);
+  if (launches) *launches = 2;
   return cudaGetLastError();
 }
 

@@ -116,12 +116,25 @@ class MoeLayerEngine:
         self._check(lib().moe_stack_forward(self._h, first_layer, n_layers, x.data_ptr(),
                                             x.shape[0], eps, _stream(stream)))
 
-    def forward_host(self, layer: int, h: np.ndarray, resid: np.ndarray | None = None):
+    def forward_host(self, layer: int, h: np.ndarray, resid: np.ndarray | None = None,
+                     out: np.ndarray | None = None, ids: np.ndarray | None = None,
+                     gates: np.ndarray | None = None):
+        """Host buffers in and out (the library copies them).  Buffers in pinned
+        host memory are read and written by DMA directly; pageable ones are
+        staged.  `out`, `ids` and `gates` may be passed to reuse buffers."""
         h = np.ascontiguousarray(h, np.float32)
         T = h.shape[0]
-        out = np.empty_like(h)
-        ids = np.empty((T, self.cfg.top_k), np.uint32)
-        gates = np.empty((T, self.cfg.top_k), np.float32)
+        K = self.cfg.top_k
+        if out is None:
+            out = np.empty_like(h)
+        if ids is None:
+            ids = np.empty((T, K), np.uint32)
+        if gates is None:
+            gates = np.empty((T, K), np.float32)
+        for a, shape, dt in ((out, h.shape, np.float32), (ids, (T, K), np.uint32),
+                             (gates, (T, K), np.float32)):
+            if a.shape != shape or a.dtype != dt or not a.flags.c_contiguous:
+                raise ValueError(f"output buffer must be C-contiguous {dt.__name__}{shape}")
         r = None if resid is None else np.ascontiguousarray(resid, np.float32)
         self._check(lib().moe_layer_forward_host(self._h, layer, h.ctypes.data,
                                                  None if r is None else r.ctypes.data,

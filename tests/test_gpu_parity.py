@@ -243,6 +243,42 @@ def test_host_variant_and_residual():
     assert np.array_equal(bits(out), bits(ref.out))
 
 
+def test_host_buffers_pinned_and_staged():
+    """moe_layer_forward_host DMAs pinned buffers directly and stages pageable
+    ones in chunks (2.4 MB here: three chunks); every mix gives the device
+    call's bits."""
+    lw = O.synth_layer(43, 0, 2048, 256, 8, 2, False)
+    T = 300
+    h = O.synth_hidden(43, T, 2048)
+    resid = O.synth_hidden(44, T, 2048)
+    eng = engine_for(lw, T)
+    ex, sc, rt = helpers.to_device(lw)
+    eng.set_layer_packed(0, ex, sc, rt)
+    hd, rd = torch.from_numpy(h).cuda(), torch.from_numpy(resid).cuda()
+    od = torch.empty_like(hd)
+    idd = torch.empty((T, 2), dtype=torch.int32, device="cuda")
+    eng.forward(0, hd, od, resid=rd, ids=idd)
+    eng.sync_status()
+    want, want_ids = od.cpu().numpy(), idd.cpu().numpy().astype(np.uint32)
+    ref = O.layer_forward(lw, h, resid=resid)
+    assert np.array_equal(want_ids, ref.ids)
+    assert helpers.rel_err(want, ref.out) < 1e-3
+
+    def pinned(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
+
+    for pin_in, pin_out in ((False, False), (True, True), (True, False), (False, True)):
+        hi = pinned(h) if pin_in else h.copy()
+        ri = pinned(resid) if pin_in else resid.copy()
+        out = pinned(np.zeros_like(h)) if pin_out else np.zeros_like(h)
+        got, ids, _ = eng.forward_host(0, hi, ri, out=out)
+        assert got is out
+        assert np.array_equal(ids, want_ids)
+        assert np.array_equal(bits(got), bits(want)), (pin_in, pin_out)
+    with pytest.raises(ValueError):
+        eng.forward_host(0, h, out=np.zeros((T, 2047), np.float32))
+
+
 def test_nonfinite_input_is_reported():
     lw = O.synth_layer(51, 0, 64, 32, 8, 2, False)
     h = O.synth_hidden(51, 2, 64)
@@ -307,6 +343,55 @@ def test_route_tiled_ragged_shapes(bf16):
         assert np.array_equal(bits(probs.cpu().numpy()[t]), bits(p)), t
         assert np.array_equal(ids.cpu().numpy()[t].astype(np.uint32), rid), t
         assert np.array_equal(bits(gates.cpu().numpy()[t]), bits(rg)), t
+
+
+@pytest.mark.parametrize("T,E", [(50, 20), (600, 36), (4010, 20), (2310, 200)])
+def test_route_pipelined_blocks(T, E):
+    """f32 routers with H % 4 == 0 take the pipelined register-blocked logits
+    kernel; these (T, E) pick its 16x16 and 32x16 tiles, each with ragged
+    token and expert edges, and H % 8 == 4 leaves a folded tail:
+    probabilities, ids and gates bit-exact."""
+    H, K = 1036, 3
+    router = O.synth_normal(63, O.KIND_ROUTER, 0, E * H, 0.02).reshape(E, H)
+    lw = O.LayerWeights(H, 8, E, K, True, np.ascontiguousarray(router),
+                        np.zeros((E, 3 * 8 * H), np.int8), np.ones((E, 2 * 8 + H), np.float32))
+    h = O.synth_hidden(64, T, H)
+    eng = engine_for(lw, T)
+    ex, sc, rt = helpers.to_device(lw)
+    eng.set_layer_packed(0, ex, sc, rt)
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    gates = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    probs = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    eng.route(0, torch.from_numpy(h).cuda(), ids, gates, probs=probs)
+    eng.sync_status()
+    g_probs, g_ids, g_gates = probs.cpu().numpy(), ids.cpu().numpy(), gates.cpu().numpy()
+    lg = np.empty(E, np.float32)
+    for t in range(T):
+        O.lib().oracle_router_logits(lw.router.ctypes.data, 0, E, H, h[t].ctypes.data,
+                                     lg.ctypes.data)
+        p = O.softmax(lg)
+        rid, rg = O.topk(p, K, True)
+        assert np.array_equal(bits(g_probs[t]), bits(p)), t
+        assert np.array_equal(g_ids[t].astype(np.uint32), rid), t
+        assert np.array_equal(bits(g_gates[t]), bits(rg)), t
+
+
+def test_route_nonfinite_input_flagged_by_blocked_kernel():
+    """The blocked kernel has no separate input scan: a non-finite input
+    element makes every logit of its token non-finite, which is reported."""
+    H, E, K, T = 512, 64, 4, 300
+    lw = O.synth_layer(65, 0, H, 64, E, K, False)
+    h = O.synth_hidden(65, T, H)
+    h[217, 333] = np.inf
+    eng = engine_for(lw, T)
+    ex, sc, rt = helpers.to_device(lw)
+    eng.set_layer_packed(0, ex, sc, rt)
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    gates = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    eng.route(0, torch.from_numpy(h).cuda(), ids, gates)
+    with pytest.raises(M.MoeError) as ei:
+        eng.sync_status()
+    assert ei.value.status == _lib.MOE_ERR_NONFINITE
 
 
 @pytest.mark.parametrize("T,E,K", [(600, 128, 8), (2100, 64, 4)])
