@@ -806,6 +806,60 @@ __global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_
   }
 }
 
+// One warp per token: the token's row is quantized once, with the same
+// arithmetic as quantize_rows_kernel, and the digits are stored at each of
+// its K routes' expert-sorted rows (r_pos; negative or out-of-range
+// positions, which invalid routes leave, are skipped), with the per-route
+// scales; the routes' activation amax is cleared for the gate/up epilogue.
+__global__ void quantize_tokens_kernel(const float *__restrict__ x,
+                                       const int32_t *__restrict__ r_pos, int T, int K, int n,
+                                       int8_t *__restrict__ q, size_t plane,
+                                       float *__restrict__ s1, float *__restrict__ s2,
+                                       uint32_t *__restrict__ amax_reset) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const uint32_t R = (uint32_t)T * (uint32_t)K;
+  const int mine = lane < K ? r_pos[(size_t)t * K + lane] : -1;
+  int pos[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) pos[k] = __shfl_sync(0xffffffffu, mine, k);
+  const float *row = x + (size_t)t * n;
+  float amax = 0.0f;
+  for (int c = lane * 4; c < n; c += 128) {
+    const float4 v = *reinterpret_cast<const float4 *>(row + c);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+  const float inv = 1.0f / s;
+  for (int c = lane * 4; c < n; c += 128) {
+    const float4 v = *reinterpret_cast<const float4 *>(row + c);
+    const float in[4] = {v.x, v.y, v.z, v.w};
+    uint32_t p1 = 0, p2 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float u = in[k] * inv;
+      const float a1 = fminf(fmaxf(rintf(u), -127.0f), 127.0f);
+      const float a2 = fminf(fmaxf(rintf((u - a1) * 254.0f), -127.0f), 127.0f);
+      p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
+      p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxTopK; ++k)
+      if (k < K && (uint32_t)pos[k] < R) {
+        *reinterpret_cast<uint32_t *>(q + (size_t)pos[k] * n + c) = p1;
+        *reinterpret_cast<uint32_t *>(q + plane + (size_t)pos[k] * n + c) = p2;
+      }
+  }
+  if (lane < K && (uint32_t)mine < R) {
+    s1[mine] = s;
+    s2[mine] = s / 254.0f;
+    if (amax_reset) amax_reset[mine] = 0u;
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -852,6 +906,16 @@ cudaError_t launch_quantize_rows(const float *src, const int32_t *rows, const ui
   if (R <= 0) return cudaSuccess;
   quantize_rows_kernel<<<(R + 7) / 8, 256, 0, s>>>(src, rows, amax_in, R, R_dev, n, q, plane, s1,
                                                    s2, amax_reset);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_tokens(const float *x, const int32_t *r_pos, int T, int K, int n,
+                                   int8_t *q, size_t plane, float *s1, float *s2,
+                                   uint32_t *amax_reset, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  if (K > kMaxTopK) return cudaErrorInvalidValue;
+  quantize_tokens_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, r_pos, T, K, n, q, plane, s1, s2,
+                                                     amax_reset);
   return cudaGetLastError();
 }
 

@@ -55,6 +55,12 @@ cudaError_t launch_build_tiles(const int32_t *seg_off, const int32_t *active,
                                int32_t *tile_row0, int32_t *tile_rows, int32_t *n_tiles,
                                int max_tiles, cudaStream_t s);
 
+// T token rows, each quantized once and stored at its K routes' sorted rows
+// r_pos[t * K + k] (rows outside [0, T * K) are skipped).
+cudaError_t launch_quantize_tokens(const float *x, const int32_t *r_pos, int T, int K, int n,
+                                   int8_t *q, size_t plane, float *s1, float *s2,
+                                   uint32_t *amax_reset, cudaStream_t s);
+
 // R rows (grid size); when R_dev is given, rows at or past *R_dev are skipped.
 cudaError_t launch_quantize_rows(const float *src, const int32_t *rows, const uint32_t *amax_in,
                                  int R, int n, int8_t *q, size_t plane, float *s1, float *s2,

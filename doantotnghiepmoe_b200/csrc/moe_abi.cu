@@ -554,8 +554,9 @@ moe_status graphed(moe_handle *h, const uint64_t (&key)[10], cudaStream_t s, F &
 }
 
 // Router + top-k + permutation for T tokens of `layer`.
+// tile_bn > 0: the permutation also writes the tensor-core tile list.
 moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T, uint32_t *ids,
-                     float *gates, float *probs, cudaStream_t s, bool permute) {
+                     float *gates, float *probs, cudaStream_t s, bool permute, int tile_bn = 0) {
   RouteArgs ra{};
   ra.h = d_h;
   ra.router = L.router;
@@ -596,6 +597,14 @@ moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T,
   pa.status = h->status;
   pa.scratch = h->perm_scratch;
   pa.scratch_words = h->perm_scratch_words;
+  if (tile_bn > 0) {
+    pa.tile_bn = tile_bn;
+    pa.max_tiles = h->max_tiles;
+    pa.tile_expert = h->tile_expert;
+    pa.tile_row0 = h->tile_row0;
+    pa.tile_rows = h->tile_rows;
+    pa.n_tiles = h->n_tiles;
+  }
   p0 = h->prof.begin(s);
   e = launch_permute(pa, s);
   h->prof.end("permute", p0, s);
@@ -691,11 +700,9 @@ moe_status tensor_experts(moe_handle *h, const LayerSlot &L, const float *d_h,
   const size_t Rcap = (size_t)h->d.max_tokens * K;
   const int bn = tc::tc_block_n(R, h->d.num_experts);
   cudaError_t e;
+  // the tile list came with the permutation (run_route with tile_bn = bn)
   cudaEvent_t p0 = h->prof.begin(s);
-  e = tc::launch_build_tiles(h->seg_off, h->active, h->n_active, bn, h->tile_expert,
-                             h->tile_row0, h->tile_rows, h->n_tiles, h->max_tiles, s);
-  if (e == cudaSuccess)
-    e = tc::launch_quantize_rows(d_h, h->r_token, nullptr, R, H, h->xq, Rcap * H, h->xs1, h->xs2,
+  e = tc::launch_quantize_tokens(d_h, h->r_pos, T, K, H, h->xq, Rcap * H, h->xs1, h->xs2,
                                  h->act_amax, s);
   h->prof.end("tc_prep", p0, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "tensor prep launch");
@@ -740,7 +747,7 @@ moe_status tensor_experts(moe_handle *h, const LayerSlot &L, const float *d_h,
     h->prof.end("combine", p0, s);
   }
   if (e != cudaSuccess) return cuda_fail(h, e, "tensor expert launch");
-  h->last_launches += 6;
+  h->last_launches += 5;
   return MOE_OK;
 }
 
@@ -783,9 +790,11 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
                                            cudaMemcpyDeviceToDevice, s);
     return MOE_OK;
   }
-  moe_status st = run_route(h, L, d_h, T, ids, gates, nullptr, s, true);
+  const bool tc = use_tensor_path(h, L, T, d_h);
+  const int bn = tc ? tc::tc_block_n(T * h->d.top_k, h->d.num_experts) : 0;
+  moe_status st = run_route(h, L, d_h, T, ids, gates, nullptr, s, true, bn);
   if (st != MOE_OK) return st;
-  if (use_tensor_path(h, L, T, d_h)) return tensor_experts(h, L, d_h, d_resid, d_out, T, s);
+  if (tc) return tensor_experts(h, L, d_h, d_resid, d_out, T, s);
   GemvArgs a{};
   a.H = h->d.hidden;
   a.I = h->d.intermediate;

@@ -377,14 +377,84 @@ __global__ void __launch_bounds__(256) route_select_kernel(RouteArgs a) {
 }
 
 // Single-CTA stable counting sort of the T*K routes by expert.
+// ---------------------------------------------------------------------------
+// Permutation: a stable counting sort of the routes by expert.
+// ---------------------------------------------------------------------------
+
+// Exclusive prefix over threads 0..255 of the block of v (threads >= 256 take
+// part and get meaningless results); `total` = sum over threads 0..255.
+// wsum: 8 words of shared memory.  Contains two block barriers.
+__device__ __forceinline__ int block_scan256(int v, int *wsum, int &total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31 && w < 8) wsum[w] = x;
+  __syncthreads();
+  int pre = 0;
+  total = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int t = wsum[i];
+    if (i < w) pre += t;
+    total += t;
+  }
+  __syncthreads();
+  return pre + x - v;
+}
+
+// Expert segments, the active list and (optionally) the tile list from the
+// per-expert counts; called by every thread of the block, thread e < 256
+// holding cnt of expert e (0 past E).  Returns the segment start of expert
+// tid.  Contains block barriers.
+__device__ __forceinline__ int segments_and_tiles(const PermuteArgs &a, int cnt, int *wsum) {
+  const int e = threadIdx.x, E = a.E;
+  const bool mine = e < E && e < kMaxExperts;
+  int total;
+  const int seg = block_scan256(mine ? cnt : 0, wsum, total);
+  int nact;
+  const int apos = block_scan256(mine && cnt > 0 ? 1 : 0, wsum, nact);
+  if (mine) {
+    a.seg_off[e] = seg;
+    if (cnt > 0) a.active[apos] = e;
+  }
+  if (e == 0) {
+    a.seg_off[E] = total;
+    *a.n_active = nact;
+  }
+  if (a.tile_bn > 0) {
+    const int bn = a.tile_bn;
+    const int nt = mine ? (cnt + bn - 1) / bn : 0;
+    int ntot;
+    const int first = block_scan256(nt, wsum, ntot);
+    for (int k = 0; k < nt && first + k < a.max_tiles; ++k) {
+      a.tile_expert[first + k] = e;
+      a.tile_row0[first + k] = seg + k * bn;
+      a.tile_rows[first + k] = min(bn, cnt - k * bn);
+    }
+    if (e == 0) *a.n_tiles = min(ntot, a.max_tiles);
+  }
+  return seg;
+}
+
+// One CTA for up to kPermSingleMax routes.  Routes go in tiles of 1024 in
+// route order; inside a tile a route's rank comes from its warp's match mask
+// plus a scan over the warps' counts for its expert (one warp scans one
+// expert's 32 warp counts with shuffles), on top of the expert's running
+// offset.
 constexpr int kPermThreads = 1024;
-__global__ void __launch_bounds__(kPermThreads) permute_kernel(PermuteArgs a) {
-  __shared__ int32_t cnt[kMaxExperts + 1];
+constexpr int kPermSingleMax = 2048;  // above: three kernels are faster (measured)
+__global__ void __launch_bounds__(kPermThreads, 1) permute_kernel(PermuteArgs a) {
+  __shared__ int32_t cnt[kMaxExperts];
   __shared__ int32_t run[kMaxExperts];
   __shared__ int32_t wcnt[kPermThreads / 32][kMaxExperts];
+  __shared__ int32_t wsum[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = a.E, R = a.T * a.K;
-  for (int e = tid; e <= E; e += kPermThreads) cnt[e] = 0;
+  if (tid < kMaxExperts) cnt[tid] = 0;
   for (int i = tid; i < (kPermThreads / 32) * kMaxExperts; i += kPermThreads)
     (&wcnt[0][0])[i] = 0;
   __syncthreads();
@@ -394,50 +464,45 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(PermuteArgs a) {
     else set_status(a.status, kStatusBadRoute);
   }
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0, na = 0;
-    for (int e = 0; e < E; ++e) {
-      const int c = cnt[e];
-      a.seg_off[e] = acc;
-      run[e] = acc;
-      if (c > 0) a.active[na++] = e;
-      acc += c;
-    }
-    a.seg_off[E] = acc;
-    *a.n_active = na;
-  }
+  const int seg = segments_and_tiles(a, tid < kMaxExperts ? cnt[tid] : 0, wsum);
+  if (tid < E) run[tid] = seg;
   __syncthreads();
-  // Tiles of 1024 routes in route order; rank inside the tile from the warp
-  // match mask plus the per-warp counts of earlier warps.
   for (int base = 0; base < R; base += kPermThreads) {
     const int r = base + tid;
     const bool valid = r < R;
     const uint32_t e = valid ? a.ids[r] : 0xFFFFFFFFu;
     const bool ok = valid && e < (uint32_t)E;
-    const uint32_t key = ok ? e : 0xFFFFFFFFu;
-    const unsigned mask = __match_any_sync(0xffffffffu, key);
+    const unsigned mask = __match_any_sync(0xffffffffu, ok ? e : 0xFFFFFFFFu);
     const int intra = __popc(mask & ((1u << lane) - 1u));
     if (ok && intra == 0) wcnt[warp][e] = __popc(mask);
     __syncthreads();
-    if (ok) {
-      int pos = run[e] + intra;
-      for (int w = 0; w < warp; ++w) pos += wcnt[w][e];
-      const int t = r / a.K, slot = r % a.K;
-      a.r_token[pos] = t;
-      a.r_slot[pos] = slot;
-      if (a.r_gate) a.r_gate[pos] = a.gates[r];
-      if (a.r_pos) a.r_pos[r] = pos;
+    // wcnt[w][e] := position of warp w's first route to e; run[e] advances
+    for (int ee = warp; ee < E; ee += kPermThreads / 32) {
+      const int v = wcnt[lane][ee];
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      const int r0 = run[ee];
+      wcnt[lane][ee] = r0 + x - v;
+      __syncwarp();
+      if (lane == 31) run[ee] = r0 + x;
     }
     __syncthreads();
-    // advance the running offsets by this tile's totals, then clear
-    for (int ee = tid; ee < E; ee += kPermThreads) {
-      int tot = 0;
-      for (int w = 0; w < kPermThreads / 32; ++w) {
-        tot += wcnt[w][ee];
-        wcnt[w][ee] = 0;
-      }
-      run[ee] += tot;
+    if (ok) {
+      const int pos = wcnt[warp][e] + intra;
+      a.r_token[pos] = r / a.K;
+      a.r_slot[pos] = r % a.K;
+      if (a.r_gate) a.r_gate[pos] = a.gates[r];
+      if (a.r_pos) a.r_pos[r] = pos;
+    } else if (valid && a.r_pos) {
+      a.r_pos[r] = -1;  // an invalid expert id holds no sorted row
     }
+    __syncthreads();
+    for (int i = tid; i < (kPermThreads / 32) * E; i += kPermThreads)
+      wcnt[i / E][i % E] = 0;
     __syncthreads();
   }
 }
@@ -445,9 +510,10 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(PermuteArgs a) {
 // Multi-CTA stable counting sort for large route counts: (1) per tile of
 // 1024 routes, the per-expert counts and each route's rank inside its tile
 // (warp match mask + earlier warps' counts); (2) one CTA turns the tile
-// counts into per-tile offsets and the expert segments; (3) every route is
-// scattered to seg_off[e] + tile offset + rank in tile.  Same order as the
-// single-CTA kernel: experts ascending, routes (tokens) ascending inside.
+// counts into per-tile offsets, the expert segments and the tile list; (3)
+// every route is scattered to seg_off[e] + tile offset + rank in tile.  Same
+// order as the single-CTA kernel: experts ascending, routes (tokens)
+// ascending inside.
 constexpr int kPermTile = 1024;
 
 __global__ void __launch_bounds__(kPermTile) perm_hist_kernel(PermuteArgs a, int32_t *tilecnt,
@@ -480,33 +546,23 @@ __global__ void __launch_bounds__(kPermTile) perm_hist_kernel(PermuteArgs a, int
 
 __global__ void __launch_bounds__(kMaxExperts) perm_scan_kernel(PermuteArgs a, int32_t *tilecnt,
                                                                 int ntiles) {
-  __shared__ int32_t tot[kMaxExperts], act[kMaxExperts];
+  __shared__ int32_t wsum[8];
   const int e = threadIdx.x, E = a.E;
+  // running offsets of expert e over the tiles, loads batched 8 at a time
   int run = 0;
   if (e < E)
-    for (int t = 0; t < ntiles; ++t) {
-      const int c = tilecnt[(size_t)t * E + e];
-      tilecnt[(size_t)t * E + e] = run;
-      run += c;
+    for (int t0 = 0; t0 < ntiles; t0 += 8) {
+      int c[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) c[k] = t0 + k < ntiles ? tilecnt[(size_t)(t0 + k) * E + e] : 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (t0 + k < ntiles) {
+          tilecnt[(size_t)(t0 + k) * E + e] = run;
+          run += c[k];
+        }
     }
-  tot[e] = e < E ? run : 0;
-  act[e] = (e < E && run > 0) ? 1 : 0;
-  __syncthreads();
-  for (int o = 1; o < kMaxExperts; o <<= 1) {  // inclusive scans
-    const int v = e >= o ? tot[e - o] : 0, w = e >= o ? act[e - o] : 0;
-    __syncthreads();
-    tot[e] += v;
-    act[e] += w;
-    __syncthreads();
-  }
-  if (e < E) {
-    a.seg_off[e] = tot[e] - run;
-    if (run > 0) a.active[act[e] - 1] = e;
-  }
-  if (e == kMaxExperts - 1) {
-    a.seg_off[E] = tot[e];
-    *a.n_active = act[e];
-  }
+  segments_and_tiles(a, run, wsum);
 }
 
 __global__ void perm_scatter_kernel(PermuteArgs a, const int32_t *tilecnt,
@@ -515,7 +571,10 @@ __global__ void perm_scatter_kernel(PermuteArgs a, const int32_t *tilecnt,
   const int R = a.T * a.K;
   if (r >= R) return;
   const uint32_t e = a.ids[r];
-  if (e >= (uint32_t)a.E) return;
+  if (e >= (uint32_t)a.E) {
+    if (a.r_pos) a.r_pos[r] = -1;  // an invalid expert id holds no sorted row
+    return;
+  }
   const int pos = a.seg_off[e] + tilecnt[(size_t)(r / kPermTile) * a.E + e] + intra[r];
   a.r_token[pos] = r / a.K;
   a.r_slot[pos] = r % a.K;
@@ -567,9 +626,21 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t s, int *launches) {
   return cudaGetLastError();
 }
 
+// MOE_PERM_SINGLE_MAX overrides the route count up to which one CTA sorts.
+int perm_single_max() {
+  static int v = -1;
+  if (v < 0) {
+    const char *env = getenv("MOE_PERM_SINGLE_MAX");
+    v = env ? atoi(env) : kPermSingleMax;
+    if (v < 0) v = kPermSingleMax;
+  }
+  return v;
+}
+
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t s) {
   const int R = a.T * a.K;
-  if (R <= 2 * kPermTile || !a.scratch || a.scratch_words < permute_scratch_words(R, a.E)) {
+  if (R <= perm_single_max() || !a.scratch ||
+      a.scratch_words < permute_scratch_words(R, a.E)) {
     permute_kernel<<<1, kPermThreads, 0, s>>>(a);
     return cudaGetLastError();
   }

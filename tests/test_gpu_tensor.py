@@ -53,6 +53,21 @@ def test_qwen3_prefill_tensor_path_with_residual():
     assert err < TOL, err
 
 
+@pytest.mark.parametrize("T,E,K", [(256, 64, 8), (2100, 16, 4)])
+def test_tensor_path_tile_list_from_permutation(T, E, K):
+    """The permutation writes the tensor-core tile list itself: one CTA up to
+    2048 routes (here exactly 2048), the multi-CTA sort above (8400 routes,
+    about 9 tiles per expert); the per-token digit planes land at every
+    route's sorted row."""
+    lw = O.synth_layer(107, 0, 256, 128, E, K, False)
+    h = O.synth_hidden(107, T, 256)
+    ref = O.layer_forward(lw, h, nthreads=8)
+    out, ids, _ = run_tensor(lw, h)
+    assert np.array_equal(ids, ref.ids)
+    err = helpers.rel_err(out, ref.out)
+    assert err < TOL, err
+
+
 def test_auto_path_picks_tensor_cores_for_prefill():
     lw = O.synth_layer(105, 0, 256, 128, 16, 4, False)
     h = O.synth_hidden(105, 256, 256)
