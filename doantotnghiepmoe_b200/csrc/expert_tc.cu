@@ -773,6 +773,7 @@ __global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_
     amax = __uint_as_float(amax_in[warp]);
   } else {
     amax = 0.0f;
+#pragma unroll 4
     for (int c = lane * 4; c < n; c += 128) {
       const float4 v = *reinterpret_cast<const float4 *>(x + c);
       amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
@@ -784,6 +785,7 @@ __global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_
   const float inv = 1.0f / s;
   int8_t *q1 = q + (size_t)warp * n;
   int8_t *q2 = q + plane + (size_t)warp * n;
+#pragma unroll 4
   for (int c = lane * 4; c < n; c += 128) {
     const float4 v = *reinterpret_cast<const float4 *>(x + c);
     const float in[4] = {v.x, v.y, v.z, v.w};
@@ -806,35 +808,39 @@ __global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_
   }
 }
 
-// One warp per token: the token's row is quantized once, with the same
+// One CTA per token: the token's row is quantized once, with the same
 // arithmetic as quantize_rows_kernel, and the digits are stored at each of
 // its K routes' expert-sorted rows (r_pos; negative or out-of-range
 // positions, which invalid routes leave, are skipped), with the per-route
 // scales; the routes' activation amax is cleared for the gate/up epilogue.
-__global__ void quantize_tokens_kernel(const float *__restrict__ x,
-                                       const int32_t *__restrict__ r_pos, int T, int K, int n,
-                                       int8_t *__restrict__ q, size_t plane,
-                                       float *__restrict__ s1, float *__restrict__ s2,
-                                       uint32_t *__restrict__ amax_reset) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
+constexpr int kQtThreads = 256;
+__global__ void __launch_bounds__(kQtThreads) quantize_tokens_kernel(
+    const float *__restrict__ x, const int32_t *__restrict__ r_pos, int T, int K, int n,
+    int8_t *__restrict__ q, size_t plane, float *__restrict__ s1, float *__restrict__ s2,
+    uint32_t *__restrict__ amax_reset) {
+  __shared__ float wmax[kQtThreads / 32];
+  __shared__ int pos_s[kMaxTopK];
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t R = (uint32_t)T * (uint32_t)K;
-  const int mine = lane < K ? r_pos[(size_t)t * K + lane] : -1;
-  int pos[kMaxTopK];
-#pragma unroll
-  for (int k = 0; k < kMaxTopK; ++k) pos[k] = __shfl_sync(0xffffffffu, mine, k);
+  if (tid < K) pos_s[tid] = r_pos[(size_t)t * K + tid];
   const float *row = x + (size_t)t * n;
   float amax = 0.0f;
-  for (int c = lane * 4; c < n; c += 128) {
+  for (int c = tid * 4; c < n; c += kQtThreads * 4) {
     const float4 v = *reinterpret_cast<const float4 *>(row + c);
     amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (lane == 0) wmax[warp] = amax;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kQtThreads / 32; ++w) amax = fmaxf(amax, wmax[w]);
   const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
   const float inv = 1.0f / s;
-  for (int c = lane * 4; c < n; c += 128) {
+  int pos[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) pos[k] = k < K ? pos_s[k] : -1;
+  for (int c = tid * 4; c < n; c += kQtThreads * 4) {
     const float4 v = *reinterpret_cast<const float4 *>(row + c);
     const float in[4] = {v.x, v.y, v.z, v.w};
     uint32_t p1 = 0, p2 = 0;
@@ -848,15 +854,15 @@ __global__ void quantize_tokens_kernel(const float *__restrict__ x,
     }
 #pragma unroll
     for (int k = 0; k < kMaxTopK; ++k)
-      if (k < K && (uint32_t)pos[k] < R) {
+      if ((uint32_t)pos[k] < R) {
         *reinterpret_cast<uint32_t *>(q + (size_t)pos[k] * n + c) = p1;
         *reinterpret_cast<uint32_t *>(q + plane + (size_t)pos[k] * n + c) = p2;
       }
   }
-  if (lane < K && (uint32_t)mine < R) {
-    s1[mine] = s;
-    s2[mine] = s / 254.0f;
-    if (amax_reset) amax_reset[mine] = 0u;
+  if (tid < K && (uint32_t)pos_s[tid] < R) {
+    s1[pos_s[tid]] = s;
+    s2[pos_s[tid]] = s / 254.0f;
+    if (amax_reset) amax_reset[pos_s[tid]] = 0u;
   }
 }
 
@@ -914,20 +920,34 @@ cudaError_t launch_quantize_tokens(const float *x, const int32_t *r_pos, int T, 
                                    uint32_t *amax_reset, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   if (K > kMaxTopK) return cudaErrorInvalidValue;
-  quantize_tokens_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, r_pos, T, K, n, q, plane, s1, s2,
-                                                     amax_reset);
+  quantize_tokens_kernel<<<T, kQtThreads, 0, s>>>(x, r_pos, T, K, n, q, plane, s1, s2,
+                                                  amax_reset);
   return cudaGetLastError();
 }
 
-// Persistent tile loop with double-buffered accumulators for 64-route tiles
-// (MOE_TC_PERSISTENT=1); by default one CTA per tile.
-bool persistent_tc() {
+// Persistent tile loop with double-buffered accumulators for 64-route tiles:
+// MOE_TC_PERSISTENT=1 for both GEMMs, =2 for the down GEMM only, =3 for the
+// gate/up GEMM only; by default one CTA per tile.
+int persistent_mode() {
   static int v = -1;
   if (v < 0) {
     const char *env = getenv("MOE_TC_PERSISTENT");
-    v = (env && env[0] == '1') ? 1 : 0;
+    v = env ? atoi(env) : 0;
+    if (v < 0 || v > 3) v = 0;
   }
-  return v == 1;
+  return v;
+}
+bool persistent_gu() { return persistent_mode() == 1 || persistent_mode() == 3; }
+bool persistent_dn() { return persistent_mode() == 1 || persistent_mode() == 2; }
+
+int tc_bn_dn_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char *env = getenv("MOE_TC_BN_DN");
+    v = env ? atoi(env) : 0;
+    if (v != 64 && v != 128) v = 0;
+  }
+  return v;
 }
 
 int tc_bn_override() {
@@ -981,7 +1001,7 @@ constexpr int kPStagesGU = 4, kPStagesDN = 6;
 
 cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
                               int bn, int max_tiles, cudaStream_t s) {
-  if (bn == PBN && persistent_tc()) {
+  if (bn == PBN && persistent_gu()) {
     const size_t smem = psmem_bytes(2, 2, kPStagesGU);
     auto k = gate_up_tc_pkernel<kPStagesGU>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -996,7 +1016,7 @@ cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, 
 
 cudaError_t launch_down_tc(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
                            int bn, int max_tiles, cudaStream_t s) {
-  if (bn == PBN && persistent_tc()) {
+  if (bn == PBN && persistent_dn()) {
     const size_t smem = psmem_bytes(1, 2, kPStagesDN);
     auto k = down_tc_pkernel<kPStagesDN>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -10,7 +10,7 @@
 namespace moe {
 namespace tc {
 
-bool persistent_tc();
+int persistent_mode();  // MOE_TC_PERSISTENT: 0 off, 1 both GEMMs, 2 down, 3 gate/up
 int tc_bn_override();  // MOE_TC_BN (64 or 128), 0 when unset
 
 // Routes per GEMM tile: 64.  Measured on B200 (OLMoE T=512, Qwen3 T=4096),
@@ -20,9 +20,23 @@ int tc_bn_override();  // MOE_TC_BN (64 or 128), 0 when unset
 inline int tc_block_n(int routes, int experts) {
   (void)routes;
   (void)experts;
-  if (persistent_tc()) return 64;
+  if (persistent_mode() == 1 || persistent_mode() == 3) return 64;
   if (const int o = tc_bn_override()) return o;
   return 64;
+}
+
+int tc_bn_dn_override();  // MOE_TC_BN_DN (64 or 128), 0 when unset
+
+// Routes per down-GEMM tile.  The down GEMM has a short K (= I), so its
+// CTAs are short-lived and per-CTA overheads weigh; 128-route tiles halve
+// the CTA count once experts average 128 routes or more.  Measured on B200:
+// Qwen3 T=4096 (256 routes per expert) 877 vs 921 us per layer, OLMoE T=512
+// (64 per expert) a tie.  MOE_TC_BN_DN (64 or 128) pins the width.
+inline int tc_block_n_down(int routes, int experts) {
+  if (persistent_mode() == 1 || persistent_mode() == 2) return 64;
+  if (const int o = tc_bn_dn_override()) return o;
+  if (tc_bn_override()) return tc_bn_override();
+  return routes >= 128 * experts ? 128 : 64;
 }
 
 struct TcArgs {

@@ -50,11 +50,13 @@ struct PermuteArgs {
   // small, one CTA sorts everything
   int32_t *scratch;
   size_t scratch_words;
-  // optional (tile_bn > 0): the tensor-core tile list -- tiles of up to
-  // tile_bn consecutive routes of one expert, experts ascending, at most
+  // optional: up to two tensor-core tile lists (those with bn > 0) -- tiles
+  // of up to bn consecutive routes of one expert, experts ascending, at most
   // max_tiles of them
-  int tile_bn, max_tiles;
-  int32_t *tile_expert, *tile_row0, *tile_rows, *n_tiles;
+  struct TileList {
+    int bn, max_tiles;
+    int32_t *expert, *row0, *rows, *count;
+  } tiles[2];
 };
 size_t permute_scratch_words(int R, int E);
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t s);

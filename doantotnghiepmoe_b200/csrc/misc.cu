@@ -15,19 +15,25 @@ __global__ void combine_kernel(const float *__restrict__ contrib, const float *_
   const int H4 = H / 4;
   bool bad = false;
   const bool vec = (H & 3) == 0 && (((uintptr_t)contrib | (uintptr_t)resid | (uintptr_t)out) & 15) == 0;
-  if (vec) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4;
-         i += (size_t)gridDim.x * blockDim.x) {
-      const size_t t = i / H4, j4 = i % H4;
+  if (vec && K <= kMaxTopK && n4 < (1u << 31)) {
+    // all K slot loads go out before the first add (kMaxTopK-wide, predicated)
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < (uint32_t)n4;
+         i += gridDim.x * blockDim.x) {
+      const uint32_t t = i / (uint32_t)H4, j4 = i - t * (uint32_t)H4;
       float4 acc = resid ? reinterpret_cast<const float4 *>(resid)[i] : make_float4(0, 0, 0, 0);
-      const float4 *c = reinterpret_cast<const float4 *>(contrib) + t * K * H4 + j4;
-      for (int k = 0; k < K; ++k) {
-        const float4 v = c[(size_t)k * H4];
-        acc.x = __fadd_rn(acc.x, v.x);
-        acc.y = __fadd_rn(acc.y, v.y);
-        acc.z = __fadd_rn(acc.z, v.z);
-        acc.w = __fadd_rn(acc.w, v.w);
-      }
+      const float4 *c = reinterpret_cast<const float4 *>(contrib) + (size_t)t * K * H4 + j4;
+      float4 v[kMaxTopK];
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K) v[k] = __ldcs(c + (size_t)k * H4);
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K) {
+          acc.x = __fadd_rn(acc.x, v[k].x);
+          acc.y = __fadd_rn(acc.y, v[k].y);
+          acc.z = __fadd_rn(acc.z, v[k].z);
+          acc.w = __fadd_rn(acc.w, v[k].w);
+        }
       bad |= !(is_finite_f(acc.x) && is_finite_f(acc.y) && is_finite_f(acc.z) &&
                is_finite_f(acc.w));
       reinterpret_cast<float4 *>(out)[i] = acc;

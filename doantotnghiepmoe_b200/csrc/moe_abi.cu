@@ -416,6 +416,9 @@ struct moe_handle {
   float *xs1 = nullptr, *xs2 = nullptr, *as1 = nullptr, *as2 = nullptr;
   uint32_t *act_amax = nullptr;
   int32_t *tile_expert = nullptr, *tile_row0 = nullptr, *tile_rows = nullptr, *n_tiles = nullptr;
+  // the down GEMM's tile list when its width differs from the gate/up one
+  int32_t *dtile_expert = nullptr, *dtile_row0 = nullptr, *dtile_rows = nullptr,
+          *n_dtiles = nullptr;
   CUtensorMap map_x64{}, map_x128{}, map_a64{}, map_a128{};  // digit planes, box 64/128 rows
   // fused decode
   FusedLayer *d_flayers = nullptr;  // [num_layers]
@@ -480,6 +483,7 @@ void free_handle(moe_handle *h) {
                   h->active,  h->n_active,  h->r_token,   h->r_slot,    h->r_pos,   h->xq,
                   h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
                   h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles, h->d_flayers,
+                  h->dtile_expert, h->dtile_row0, h->dtile_rows, h->n_dtiles,
                   h->tok_cnt, h->fbar, h->phase_ts, h->sctr, h->perm_scratch};
   for (void *p : ptrs) cudaFree(p);
   cudaFreeHost(h->h_pin_in);
@@ -554,9 +558,11 @@ moe_status graphed(moe_handle *h, const uint64_t (&key)[10], cudaStream_t s, F &
 }
 
 // Router + top-k + permutation for T tokens of `layer`.
-// tile_bn > 0: the permutation also writes the tensor-core tile list.
+// bn_gu > 0: the permutation also writes the tensor-core tile list of the
+// gate/up GEMM, and (bn_dn > 0, != bn_gu) the down GEMM's.
 moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T, uint32_t *ids,
-                     float *gates, float *probs, cudaStream_t s, bool permute, int tile_bn = 0) {
+                     float *gates, float *probs, cudaStream_t s, bool permute, int bn_gu = 0,
+                     int bn_dn = 0) {
   RouteArgs ra{};
   ra.h = d_h;
   ra.router = L.router;
@@ -597,14 +603,11 @@ moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T,
   pa.status = h->status;
   pa.scratch = h->perm_scratch;
   pa.scratch_words = h->perm_scratch_words;
-  if (tile_bn > 0) {
-    pa.tile_bn = tile_bn;
-    pa.max_tiles = h->max_tiles;
-    pa.tile_expert = h->tile_expert;
-    pa.tile_row0 = h->tile_row0;
-    pa.tile_rows = h->tile_rows;
-    pa.n_tiles = h->n_tiles;
-  }
+  if (bn_gu > 0)
+    pa.tiles[0] = {bn_gu, h->max_tiles, h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles};
+  if (bn_dn > 0 && bn_dn != bn_gu)
+    pa.tiles[1] = {bn_dn, h->max_tiles, h->dtile_expert, h->dtile_row0, h->dtile_rows,
+                   h->n_dtiles};
   p0 = h->prof.begin(s);
   e = launch_permute(pa, s);
   h->prof.end("permute", p0, s);
@@ -700,7 +703,7 @@ moe_status tensor_experts(moe_handle *h, const LayerSlot &L, const float *d_h,
   const size_t Rcap = (size_t)h->d.max_tokens * K;
   const int bn = tc::tc_block_n(R, h->d.num_experts);
   cudaError_t e;
-  // the tile list came with the permutation (run_route with tile_bn = bn)
+  // the tile lists came with the permutation (run_route with the same widths)
   cudaEvent_t p0 = h->prof.begin(s);
   e = tc::launch_quantize_tokens(d_h, h->r_pos, T, K, H, h->xq, Rcap * H, h->xs1, h->xs2,
                                  h->act_amax, s);
@@ -737,8 +740,17 @@ moe_status tensor_experts(moe_handle *h, const LayerSlot &L, const float *d_h,
     h->prof.end("tc_act_digits", p0, s);
   }
   if (e == cudaSuccess) {
+    const int dbn = tc::tc_block_n_down(R, h->d.num_experts);
+    int dtiles = tiles;
+    if (dbn != bn) {  // its own list, written by the permutation
+      a.tile_expert = h->dtile_expert;
+      a.tile_row0 = h->dtile_row0;
+      a.tile_rows = h->dtile_rows;
+      a.n_tiles = h->n_dtiles;
+      dtiles = std::min(h->max_tiles, (R + dbn - 1) / dbn + std::min(h->d.num_experts, R));
+    }
     p0 = h->prof.begin(s);
-    e = tc::launch_down_tc(L.map_dn, bn == 64 ? h->map_a64 : h->map_a128, a, bn, tiles, s);
+    e = tc::launch_down_tc(L.map_dn, dbn == 64 ? h->map_a64 : h->map_a128, a, dbn, dtiles, s);
     h->prof.end("down_tc", p0, s);
   }
   if (e == cudaSuccess) {
@@ -791,8 +803,9 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
     return MOE_OK;
   }
   const bool tc = use_tensor_path(h, L, T, d_h);
-  const int bn = tc ? tc::tc_block_n(T * h->d.top_k, h->d.num_experts) : 0;
-  moe_status st = run_route(h, L, d_h, T, ids, gates, nullptr, s, true, bn);
+  const int R = T * h->d.top_k, E = h->d.num_experts;
+  moe_status st = run_route(h, L, d_h, T, ids, gates, nullptr, s, true,
+                            tc ? tc::tc_block_n(R, E) : 0, tc ? tc::tc_block_n_down(R, E) : 0);
   if (st != MOE_OK) return st;
   if (tc) return tensor_experts(h, L, d_h, d_resid, d_out, T, s);
   GemvArgs a{};
@@ -885,6 +898,10 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && dalloc(&h->tile_row0, h->max_tiles) == cudaSuccess;
   ok = ok && dalloc(&h->tile_rows, h->max_tiles) == cudaSuccess;
   ok = ok && dalloc(&h->n_tiles, 1) == cudaSuccess;
+  ok = ok && dalloc(&h->dtile_expert, h->max_tiles) == cudaSuccess;
+  ok = ok && dalloc(&h->dtile_row0, h->max_tiles) == cudaSuccess;
+  ok = ok && dalloc(&h->dtile_rows, h->max_tiles) == cudaSuccess;
+  ok = ok && dalloc(&h->n_dtiles, 1) == cudaSuccess;
   ok = ok && dalloc(&h->d_flayers, d.num_layers) == cudaSuccess;
   ok = ok && dalloc(&h->tok_cnt, T) == cudaSuccess && dalloc(&h->fbar, 1) == cudaSuccess;
   ok = ok && cudaMemset(h->tok_cnt, 0, T * sizeof(uint32_t)) == cudaSuccess;

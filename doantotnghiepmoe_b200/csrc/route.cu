@@ -425,28 +425,33 @@ __device__ __forceinline__ int segments_and_tiles(const PermuteArgs &a, int cnt,
     a.seg_off[E] = total;
     *a.n_active = nact;
   }
-  if (a.tile_bn > 0) {
-    const int bn = a.tile_bn;
-    const int nt = mine ? (cnt + bn - 1) / bn : 0;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const PermuteArgs::TileList &L = a.tiles[i];
+    if (L.bn <= 0) continue;  // block-uniform
+    const int nt = mine ? (cnt + L.bn - 1) / L.bn : 0;
     int ntot;
     const int first = block_scan256(nt, wsum, ntot);
-    for (int k = 0; k < nt && first + k < a.max_tiles; ++k) {
-      a.tile_expert[first + k] = e;
-      a.tile_row0[first + k] = seg + k * bn;
-      a.tile_rows[first + k] = min(bn, cnt - k * bn);
+    for (int k = 0; k < nt && first + k < L.max_tiles; ++k) {
+      L.expert[first + k] = e;
+      L.row0[first + k] = seg + k * L.bn;
+      L.rows[first + k] = min(L.bn, cnt - k * L.bn);
     }
-    if (e == 0) *a.n_tiles = min(ntot, a.max_tiles);
+    if (e == 0) *L.count = min(ntot, L.max_tiles);
   }
   return seg;
 }
 
-// One CTA for up to kPermSingleMax routes.  Routes go in tiles of 1024 in
-// route order; inside a tile a route's rank comes from its warp's match mask
-// plus a scan over the warps' counts for its expert (one warp scans one
-// expert's 32 warp counts with shuffles), on top of the expert's running
-// offset.
+// One CTA sorts up to kPermSingleMax routes (and any count when no scratch
+// for the multi-CTA sort is given).  Routes go in tiles of 1024 in route
+// order; inside a tile a route's rank comes from its warp's match mask plus a
+// scan over the warps' counts for its expert (one warp scans one expert's 32
+// warp counts with shuffles), on top of the expert's running offset.  The
+// ids and gates of the first kPermPer tiles are loaded up front, so those
+// tiles wait on no global load.
 constexpr int kPermThreads = 1024;
-constexpr int kPermSingleMax = 2048;  // above: three kernels are faster (measured)
+constexpr int kPermPer = 8;
+constexpr int kPermSingleMax = 2048;  // above: the three-kernel sort is faster (measured)
 __global__ void __launch_bounds__(kPermThreads, 1) permute_kernel(PermuteArgs a) {
   __shared__ int32_t cnt[kMaxExperts];
   __shared__ int32_t run[kMaxExperts];
@@ -454,11 +459,25 @@ __global__ void __launch_bounds__(kPermThreads, 1) permute_kernel(PermuteArgs a)
   __shared__ int32_t wsum[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = a.E, R = a.T * a.K;
+  uint32_t eid[kPermPer];
+  float gv[kPermPer];
+#pragma unroll
+  for (int k = 0; k < kPermPer; ++k) {
+    const int r = k * kPermThreads + tid;
+    eid[k] = r < R ? a.ids[r] : 0xFFFFFFFFu;
+    gv[k] = (r < R && a.r_gate) ? a.gates[r] : 0.0f;
+  }
   if (tid < kMaxExperts) cnt[tid] = 0;
   for (int i = tid; i < (kPermThreads / 32) * kMaxExperts; i += kPermThreads)
     (&wcnt[0][0])[i] = 0;
   __syncthreads();
-  for (int r = tid; r < R; r += kPermThreads) {
+#pragma unroll
+  for (int k = 0; k < kPermPer; ++k)
+    if (k * kPermThreads + tid < R) {
+      if (eid[k] < (uint32_t)E) atomicAdd(&cnt[eid[k]], 1);
+      else set_status(a.status, kStatusBadRoute);
+    }
+  for (int r = kPermPer * kPermThreads + tid; r < R; r += kPermThreads) {
     const uint32_t e = a.ids[r];
     if (e < (uint32_t)E) atomicAdd(&cnt[e], 1);
     else set_status(a.status, kStatusBadRoute);
@@ -467,10 +486,9 @@ __global__ void __launch_bounds__(kPermThreads, 1) permute_kernel(PermuteArgs a)
   const int seg = segments_and_tiles(a, tid < kMaxExperts ? cnt[tid] : 0, wsum);
   if (tid < E) run[tid] = seg;
   __syncthreads();
-  for (int base = 0; base < R; base += kPermThreads) {
-    const int r = base + tid;
+  // one tile of 1024 routes (block-uniform call)
+  auto tile = [&](int r, uint32_t e, float gate) {
     const bool valid = r < R;
-    const uint32_t e = valid ? a.ids[r] : 0xFFFFFFFFu;
     const bool ok = valid && e < (uint32_t)E;
     const unsigned mask = __match_any_sync(0xffffffffu, ok ? e : 0xFFFFFFFFu);
     const int intra = __popc(mask & ((1u << lane) - 1u));
@@ -495,15 +513,22 @@ __global__ void __launch_bounds__(kPermThreads, 1) permute_kernel(PermuteArgs a)
       const int pos = wcnt[warp][e] + intra;
       a.r_token[pos] = r / a.K;
       a.r_slot[pos] = r % a.K;
-      if (a.r_gate) a.r_gate[pos] = a.gates[r];
+      if (a.r_gate) a.r_gate[pos] = gate;
       if (a.r_pos) a.r_pos[r] = pos;
     } else if (valid && a.r_pos) {
       a.r_pos[r] = -1;  // an invalid expert id holds no sorted row
     }
     __syncthreads();
-    for (int i = tid; i < (kPermThreads / 32) * E; i += kPermThreads)
-      wcnt[i / E][i % E] = 0;
+    for (int i = tid; i < (kPermThreads / 32) * E; i += kPermThreads) wcnt[i / E][i % E] = 0;
     __syncthreads();
+  };
+#pragma unroll
+  for (int k = 0; k < kPermPer; ++k)
+    if (k * kPermThreads < R) tile(k * kPermThreads + tid, eid[k], gv[k]);
+  for (int base = kPermPer * kPermThreads; base < R; base += kPermThreads) {
+    const int r = base + tid;
+    const uint32_t e = r < R ? a.ids[r] : 0xFFFFFFFFu;
+    tile(r, e, (r < R && a.r_gate) ? a.gates[r] : 0.0f);
   }
 }
 
