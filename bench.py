@@ -328,13 +328,17 @@ def main():
     # ---- e2e through the host-buffer C-ABI call --------------------------
     e2e = None
     if n_stack == 1:
-        # pinned host buffers, as a serving loop keeps them; the library DMAs
-        # straight from and into them
-        h_host = [hs[i].cpu().pin_memory().numpy() for i in range(min(2, n_inputs))]
-        o_host = [torch.empty((T, H), dtype=torch.float32).pin_memory().numpy()
-                  for _ in range(2)]
-        i_host = np.empty((T, K), np.uint32)
-        g_host = np.empty((T, K), np.float32)
+        # pinned host buffers from the library (moe_host_alloc), kept across
+        # steps as a serving loop keeps them; the library DMAs straight from
+        # and into them
+        h_host = []
+        for i in range(min(2, n_inputs)):
+            buf = M.host_empty((T, H), np.float32)
+            buf[:] = hs[i].cpu().numpy()
+            h_host.append(buf)
+        o_host = [M.host_empty((T, H), np.float32) for _ in range(2)]
+        i_host = M.host_empty((T, K), np.uint32)
+        g_host = M.host_empty((T, K), np.float32)
 
         def host_step(i):
             eng.forward_host(i % n_layers, h_host[i % len(h_host)], out=o_host[i % 2],
@@ -509,8 +513,12 @@ def run_ep(args, cfg, rank, world, local):
     tokens = T * world
     value = tokens / (ms_max / 1e3)
     # e2e: host hidden states in (pinned), layer, host outputs back, per step
-    h_host = [hs[i].cpu().pin_memory() for i in range(2)]
-    o_host = [torch.empty((T, H), dtype=torch.float32).pin_memory() for _ in range(2)]
+    h_host = []
+    for i in range(2):
+        buf = M.host_empty((T, H), np.float32)
+        buf[:] = hs[i].cpu().numpy()
+        h_host.append(torch.from_numpy(buf))
+    o_host = [torch.from_numpy(M.host_empty((T, H), np.float32)) for _ in range(2)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist.barrier()
     e0.record(stream)

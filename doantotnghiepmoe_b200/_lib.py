@@ -67,6 +67,8 @@ SIGNATURES = {
     "moe_layer_forward": (I32, [P, I32, P, P, P, I32, P, P, P]),
     "moe_stack_forward": (I32, [P, I32, I32, P, I32, F32, P]),
     "moe_layer_forward_host": (I32, [P, I32, P, P, P, I32, P, P]),
+    "moe_host_alloc": (I32, [SZ, PP]),
+    "moe_host_free": (I32, [P]),
     "moe_sync_status": (I32, [P, P]),
     "moe_last_launch_count": (I32, [P]),
     "moe_synth_expert": (I32, [U64, I32, I32, I32, I32, P, P, P]),

@@ -406,6 +406,7 @@ struct moe_handle {
           *r_slot = nullptr, *r_pos = nullptr;
   float *h_pin_in = nullptr, *h_pin_out = nullptr;
   uint32_t *h_pin_status = nullptr;
+  float *h_pin_meta = nullptr;  // [2][max_tokens * top_k]: ids, gates
   cudaEvent_t stage_ev[16] = {};  // chunked staging of pageable host outputs
   int last_launches = 0;
   Profiler prof;
@@ -489,6 +490,7 @@ void free_handle(moe_handle *h) {
   cudaFreeHost(h->h_pin_in);
   cudaFreeHost(h->h_pin_out);
   cudaFreeHost(h->h_pin_status);
+  cudaFreeHost(h->h_pin_meta);
   for (auto ev : h->stage_ev)
     if (ev) cudaEventDestroy(ev);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
@@ -885,6 +887,7 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && cudaMallocHost(&h->h_pin_in, 2 * T * H * sizeof(float)) == cudaSuccess;
   ok = ok && cudaMallocHost(&h->h_pin_out, T * H * sizeof(float)) == cudaSuccess;
   ok = ok && cudaMallocHost(&h->h_pin_status, 64) == cudaSuccess;
+  ok = ok && cudaMallocHost(&h->h_pin_meta, 2 * T * K * sizeof(float)) == cudaSuccess;
   ok = ok && cudaMemset(h->status, 0, 4) == cudaSuccess;
   // tensor-core path scratch and the activation-side tensor maps
   const size_t R = T * K;
@@ -1248,18 +1251,24 @@ extern "C" moe_status moe_layer_forward_host(moe_handle *h, int layer, const flo
     st = layer_forward_locked(h, layer, h->io_in, h_resid ? h->io_resid : nullptr, h->io_out, T,
                               h->ids, h->gates, s);
     if (st != MOE_OK) return st;
+    // ids and gates: straight into pinned buffers, else through the handle's
+    // pinned staging (a copy into pageable memory would block the host)
+    const bool pin_ids = h_ids && host_is_pinned(h_ids);
+    const bool pin_gates = h_gates && host_is_pinned(h_gates);
+    uint32_t *ids_dst = pin_ids ? h_ids : reinterpret_cast<uint32_t *>(h->h_pin_meta);
+    float *gates_dst = pin_gates ? h_gates : h->h_pin_meta + R;
     // the status word travels back with the outputs and is cleared behind
     // them, so the call needs one stream synchronisation
-    auto status_back = [&] {
+    auto meta_back = [&] {
+      if (h_ids) cudaMemcpyAsync(ids_dst, h->ids, R * 4, cudaMemcpyDeviceToHost, s);
+      if (h_gates) cudaMemcpyAsync(gates_dst, h->gates, R * 4, cudaMemcpyDeviceToHost, s);
       cudaMemcpyAsync(h->h_pin_status, h->status, 4, cudaMemcpyDeviceToHost, s);
       cudaMemsetAsync(h->status, 0, 4, s);
     };
     cudaError_t e = cudaSuccess;
     if (host_is_pinned(h_out)) {
       cudaMemcpyAsync(h_out, h->io_out, bytes, cudaMemcpyDeviceToHost, s);
-      if (h_ids) cudaMemcpyAsync(h_ids, h->ids, R * 4, cudaMemcpyDeviceToHost, s);
-      if (h_gates) cudaMemcpyAsync(h_gates, h->gates, R * 4, cudaMemcpyDeviceToHost, s);
-      status_back();
+      meta_back();
       e = cudaStreamSynchronize(s);
     } else {
       // chunk i is copied out on the host while chunk i + 1 is in flight
@@ -1273,7 +1282,7 @@ extern "C" moe_status moe_layer_forward_host(moe_handle *h, int layer, const flo
                         cudaMemcpyDeviceToHost, s);
         cudaEventRecord(h->stage_ev[nc], s);
       }
-      status_back();
+      meta_back();
       for (int i = 0; i < nc && e == cudaSuccess; ++i) {
         e = cudaEventSynchronize(h->stage_ev[i]);
         const size_t o = (size_t)i * c;
@@ -1281,16 +1290,25 @@ extern "C" moe_status moe_layer_forward_host(moe_handle *h, int layer, const flo
           memcpy(reinterpret_cast<char *>(h_out) + o,
                  reinterpret_cast<char *>(h->h_pin_out) + o, std::min(c, bytes - o));
       }
-      if (e == cudaSuccess && h_ids)
-        e = cudaMemcpyAsync(h_ids, h->ids, R * 4, cudaMemcpyDeviceToHost, s);
-      if (e == cudaSuccess && h_gates)
-        e = cudaMemcpyAsync(h_gates, h->gates, R * 4, cudaMemcpyDeviceToHost, s);
       cudaError_t e2 = cudaStreamSynchronize(s);
       if (e == cudaSuccess) e = e2;
     }
+    if (e == cudaSuccess && h_ids && !pin_ids) memcpy(h_ids, ids_dst, R * 4);
+    if (e == cudaSuccess && h_gates && !pin_gates) memcpy(h_gates, gates_dst, R * 4);
     if (e != cudaSuccess) return cuda_fail(h, e, "layer_forward_host");
     return status_error(h, *h->h_pin_status);
   }
+}
+
+extern "C" moe_status moe_host_alloc(size_t bytes, void **out) {
+  if (!out || bytes == 0) return MOE_ERR_INVALID;
+  *out = nullptr;
+  return cudaHostAlloc(out, bytes, cudaHostAllocPortable) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+extern "C" moe_status moe_host_free(void *p) {
+  if (!p) return MOE_OK;
+  return cudaFreeHost(p) == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
 extern "C" int moe_last_launch_count(const moe_handle *h) { return h ? h->last_launches : 0; }

@@ -203,6 +203,34 @@ def synth_normal(seed: int, kind: int, layer: int, n: int, std: float) -> np.nda
 KIND_ROUTER, KIND_HIDDEN = 3, 4
 
 
+class _HostBlock:
+    """Owner of one moe_host_alloc() block; freed when the last array view
+    referring to it goes away."""
+
+    def __init__(self, nbytes: int):
+        p = ctypes.c_void_p()
+        st = lib().moe_host_alloc(nbytes, ctypes.byref(p))
+        if st != MOE_OK:
+            raise MoeError(st, "moe_host_alloc failed")
+        self.ptr = p.value
+
+    def __del__(self):
+        if getattr(self, "ptr", None):
+            lib().moe_host_free(self.ptr)
+            self.ptr = None
+
+
+def host_empty(shape, dtype=np.float32) -> np.ndarray:
+    """Pinned host array for MoeLayerEngine.forward_host (moe_host_alloc):
+    allocate once and reuse across calls."""
+    dtype = np.dtype(dtype)
+    n = int(np.prod(shape)) * dtype.itemsize
+    blk = _HostBlock(max(n, 1))
+    raw = (ctypes.c_ubyte * max(n, 1)).from_address(blk.ptr)
+    raw._moe_block = blk  # keeps the block alive while any view exists
+    return np.frombuffer(raw, dtype=dtype, count=int(np.prod(shape))).reshape(shape)
+
+
 def ep_unique_id() -> bytes:
     buf = (ctypes.c_ubyte * 128)()
     st = lib().moe_ep_unique_id(buf)

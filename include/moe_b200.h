@@ -164,10 +164,20 @@ moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_layers, float
                              float rms_eps, void *stream);
 
 /* Host-buffer variant of moe_layer_forward (copies in and out inside the
- * call, synchronous, checks the status word like the reference's `finite`). */
+ * call, synchronous, checks the status word like the reference's `finite`).
+ * Buffers in pinned host memory are read and written by DMA directly;
+ * pageable ones go through the handle's pinned staging in chunks.  Buffers
+ * from moe_host_alloc() take the fastest host-to-device path. */
 moe_status moe_layer_forward_host(moe_handle *h, int layer, const float *h_in,
                                   const float *h_resid, float *h_out, int T, uint32_t *h_ids,
                                   float *h_gates);
+
+/* Pinned host memory for the host-buffer calls (cudaHostAlloc, portable
+ * across devices), to be kept and reused across calls; free it with
+ * moe_host_free().  Device reads of it run at the link's full rate, which
+ * memory pinned after allocation (cudaHostRegister) may not reach. */
+moe_status moe_host_alloc(size_t bytes, void **out);
+moe_status moe_host_free(void *p);
 
 /* Synchronise the handle's stream (or `stream`), read and clear the device
  * status word: MOE_OK, MOE_ERR_NONFINITE or MOE_ERR_TIMEOUT. */

@@ -267,12 +267,20 @@ def test_host_buffers_pinned_and_staged():
     def pinned(a):
         return torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
 
-    for pin_in, pin_out in ((False, False), (True, True), (True, False), (False, True)):
-        hi = pinned(h) if pin_in else h.copy()
-        ri = pinned(resid) if pin_in else resid.copy()
-        out = pinned(np.zeros_like(h)) if pin_out else np.zeros_like(h)
-        got, ids, _ = eng.forward_host(0, hi, ri, out=out)
-        assert got is out
+    def lib_pinned(a):
+        buf = M.host_empty(a.shape, a.dtype)
+        buf[:] = a
+        return buf
+
+    for pin_in, pin_out in ((False, False), (True, True), (True, False), (False, True),
+                            (lib_pinned, lib_pinned)):
+        mk_in = pin_in if callable(pin_in) else (pinned if pin_in else np.copy)
+        mk_out = pin_out if callable(pin_out) else (pinned if pin_out else np.copy)
+        hi, ri = mk_in(h), mk_in(resid)
+        out = mk_out(np.zeros_like(h))
+        ids_buf = mk_out(np.zeros((T, 2), np.uint32))
+        got, ids, _ = eng.forward_host(0, hi, ri, out=out, ids=ids_buf)
+        assert got is out and ids is ids_buf
         assert np.array_equal(ids, want_ids)
         assert np.array_equal(bits(got), bits(want)), (pin_in, pin_out)
     with pytest.raises(ValueError):
