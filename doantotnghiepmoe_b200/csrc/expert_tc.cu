@@ -279,6 +279,26 @@ constexpr size_t smem_bytes(int na, int nb, int bn, int stages) {
 // Named barrier among the four epilogue warps (ids 1.., 128 threads).
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Max over the warp's 32 lanes of each of 16 per-lane values, as a butterfly
+// reduce-scatter: at each step a lane keeps half of its columns and folds in
+// its partner's copy of them, so 8 + 4 + 2 + 1 + 1 shuffles reduce all 16
+// columns.  Lane l ends with the maximum of column (l >> 1) & 15 (lanes l
+// and l ^ 1 hold the same column).  Exact: max does not depend on order.
+__device__ __forceinline__ float warp_colmax16(float (&m)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+    const bool hi = (lane & bit) != 0;
+#pragma unroll
+    for (int j = 0; j < half; ++j) {
+      const float send = hi ? m[j] : m[j + half];
+      const float keep = hi ? m[j + half] : m[j];
+      m[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, bit));
+    }
+  }
+  return fmaxf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 1));
+}
+
 // ---------------------------------------------------------------------------
 // GEMM 1: gate/up.  A = gate rows [m0, m0+128) and up rows [I+m0, ...) of
 // expert e; B = the two digit planes of the tile's routes.  BN routes per
@@ -325,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
 #pragma unroll
         for (int acc = 0; acc < 4; ++acc) tmem_ld16(trow + acc * BN + c0, v[acc]);
         tmem_wait_ld();
+        float mx[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int c = c0 + j;
@@ -339,12 +360,12 @@ __global__ void __launch_bounds__(kThreads, MINB)
             act = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
             if (i < a.I) a.act[(size_t)r * a.I + i] = act;
           }
-          // max |act| over this warp's 32 rows for route column c
-          float m = fabsf(act);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if (lane == 0 && c < nr) atomicMax(&a.act_amax[r0 + c], __float_as_uint(m));
+          mx[j] = fabsf(act);
         }
+        // max |act| over this warp's 32 rows, all 16 route columns at once
+        const float m = warp_colmax16(mx);
+        const int c = c0 + ((lane >> 1) & 15);
+        if ((lane & 1) == 0 && c < nr) atomicMax(&a.act_amax[r0 + c], __float_as_uint(m));
       }
     }
   }
@@ -620,6 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int acc = 0; acc < 4; ++acc) tmem_ld16(trow + acc * PBN + c0, v[acc]);
         tmem_wait_ld();
+        float mx[16];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const int c = c0 + jj;
@@ -634,11 +656,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             act = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
             if (i < I) a.act[(size_t)r * I + i] = act;
           }
-          float mx = fabsf(act);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          if (lane == 0 && c < nr) atomicMax(&a.act_amax[r0 + c], __float_as_uint(mx));
+          mx[jj] = fabsf(act);
         }
+        const float m = warp_colmax16(mx);
+        const int cm = c0 + ((lane >> 1) & 15);
+        if ((lane & 1) == 0 && cm < nr) atomicMax(&a.act_amax[r0 + cm], __float_as_uint(m));
       }
       fence_before_sync();
       __syncwarp();
