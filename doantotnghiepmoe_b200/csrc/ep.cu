@@ -290,9 +290,9 @@ __device__ void ep_dest_bases(const int32_t *cm, const int32_t *owner, int E, in
 
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const float *__restrict__ x, const int32_t *__restrict__ seg_off,
-    const int32_t *__restrict__ r_token, const int32_t *__restrict__ r_slot,
-    const float *__restrict__ r_gate, const int32_t *__restrict__ owner, int E, int R, int H,
-    EpP2P p, const uint32_t *epoch_p, uint32_t *done, uint32_t *status) {
+    const uint32_t *__restrict__ ids, const float *__restrict__ gates,
+    const int32_t *__restrict__ r_pos, const int32_t *__restrict__ owner, int E, int T, int K,
+    int H, EpP2P p, const uint32_t *epoch_p, uint32_t *done, uint32_t *status) {
   __shared__ int32_t tot[kMaxExperts], base[kMaxExperts], segs[kMaxExperts + 1];
   __shared__ int ok;
   const uint32_t epoch = *epoch_p;
@@ -310,15 +310,29 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
         reinterpret_cast<const int32_t *>(p.base[p.rank] + p.off_counts) + (size_t)par * p.nranks * E;
     ep_dest_bases(cm, owner, E, p.rank, p.nranks, tot, base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r = blockIdx.x * 8 + warp; r < R; r += gridDim.x * 8) {
-      int lo = 0, hi = E - 1;  // expert of permuted route r: last e with segs[e] <= r
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (segs[mid] <= r) lo = mid; else hi = mid - 1;
+    // one warp per token: the row is quantized once and stored at each of
+    // its K routes' rows in their owners' expert-sorted buffers
+    for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
+      int q = 0, pos = 0, slot_ok = 0;
+      float g = 0.0f;
+      if (lane < K) {
+        const uint32_t e = ids[(size_t)t * K + lane];
+        const int r = r_pos[(size_t)t * K + lane];
+        if (e < (uint32_t)E && r >= 0) {
+          q = owner[e];
+          pos = base[e] + (r - segs[e]);
+          g = gates[(size_t)t * K + lane];
+          slot_ok = 1;
+        }
       }
-      const int e = lo, q = owner[e];
-      const size_t pos = (size_t)base[e] + (r - segs[e]);
-      const int t = r_token[r];
+      const unsigned vmask = __ballot_sync(0xffffffffu, slot_ok);
+      uint8_t *dst[kMaxTopK];
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k) {
+        const int qk = __shfl_sync(0xffffffffu, q, k);
+        const int pk = __shfl_sync(0xffffffffu, pos, k);
+        dst[k] = peer_at(p, qk, p.off_xq) + (size_t)pk * H;
+      }
       const float *xr = x + (size_t)t * H;
       // the single-GPU tensor path's two-digit quantization of the row
       float amax = 0.0f;
@@ -330,8 +344,6 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
       const float inv = 1.0f / s;
-      uint8_t *qbase = peer_at(p, q, p.off_xq);
-      uint8_t *d1 = qbase + pos * H, *d2 = qbase + p.plane + pos * H;
       // 16 elements per lane per pass: 16-byte stores, 512 bytes per warp
       // instruction on the link (H is a multiple of 16)
       for (int c = lane * 16; c < H; c += 512) {
@@ -352,16 +364,22 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
           p1[w4] = b1;
           p2[w4] = b2;
         }
-        *reinterpret_cast<uint4 *>(d1 + c) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-        *reinterpret_cast<uint4 *>(d2 + c) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+        const uint4 v1 = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+        const uint4 v2 = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+#pragma unroll
+        for (int k = 0; k < kMaxTopK; ++k)
+          if ((vmask >> k) & 1u) {
+            *reinterpret_cast<uint4 *>(dst[k] + c) = v1;
+            *reinterpret_cast<uint4 *>(dst[k] + p.plane + c) = v2;
+          }
       }
-      if (lane == 0) {
+      if (slot_ok) {
         reinterpret_cast<float *>(peer_at(p, q, p.off_s1))[pos] = s;
         reinterpret_cast<float *>(peer_at(p, q, p.off_s2))[pos] = s / 254.0f;
-        reinterpret_cast<float *>(peer_at(p, q, p.off_gate))[pos] = r_gate[r];
+        reinterpret_cast<float *>(peer_at(p, q, p.off_gate))[pos] = g;
         reinterpret_cast<int32_t *>(peer_at(p, q, p.off_rank))[pos] = p.rank;
         reinterpret_cast<int32_t *>(peer_at(p, q, p.off_tok))[pos] = t;
-        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_slot))[pos] = r_slot[r];
+        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_slot))[pos] = lane;
         reinterpret_cast<uint32_t *>(peer_at(p, q, p.off_amax))[pos] = 0u;
       }
     }
@@ -468,11 +486,12 @@ cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uin
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const int32_t *r_token,
-                               const int32_t *r_slot, const float *r_gate, const int32_t *owner,
-                               int E, int R, int H, const EpP2P &p, const uint32_t *epoch,
+cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const uint32_t *ids,
+                               const float *gates, const int32_t *r_pos, const int32_t *owner,
+                               int E, int T, int K, int H, const EpP2P &p, const uint32_t *epoch,
                                uint32_t *done, int grid, uint32_t *status, cudaStream_t s) {
-  ep_dispatch_kernel<<<grid, 256, 0, s>>>(x, seg_off, r_token, r_slot, r_gate, owner, E, R, H, p,
+  if (K > kMaxTopK) return cudaErrorInvalidValue;
+  ep_dispatch_kernel<<<grid, 256, 0, s>>>(x, seg_off, ids, gates, r_pos, owner, E, T, K, H, p,
                                           epoch, done, status);
   return cudaGetLastError();
 }

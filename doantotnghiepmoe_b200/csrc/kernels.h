@@ -186,9 +186,12 @@ struct EpP2P {
 // advances it, every later kernel of the call reads it.
 cudaError_t launch_ep_publish(const int32_t *seg_off, int E, const EpP2P &p, uint32_t *epoch,
                               cudaStream_t s);
-cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const int32_t *r_token,
-                               const int32_t *r_slot, const float *r_gate, const int32_t *owner,
-                               int E, int R, int H, const EpP2P &p, const uint32_t *epoch,
+// One warp per token: quantize the row once, store it at each of its K
+// routes' rows in the owners' buffers (r_pos: route -> position in this
+// rank's expert-sorted order, as the permutation writes it).
+cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const uint32_t *ids,
+                               const float *gates, const int32_t *r_pos, const int32_t *owner,
+                               int E, int T, int K, int H, const EpP2P &p, const uint32_t *epoch,
                                uint32_t *done, int grid, uint32_t *status, cudaStream_t s);
 cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p,
                                 const uint32_t *epoch, int32_t *seg_l, int32_t *active_l,

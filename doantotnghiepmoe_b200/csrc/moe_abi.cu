@@ -372,6 +372,9 @@ struct EpState {
   float *xs1 = nullptr, *xs2 = nullptr, *as1 = nullptr, *as2 = nullptr;
   uint32_t *act_amax = nullptr;
   int32_t *tile_expert = nullptr, *tile_row0 = nullptr, *tile_rows = nullptr, *n_tiles = nullptr;
+  // the down GEMM's tile list when its width differs from the gate/up one
+  int32_t *dtile_expert = nullptr, *dtile_row0 = nullptr, *dtile_rows = nullptr,
+          *n_dtiles = nullptr;
   CUtensorMap map_x64{}, map_x128{}, map_a64{}, map_a128{};
   std::vector<void *> allocs;
   // device-driven exchange over NVLink peer memory (CUDA IPC)
@@ -1628,6 +1631,9 @@ extern "C" moe_status moe_ep_init(moe_handle *h, int rank, int nranks,
             ep_alloc(ep, &ep.tile_expert, ep.max_tiles) &&
             ep_alloc(ep, &ep.tile_row0, ep.max_tiles) &&
             ep_alloc(ep, &ep.tile_rows, ep.max_tiles) && ep_alloc(ep, &ep.n_tiles, 1) &&
+            ep_alloc(ep, &ep.dtile_expert, ep.max_tiles) &&
+            ep_alloc(ep, &ep.dtile_row0, ep.max_tiles) &&
+            ep_alloc(ep, &ep.dtile_rows, ep.max_tiles) && ep_alloc(ep, &ep.n_dtiles, 1) &&
             cudaMallocHost(&ep.h_counts, 2 * nranks * sizeof(int32_t)) == cudaSuccess;
   if (!ok) {
     free_ep(h);
@@ -1736,7 +1742,7 @@ moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const floa
     pa.r_token = h->r_token;
     pa.r_slot = h->r_slot;
     pa.r_gate = h->r_gate;
-    pa.r_pos = nullptr;
+    pa.r_pos = h->r_pos;
     pa.status = h->status;
     pa.scratch = h->perm_scratch;
     pa.scratch_words = h->perm_scratch_words;
@@ -1749,18 +1755,24 @@ moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const floa
   cudaEvent_t p1 = h->prof.begin(s);
   if (e == cudaSuccess) e = launch_ep_publish(h->seg_off, E, P, epoch, s);
   if (e == cudaSuccess)
-    e = launch_ep_dispatch(d_h, h->seg_off, h->r_token, h->r_slot, h->r_gate, ep.d_owner, E, R,
-                           H, P, epoch, ep.done, ep.dispatch_grid, h->status, s);
+    e = launch_ep_dispatch(d_h, h->seg_off, h->ids, h->gates, h->r_pos, ep.d_owner, E, T, K, H,
+                           P, epoch, ep.done, ep.dispatch_grid, h->status, s);
   h->prof.end("ep_dispatch", p1, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "ep dispatch");
   // 4. wait for every rank's routes; expert segments from the count matrix
   cudaEvent_t p2 = h->prof.begin(s);
   e = launch_ep_recv_prep(ep.d_owner, E, P, epoch, ep.seg_l, ep.active_l, ep.n_active_l,
                           ep.n_recv, h->status, s);
+  // tile widths from the expected receive count (this rank's own route
+  // count: the ranks route equal token counts)
   const int bn = tc::tc_block_n(std::max(R, 1), std::max(ep.E_local, 1));
+  const int dbn = tc::tc_block_n_down(std::max(R, 1), std::max(ep.E_local, 1));
   if (e == cudaSuccess && ep.E_local > 0)
     e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, bn, ep.tile_expert,
                                ep.tile_row0, ep.tile_rows, ep.n_tiles, ep.max_tiles, s);
+  if (e == cudaSuccess && ep.E_local > 0 && dbn != bn)
+    e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, dbn, ep.dtile_expert,
+                               ep.dtile_row0, ep.dtile_rows, ep.n_dtiles, ep.max_tiles, s);
   h->prof.end("ep_recv", p2, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "ep receive");
   // 5. experts; the down epilogue writes each output row to its source rank
@@ -1797,9 +1809,15 @@ moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const floa
       e = tc::launch_quantize_rows(ep.act, nullptr, a.act_amax, (int)RR, I, ep.aq, RR * I,
                                    ep.as1, ep.as2, nullptr, s, ep.n_recv);
     h->prof.end("tc_act_digits", p3, s);
+    if (dbn != bn) {
+      a.tile_expert = ep.dtile_expert;
+      a.tile_row0 = ep.dtile_row0;
+      a.tile_rows = ep.dtile_rows;
+      a.n_tiles = ep.n_dtiles;
+    }
     p3 = h->prof.begin(s);
     if (e == cudaSuccess)
-      e = tc::launch_down_tc(EL.map_dn, bn == 64 ? ep.map_a64 : ep.map_a128, a, bn,
+      e = tc::launch_down_tc(EL.map_dn, dbn == 64 ? ep.map_a64 : ep.map_a128, a, dbn,
                              ep.max_tiles, s);
     h->prof.end("down_tc", p3, s);
     if (e != cudaSuccess) return cuda_fail(h, e, "ep experts");
@@ -1938,9 +1956,13 @@ extern "C" moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float
       e = launch_ep_unpack_digits(ep.recv, ep.rtok_l, Rri, H, ep.xq, RR * H, ep.xs1, ep.xs2,
                                   ep.act_amax, s);
     const int bn = tc::tc_block_n(Rri, ep.E_local);
+    const int dbn = tc::tc_block_n_down(Rri, ep.E_local);
     if (e == cudaSuccess)
       e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, bn, ep.tile_expert,
                                  ep.tile_row0, ep.tile_rows, ep.n_tiles, ep.max_tiles, s);
+    if (e == cudaSuccess && dbn != bn)
+      e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, dbn, ep.dtile_expert,
+                                 ep.dtile_row0, ep.dtile_rows, ep.n_dtiles, ep.max_tiles, s);
     h->prof.end("ep_unpack", p2, s);
     tc::TcArgs a{};
     a.H = H;
@@ -1973,9 +1995,17 @@ extern "C" moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float
       e = tc::launch_quantize_rows(ep.act, nullptr, ep.act_amax, Rri, I, ep.aq, RR * I, ep.as1,
                                    ep.as2, nullptr, s);
     h->prof.end("tc_act_digits", p3, s);
+    int dtiles = tiles;
+    if (dbn != bn) {
+      a.tile_expert = ep.dtile_expert;
+      a.tile_row0 = ep.dtile_row0;
+      a.tile_rows = ep.dtile_rows;
+      a.n_tiles = ep.n_dtiles;
+      dtiles = std::min(ep.max_tiles, (Rri + dbn - 1) / dbn + std::min(ep.E_local, Rri));
+    }
     p3 = h->prof.begin(s);
     if (e == cudaSuccess)
-      e = tc::launch_down_tc(EL.map_dn, bn == 64 ? ep.map_a64 : ep.map_a128, a, bn, tiles, s);
+      e = tc::launch_down_tc(EL.map_dn, dbn == 64 ? ep.map_a64 : ep.map_a128, a, dbn, dtiles, s);
     h->prof.end("down_tc", p3, s);
     if (e != cudaSuccess) return cuda_fail(h, e, "ep experts");
   }
