@@ -466,14 +466,45 @@ __global__ void ep_wait_combine_kernel(EpP2P p, const uint32_t *epoch_p,
   if (!ok) return;
   const float *contrib = reinterpret_cast<const float *>(p.base[p.rank] + p.off_contrib);
   bool bad = false;
-  const size_t n = (size_t)T * H;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t t = i / H, j = i % H;
-    float acc = resid ? resid[i] : 0.0f;
-    for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __ldcg(contrib + (t * K + k) * H + j));
-    bad |= !is_finite_f(acc);
-    out[i] = acc;
+  // slot order as the single-GPU combine; 4 columns per thread, all K slot
+  // loads issued before the first add (the peers' stores reached this
+  // buffer before their flags C, so the loads bypass L1)
+  const bool vec = (H & 3) == 0 && K <= kMaxTopK &&
+                   (((uintptr_t)out | (uintptr_t)resid | (uintptr_t)contrib) & 15) == 0 &&
+                   (size_t)T * H / 4 < (1u << 31);
+  if (vec) {
+    const uint32_t H4 = H / 4, n4 = (uint32_t)((size_t)T * H / 4);
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += gridDim.x * blockDim.x) {
+      const uint32_t t = i / H4, j4 = i - t * H4;
+      float4 acc = resid ? reinterpret_cast<const float4 *>(resid)[i] : make_float4(0, 0, 0, 0);
+      const float4 *c = reinterpret_cast<const float4 *>(contrib) + (size_t)t * K * H4 + j4;
+      float4 v[kMaxTopK];
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K) v[k] = __ldcg(c + (size_t)k * H4);
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K) {
+          acc.x = __fadd_rn(acc.x, v[k].x);
+          acc.y = __fadd_rn(acc.y, v[k].y);
+          acc.z = __fadd_rn(acc.z, v[k].z);
+          acc.w = __fadd_rn(acc.w, v[k].w);
+        }
+      bad |= !(is_finite_f(acc.x) && is_finite_f(acc.y) && is_finite_f(acc.z) &&
+               is_finite_f(acc.w));
+      reinterpret_cast<float4 *>(out)[i] = acc;
+    }
+  } else {
+    const size_t n = (size_t)T * H;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+      const size_t t = i / H, j = i % H;
+      float acc = resid ? resid[i] : 0.0f;
+      for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __ldcg(contrib + (t * K + k) * H + j));
+      bad |= !is_finite_f(acc);
+      out[i] = acc;
+    }
   }
   if (bad) set_status(status, kStatusNonFinite);
 }
