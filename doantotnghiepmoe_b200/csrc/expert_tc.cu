@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
 // digit planes of the tile's activations.  Epilogue writes gate * y into the
 // (token, slot) contribution row.
 // ---------------------------------------------------------------------------
-template <int BN, int S, int MINB, int NA>
+template <int BN, int S, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB)
     down_tc_kernel(const __grid_constant__ CUtensorMap mapW,
                    const __grid_constant__ CUtensorMap mapA, TcArgs a) {
@@ -388,14 +388,12 @@ __global__ void __launch_bounds__(kThreads, MINB)
   RouteTab &tab = *reinterpret_cast<RouteTab *>(smem_raw + sizeof(Pipe));
   uint8_t *tiles = align1024(smem_raw + sizeof(Pipe) + sizeof(RouteTab));
   const int e = a.tile_expert[g], r0 = a.tile_row0[g], nr = a.tile_rows[g];
-  const int m0 = blockIdx.x * (NA * BM);
+  const int m0 = blockIdx.x * BM;
   const int nk = (a.I + BK - 1) / BK;
-  constexpr uint32_t kCols = NA * 2 * BN;
+  constexpr uint32_t kCols = 2 * BN;
   setup(pp, S, kCols);
-  int arow[NA];
-#pragma unroll
-  for (int x = 0; x < NA; ++x) arow[x] = m0 + x * BM;
-  mainloop<NA, 2, S, BN>(pp, tiles, &mapW, &mapA, arow, e, r0, nk, pp.tmem_base);
+  const int arow[1] = {m0};
+  mainloop<1, 2, S, BN>(pp, tiles, &mapW, &mapA, arow, e, r0, nk, pp.tmem_base);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= 2) {
     for (int c = threadIdx.x - 64; c < nr; c += 128) {
@@ -408,12 +406,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
       tab.rank[c] = a.r_rank ? a.r_rank[r] : 0;
     }
     const int q = warp & 3;
-    float sd[NA];
-#pragma unroll
-    for (int x = 0; x < NA; ++x) {
-      const int j = m0 + x * BM + 32 * q + lane;  // output row (hidden index)
-      sd[x] = j < a.H ? a.s_ptr[e][2 * a.I + j] : 0.0f;
-    }
+    const int j = m0 + 32 * q + lane;  // output row (hidden index)
+    const float sd = j < a.H ? a.s_ptr[e][2 * a.I + j] : 0.0f;
     epi_sync();
     bool ok = mbar_wait(&pp.done, 0, &pp.abort_flag);
     if (!ok) pp.abort_flag = 1;
@@ -422,27 +416,22 @@ __global__ void __launch_bounds__(kThreads, MINB)
       fence_after_sync();
       const uint32_t trow = pp.tmem_base + ((uint32_t)(32 * q) << 16);
       bool bad = false;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (c0 >= nr) break;
+        int32_t v[2][16];
+        tmem_ld16(trow + c0, v[0]);
+        tmem_ld16(trow + BN + c0, v[1]);
+        tmem_wait_ld();
 #pragma unroll
-      for (int x = 0; x < NA; ++x) {
-        const int j = m0 + x * BM + 32 * q + lane;
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          if (c0 >= nr) break;
-          int32_t v[2][16];
-          tmem_ld16(trow + (2 * x) * BN + c0, v[0]);
-          tmem_ld16(trow + (2 * x + 1) * BN + c0, v[1]);
-          tmem_wait_ld();
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int c = c0 + jj;
-            if (c < nr && j < a.H) {
-              const float y =
-                  fmaf(tab.s1[c], (float)v[0][jj], tab.s2[c] * (float)v[1][jj]) * sd[x];
-              bad |= !is_finite_f(y);
-              // expert parallelism: the row goes straight to the source rank's
-              // contribution buffer (peer memory over NVLink)
-              float *dst = a.r_rank ? a.peer_contrib[tab.rank[c]] : a.contrib;
-              dst[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + j] = __fmul_rn(tab.gate[c], y);
-            }
+        for (int jj = 0; jj < 16; ++jj) {
+          const int c = c0 + jj;
+          if (c < nr && j < a.H) {
+            const float y = fmaf(tab.s1[c], (float)v[0][jj], tab.s2[c] * (float)v[1][jj]) * sd;
+            bad |= !is_finite_f(y);
+            // expert parallelism: the row goes straight to the source rank's
+            // contribution buffer (peer memory over NVLink)
+            float *dst = a.r_rank ? a.peer_contrib[tab.rank[c]] : a.contrib;
+            dst[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + j] = __fmul_rn(tab.gate[c], y);
           }
         }
       }
@@ -973,15 +962,6 @@ int persistent_mode() {
 bool persistent_gu() { return persistent_mode() == 1 || persistent_mode() == 3; }
 bool persistent_dn() { return persistent_mode() == 1 || persistent_mode() == 2; }
 
-bool down_two_tiles() {
-  static int v = -1;
-  if (v < 0) {
-    const char *env = getenv("MOE_TC_DN_NA");
-    v = (env && env[0] == '1') ? 0 : 1;
-  }
-  return v == 1;
-}
-
 int tc_bn_dn_override() {
   static int v = -1;
   if (v < 0) {
@@ -1016,13 +996,13 @@ cudaError_t launch_gu(const CUtensorMap &mapW, const CUtensorMap &mapX, const Tc
   return cudaGetLastError();
 }
 
-template <int BN, int S, int MINB, int NA = 1>
+template <int BN, int S, int MINB>
 cudaError_t launch_dn(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
                       int max_tiles, cudaStream_t s) {
-  const size_t smem = smem_bytes(NA, 2, BN, S);
-  auto k = down_tc_kernel<BN, S, MINB, NA>;
+  const size_t smem = smem_bytes(1, 2, BN, S);
+  auto k = down_tc_kernel<BN, S, MINB>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid((a.H + NA * BM - 1) / (NA * BM), max_tiles);
+  dim3 grid((a.H + BM - 1) / BM, max_tiles);
   k<<<grid, kThreads, smem, s>>>(mapW, mapA, a);
   return cudaGetLastError();
 }
@@ -1067,10 +1047,6 @@ cudaError_t launch_down_tc(const CUtensorMap &mapW, const CUtensorMap &mapA, con
     k<<<grid, kThreads, smem, s>>>(mapW, mapA, a);
     return cudaGetLastError();
   }
-  // 64-route tiles: two 128-row weight tiles per CTA (half the CTAs and half
-  // the digit-tile reads) when H allows it; MOE_TC_DN_NA=1 keeps one.
-  if (bn == 64 && a.H % (2 * BM) == 0 && down_two_tiles())
-    return launch_dn<64, 2, 2, 2>(mapW, mapA, a, max_tiles, s);
   return bn == 64 ? launch_dn<64, 3, 2>(mapW, mapA, a, max_tiles, s)
                   : launch_dn<128, 2, 2>(mapW, mapA, a, max_tiles, s);
 }
