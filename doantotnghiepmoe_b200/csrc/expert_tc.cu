@@ -835,8 +835,25 @@ __global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_
 // its K routes' expert-sorted rows (r_pos; negative or out-of-range
 // positions, which invalid routes leave, are skipped), with the per-route
 // scales; the routes' activation amax is cleared for the gate/up epilogue.
-constexpr int kQtThreads = 256;
-__global__ void __launch_bounds__(kQtThreads) quantize_tokens_kernel(
+// A thread owns 16 consecutive elements per pass (n % 16 == 0), so every
+// digit store is 16 bytes.
+constexpr int kQtThreads = 128;
+__device__ __forceinline__ uint32_t digits4(const float4 v, float inv, uint32_t &hi) {
+  const float in[4] = {v.x, v.y, v.z, v.w};
+  uint32_t p1 = 0, p2 = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float u = in[k] * inv;
+    const float a1 = fminf(fmaxf(rintf(u), -127.0f), 127.0f);
+    const float a2 = fminf(fmaxf(rintf((u - a1) * 254.0f), -127.0f), 127.0f);
+    p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
+    p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
+  }
+  hi = p2;
+  return p1;
+}
+
+__global__ void __launch_bounds__(kQtThreads, 4) quantize_tokens_kernel(
     const float *__restrict__ x, const int32_t *__restrict__ r_pos, int T, int K, int n,
     int8_t *__restrict__ q, size_t plane, float *__restrict__ s1, float *__restrict__ s2,
     uint32_t *__restrict__ amax_reset) {
@@ -845,11 +862,14 @@ __global__ void __launch_bounds__(kQtThreads) quantize_tokens_kernel(
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t R = (uint32_t)T * (uint32_t)K;
   if (tid < K) pos_s[tid] = r_pos[(size_t)t * K + tid];
-  const float *row = x + (size_t)t * n;
+  const float4 *row = reinterpret_cast<const float4 *>(x + (size_t)t * n);
   float amax = 0.0f;
-  for (int c = tid * 4; c < n; c += kQtThreads * 4) {
-    const float4 v = *reinterpret_cast<const float4 *>(row + c);
-    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  for (int c = tid * 16; c < n; c += kQtThreads * 16) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float4 v = row[c / 4 + w];
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -862,23 +882,17 @@ __global__ void __launch_bounds__(kQtThreads) quantize_tokens_kernel(
   int pos[kMaxTopK];
 #pragma unroll
   for (int k = 0; k < kMaxTopK; ++k) pos[k] = k < K ? pos_s[k] : -1;
-  for (int c = tid * 4; c < n; c += kQtThreads * 4) {
-    const float4 v = *reinterpret_cast<const float4 *>(row + c);
-    const float in[4] = {v.x, v.y, v.z, v.w};
-    uint32_t p1 = 0, p2 = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float u = in[k] * inv;
-      const float a1 = fminf(fmaxf(rintf(u), -127.0f), 127.0f);
-      const float a2 = fminf(fmaxf(rintf((u - a1) * 254.0f), -127.0f), 127.0f);
-      p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
-      p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
-    }
+  for (int c = tid * 16; c < n; c += kQtThreads * 16) {
+    uint4 lo, hi;
+    lo.x = digits4(row[c / 4 + 0], inv, hi.x);
+    lo.y = digits4(row[c / 4 + 1], inv, hi.y);
+    lo.z = digits4(row[c / 4 + 2], inv, hi.z);
+    lo.w = digits4(row[c / 4 + 3], inv, hi.w);
 #pragma unroll
     for (int k = 0; k < kMaxTopK; ++k)
       if ((uint32_t)pos[k] < R) {
-        *reinterpret_cast<uint32_t *>(q + (size_t)pos[k] * n + c) = p1;
-        *reinterpret_cast<uint32_t *>(q + plane + (size_t)pos[k] * n + c) = p2;
+        *reinterpret_cast<uint4 *>(q + (size_t)pos[k] * n + c) = lo;
+        *reinterpret_cast<uint4 *>(q + plane + (size_t)pos[k] * n + c) = hi;
       }
   }
   if (tid < K && (uint32_t)pos_s[tid] < R) {
@@ -941,7 +955,7 @@ cudaError_t launch_quantize_tokens(const float *x, const int32_t *r_pos, int T, 
                                    int8_t *q, size_t plane, float *s1, float *s2,
                                    uint32_t *amax_reset, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  if (K > kMaxTopK) return cudaErrorInvalidValue;
+  if (K > kMaxTopK || n % 16) return cudaErrorInvalidValue;
   quantize_tokens_kernel<<<T, kQtThreads, 0, s>>>(x, r_pos, T, K, n, q, plane, s1, s2,
                                                   amax_reset);
   return cudaGetLastError();

@@ -60,6 +60,7 @@ struct PermuteArgs {
 };
 size_t permute_scratch_words(int R, int E);
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t s);
+int permute_launches(const PermuteArgs &a);  // kernels launch_permute enqueues
 
 // Grouped INT8 GEMV over expert segments (expert_gemv.cu), in the exact
 // reduction order of the reference's AVX2 kernels.

@@ -617,7 +617,7 @@ moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T,
   e = launch_permute(pa, s);
   h->prof.end("permute", p0, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "permute launch");
-  h->last_launches += 1;
+  h->last_launches += permute_launches(pa);
   return MOE_OK;
 }
 
@@ -1748,6 +1748,7 @@ moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const floa
     pa.scratch_words = h->perm_scratch_words;
     e = launch_permute(pa, s);
     h->prof.end("permute", p0, s);
+    h->last_launches += permute_launches(pa);
   } else {
     e = cudaMemsetAsync(h->seg_off, 0, (E + 1) * sizeof(int32_t), s);
   }
@@ -1829,7 +1830,9 @@ moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const floa
     e = launch_ep_wait_combine(P, epoch, d_resid, d_out, T, K, H, h->status, s);
   h->prof.end("ep_combine", p4, s);
   if (e != cudaSuccess) return cuda_fail(h, e, "ep combine");
-  h->last_launches += 11;
+  // publish, dispatch, receive, signal, combine; tile lists and the three
+  // expert kernels when this rank owns experts
+  h->last_launches += 5 + (ep.E_local > 0 ? 4 + (dbn != bn ? 1 : 0) : 0);
   return MOE_OK;
 }
 }  // namespace

@@ -662,6 +662,14 @@ int perm_single_max() {
   return v;
 }
 
+int permute_launches(const PermuteArgs &a) {
+  const int R = a.T * a.K;
+  return (R <= perm_single_max() || !a.scratch ||
+          a.scratch_words < permute_scratch_words(R, a.E))
+             ? 1
+             : 3;
+}
+
 cudaError_t launch_permute(const PermuteArgs &a, cudaStream_t s) {
   const int R = a.T * a.K;
   if (R <= perm_single_max() || !a.scratch ||
