@@ -9,5 +9,5 @@ reference's interfaces:
 """
 from ._lib import LIB_PATH, MoeDims, MoeError, lib  # noqa: F401
 from .gpu_expert import GpuExpertKernels, GpuExpertWeights  # noqa: F401
-from .layer import (MoeConfig, MoeLayerEngine, host_empty, synth_expert,  # noqa: F401
-                    synth_normal)
+from .layer import (Checkpoint, MoeConfig, MoeLayerEngine, host_empty,  # noqa: F401
+                    synth_expert, synth_normal)

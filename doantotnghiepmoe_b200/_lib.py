@@ -67,6 +67,14 @@ SIGNATURES = {
     "moe_layer_forward": (I32, [P, I32, P, P, P, I32, P, P, P]),
     "moe_stack_forward": (I32, [P, I32, I32, P, I32, F32, P]),
     "moe_layer_forward_host": (I32, [P, I32, P, P, P, I32, P, P]),
+    "moe_ckpt_open": (I32, [ctypes.c_char_p, PP, ctypes.c_char_p, SZ]),
+    "moe_ckpt_close": (None, [P]),
+    "moe_ckpt_num_tensors": (I32, [P]),
+    "moe_ckpt_tensor_info": (I32, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int),
+                                   ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int64),
+                                   ctypes.POINTER(ctypes.c_size_t)]),
+    "moe_ckpt_read": (I32, [P, ctypes.c_char_p, P, SZ]),
+    "moe_load_layer": (I32, [P, P, I32, I32, I32]),
     "moe_host_alloc": (I32, [SZ, PP]),
     "moe_host_free": (I32, [P]),
     "moe_sync_status": (I32, [P, P]),

@@ -19,6 +19,7 @@
 #include "common.cuh"
 #include "expert_tc.h"
 #include "kernels.h"
+#include "ckpt.h"
 
 using namespace moe;
 
@@ -301,6 +302,8 @@ struct LayerSlot {
   // tensor-core path: only for the packed layout (one 3D tensor map per GEMM)
   bool tc_ok = false;
   CUtensorMap map_gu{}, map_dn{};
+  // device copies made by moe_load_layer (owned by the handle)
+  void *own_w = nullptr, *own_s = nullptr, *own_r = nullptr;
 };
 }  // namespace
 
@@ -481,6 +484,9 @@ void free_handle(moe_handle *h) {
   for (auto &l : h->layers) {
     cudaFree(l.d_wptr);
     cudaFree(l.d_sptr);
+    cudaFree(l.own_w);
+    cudaFree(l.own_s);
+    cudaFree(l.own_r);
   }
   void *ptrs[] = {h->logits,  h->gates,     h->r_gate,    h->act,       h->contrib, h->hbuf,
                   h->io_in,   h->io_out,    h->io_resid,  h->ids,       h->status,  h->seg_off,
@@ -1034,6 +1040,149 @@ extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const 
       cudaMemcpy(h->d_flayers + layer, &F, sizeof(FusedLayer), cudaMemcpyHostToDevice);
   if (e3 != cudaSuccess) return cuda_fail(h, e3, "set_layer");
   L.set = true;
+  if (L.own_w && L.own_w != d_weights[0]) {  // the slot no longer uses a loaded copy
+    cudaFree(L.own_w);
+    cudaFree(L.own_s);
+    cudaFree(L.own_r);
+    L.own_w = L.own_s = L.own_r = nullptr;
+  }
+  return MOE_OK;
+}
+
+namespace {
+// IEEE binary16 -> binary32, exact (every half is a float).
+float half_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+  uint32_t bits;
+  if (exp == 0x1F) {
+    bits = sign | 0x7F800000u | (man << 13);  // inf / nan
+  } else if (exp != 0) {
+    bits = sign | ((exp + 112u) << 23) | (man << 13);
+  } else if (man == 0) {
+    bits = sign;  // signed zero
+  } else {  // subnormal half: normalise
+    int e = -1;
+    do {
+      man <<= 1;
+      ++e;
+    } while (!(man & 0x400u));
+    bits = sign | ((uint32_t)(112 - e) << 23) | ((man & 0x3FFu) << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+}  // namespace
+
+extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_layer,
+                                     int layer, int keep_bf16) {
+  if (!h || !c || ckpt_layer < 0) return MOE_ERR_INVALID;
+  const size_t E = h->d.num_experts, H = h->d.hidden, I = h->d.intermediate;
+  const size_t wcount = 3 * I * H, scount = 2 * I + H;
+  auto fail = [&](moe_status st, const std::string &m) {
+    std::lock_guard<std::mutex> lock(h->mu);
+    set_err(h->err, "%s", m.c_str());
+    return st;
+  };
+  if (layer < 0 || layer >= (int)h->layers.size()) return fail(MOE_ERR_INVALID, "layer out of range");
+  // descriptors first, no payload read (src/olmoe.rs:1080-1099)
+  std::vector<const CkptTensor *> wt(E), st(E);
+  for (size_t e = 0; e < E; ++e) {
+    const std::string pre = "model.layers." + std::to_string(ckpt_layer) + ".mlp.experts." +
+                            std::to_string(e);
+    wt[e] = ckpt_find(c, pre + ".merged_weight");
+    st[e] = ckpt_find(c, pre + ".qs");
+    if (!wt[e]) return fail(MOE_ERR_INVALID, "missing tensor: " + pre + ".merged_weight");
+    if (!st[e]) return fail(MOE_ERR_INVALID, "missing tensor: " + pre + ".qs");
+    const auto &ws = wt[e]->shape;
+    if (wt[e]->dtype == MOE_DT_U8 && ws.size() == 1 && (size_t)ws[0] == wcount / 2)
+      return fail(MOE_ERR_INVALID, pre + ": INT4 experts are not supported on this path");
+    if (wt[e]->dtype != MOE_DT_I8 || ws.size() != 1 || (size_t)ws[0] != wcount ||
+        st[e]->dtype != MOE_DT_F32 || st[e]->shape.size() != 1 ||
+        (size_t)st[e]->shape[0] != scount)
+      return fail(MOE_ERR_INVALID, pre + ": invalid merged expert layout");
+  }
+  const std::string rname = "model.layers." + std::to_string(ckpt_layer) + ".mlp.gate.weight";
+  const CkptTensor *rt = ckpt_find(c, rname);
+  if (!rt) return fail(MOE_ERR_INVALID, "missing tensor: " + rname);
+  if (rt->shape.size() != 2 || (size_t)rt->shape[0] != E || (size_t)rt->shape[1] != H ||
+      (rt->dtype != MOE_DT_F32 && rt->dtype != MOE_DT_BF16 && rt->dtype != MOE_DT_F16))
+    return fail(MOE_ERR_INVALID, rname + ": incorrect shape or dtype");
+  // router on the host: finite values, kept bf16 or widened to f32
+  std::vector<uint8_t> raw(rt->bytes);
+  if (!ckpt_read(c, *rt, raw.data())) return fail(MOE_ERR_INVALID, rname + ": short read");
+  const bool bf16 = rt->dtype == MOE_DT_BF16 && keep_bf16;
+  std::vector<float> rf(E * H);
+  for (size_t i = 0; i < E * H; ++i) {
+    if (rt->dtype == MOE_DT_F32) {
+      memcpy(&rf[i], &raw[4 * i], 4);
+    } else {
+      uint16_t b;
+      memcpy(&b, &raw[2 * i], 2);
+      if (rt->dtype == MOE_DT_F16) {
+        rf[i] = half_to_float(b);
+      } else {
+        const uint32_t bits = (uint32_t)b << 16;
+        memcpy(&rf[i], &bits, 4);
+      }
+    }
+    if (!std::isfinite(rf[i])) return fail(MOE_ERR_NONFINITE, rname + ": non-finite value");
+  }
+  DeviceGuard g(h->device);
+  int8_t *dw = nullptr;
+  float *ds = nullptr;
+  void *dr = nullptr;
+  uint8_t *stage = nullptr;
+  auto release = [&] {
+    cudaFree(dw);
+    cudaFree(ds);
+    cudaFree(dr);
+    cudaFreeHost(stage);
+  };
+  if (cudaMalloc(&dw, E * wcount) != cudaSuccess || cudaMalloc(&ds, E * scount * 4) != cudaSuccess ||
+      cudaMalloc(&dr, bf16 ? E * H * 2 : E * H * 4) != cudaSuccess ||
+      cudaMallocHost(&stage, wcount + scount * 4) != cudaSuccess) {
+    release();
+    return fail(MOE_ERR_NOMEM, "moe_load_layer: out of memory");
+  }
+  // experts one by one through a pinned staging buffer
+  for (size_t e = 0; e < E; ++e) {
+    float *sc = reinterpret_cast<float *>(stage + wcount);
+    if (!ckpt_read(c, *wt[e], stage) || !ckpt_read(c, *st[e], sc)) {
+      release();
+      return fail(MOE_ERR_INVALID, "expert " + std::to_string(e) + ": short read");
+    }
+    for (size_t i = 0; i < scount; ++i)
+      if (!std::isfinite(sc[i]) || !(sc[i] > 0.0f)) {  // src/int8_expert.rs:151-153
+        release();
+        return fail(MOE_ERR_INVALID, "expert scales must be finite and positive");
+      }
+    if (cudaMemcpy(dw + e * wcount, stage, wcount, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(ds + e * scount, sc, scount * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+      release();
+      return fail(MOE_ERR_CUDA, "moe_load_layer: upload failed");
+    }
+  }
+  const cudaError_t ce = bf16 ? cudaMemcpy(dr, raw.data(), E * H * 2, cudaMemcpyHostToDevice)
+                              : cudaMemcpy(dr, rf.data(), E * H * 4, cudaMemcpyHostToDevice);
+  cudaFreeHost(stage);
+  stage = nullptr;
+  if (ce != cudaSuccess) {
+    release();
+    return fail(MOE_ERR_CUDA, "moe_load_layer: router upload failed");
+  }
+  const moe_status st2 =
+      moe_set_layer_packed(h, layer, dw, ds, dr, bf16 ? MOE_ROUTER_BF16 : MOE_ROUTER_F32);
+  if (st2 != MOE_OK) {
+    release();
+    return st2;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  LayerSlot &L = h->layers[layer];
+  L.own_w = dw;
+  L.own_s = ds;
+  L.own_r = dr;
   return MOE_OK;
 }
 

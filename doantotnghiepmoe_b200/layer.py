@@ -142,6 +142,12 @@ class MoeLayerEngine:
                                                  gates.ctypes.data))
         return out, ids, gates
 
+    def load_layer(self, ckpt: "Checkpoint", ckpt_layer: int, layer: int | None = None,
+                   keep_bf16: bool = True):
+        """moe_load_layer: checkpoint layer -> device copy owned by the engine."""
+        self._check(lib().moe_load_layer(self._h, ckpt._c, ckpt_layer,
+                                         ckpt_layer if layer is None else layer, int(keep_bf16)))
+
     def sync_status(self, stream=None):
         self._check(lib().moe_sync_status(self._h, _stream(stream)))
 
@@ -201,6 +207,52 @@ def synth_normal(seed: int, kind: int, layer: int, n: int, std: float) -> np.nda
 
 
 KIND_ROUTER, KIND_HIDDEN = 3, 4
+
+
+_DT = {0: ("U8", np.uint8), 1: ("I8", np.int8), 2: ("F16", np.float16),
+       3: ("BF16", np.uint16), 4: ("F32", np.float32)}
+
+
+class Checkpoint:
+    """A directory of merged-INT8 safetensors shards (moe_ckpt_open); BF16
+    payloads come back as their uint16 bit patterns."""
+
+    def __init__(self, directory: str):
+        c = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        st = lib().moe_ckpt_open(directory.encode(), ctypes.byref(c), err, len(err))
+        if st != MOE_OK:
+            raise MoeError(st, err.value.decode(errors="replace"))
+        self._c = c.value
+
+    def close(self):
+        if getattr(self, "_c", None):
+            lib().moe_ckpt_close(self._c)
+            self._c = None
+
+    def __del__(self):
+        self.close()
+
+    def __len__(self) -> int:
+        return int(lib().moe_ckpt_num_tensors(self._c))
+
+    def info(self, name: str):
+        dt, nd = ctypes.c_int(), ctypes.c_int()
+        shape = (ctypes.c_int64 * 8)()
+        nbytes = ctypes.c_size_t()
+        st = lib().moe_ckpt_tensor_info(self._c, name.encode(), ctypes.byref(dt), ctypes.byref(nd),
+                                        shape, ctypes.byref(nbytes))
+        if st != MOE_OK:
+            raise MoeError(st, f"missing tensor: {name}")
+        return _DT[dt.value][0], tuple(shape[i] for i in range(nd.value)), int(nbytes.value)
+
+    def read(self, name: str) -> np.ndarray:
+        dname, shape, nbytes = self.info(name)
+        out = np.empty(shape, _DT[[k for k, v in _DT.items() if v[0] == dname][0]][1])
+        st = lib().moe_ckpt_read(self._c, name.encode(), out.ctypes.data, nbytes)
+        if st != MOE_OK:
+            raise MoeError(st, f"read failed: {name}")
+        return out
 
 
 class _HostBlock:

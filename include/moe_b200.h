@@ -254,6 +254,37 @@ moe_status moe_profile_enable(moe_handle *h, int enable);
 moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int max_entries,
                             int *n_entries);
 
+/* ---- Merged-INT8 checkpoints --------------------------------------------
+ * The safetensors shards written by the reference's converter
+ * (tools/prepare_olmoe.py:85-94): per expert
+ * `model.layers.{l}.mlp.experts.{e}.merged_weight` I8 [3*I*H] = [gate I x H |
+ * up I x H | down H x I] and `.qs` F32 [2*I + H]; the router
+ * `model.layers.{l}.mlp.gate.weight` F32, BF16 or F16 [E, H].  The shard
+ * index makes the header checks of the reference's TensorIndex
+ * (src/safetensors.rs:90-181) and rejects a malformed shard with
+ * MOE_ERR_INVALID and the reason in `err`. */
+typedef struct moe_ckpt moe_ckpt;
+enum { MOE_DT_U8 = 0, MOE_DT_I8 = 1, MOE_DT_F16 = 2, MOE_DT_BF16 = 3, MOE_DT_F32 = 4 };
+/* Index every *.safetensors file in `dir` (headers only). */
+moe_status moe_ckpt_open(const char *dir, moe_ckpt **out, char *err, size_t err_len);
+void moe_ckpt_close(moe_ckpt *c);
+int moe_ckpt_num_tensors(const moe_ckpt *c);
+/* dtype (MOE_DT_*), rank, up to 8 dimensions, payload bytes. */
+moe_status moe_ckpt_tensor_info(const moe_ckpt *c, const char *name, int *dtype, int *ndim,
+                                int64_t *shape, size_t *bytes);
+/* Raw little-endian payload of one tensor into host memory. */
+moe_status moe_ckpt_read(const moe_ckpt *c, const char *name, void *dst, size_t dst_bytes);
+/* Load checkpoint layer `ckpt_layer` into the handle's layer slot `layer`:
+ * the E experts go to one packed device allocation that the handle owns
+ * (freed by moe_destroy, or when the slot is set again), the router to a
+ * device copy (kept BF16 when stored BF16 and keep_bf16 != 0, else f32).
+ * The checks are the reference's Int8Expert::load_into
+ * (src/int8_expert.rs:90-170): I8 merged_weight of exactly 3*I*H elements,
+ * F32 qs of 2*I + H, scales finite and > 0; a router of [E, H] with finite
+ * values.  INT4 experts (U8 [3*I*H/2]) are reported as unsupported. */
+moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_layer, int layer,
+                          int keep_bf16);
+
 /* Seeded N(0, stddev^2) values on the host (Box-Muller in double precision);
  * kind/layer select an independent stream. */
 moe_status moe_synth_normal_host(uint64_t seed, uint32_t kind, uint32_t layer, size_t n,

@@ -49,3 +49,26 @@ def to_device(lw: "O.LayerWeights", device="cuda"):
     else:
         router = torch.from_numpy(np.ascontiguousarray(lw.router)).to(device)
     return experts, scales, router
+
+
+def write_safetensors(path, tensors, metadata=None):
+    """A shard in the safetensors layout: u64 header length, JSON header
+    (padded with spaces to 8 bytes), then the payloads in the given order.
+    tensors: [(name, dtype string, array)]."""
+    import json
+    import struct
+    header, blobs, off = {}, [], 0
+    for name, dt, arr in tensors:
+        b = np.ascontiguousarray(arr).tobytes()
+        header[name] = {"dtype": dt, "shape": list(np.shape(arr)), "data_offsets": [off, off + len(b)]}
+        off += len(b)
+        blobs.append(b)
+    if metadata is not None:
+        header["__metadata__"] = metadata
+    hj = json.dumps(header).encode()
+    hj += b" " * ((8 - len(hj) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hj)))
+        f.write(hj)
+        for b in blobs:
+            f.write(b)
