@@ -75,6 +75,7 @@ SIGNATURES = {
                                    ctypes.POINTER(ctypes.c_size_t)]),
     "moe_ckpt_read": (I32, [P, ctypes.c_char_p, P, SZ]),
     "moe_load_layer": (I32, [P, P, I32, I32, I32]),
+    "moe_set_layer_norm": (I32, [P, I32, P]),
     "moe_host_alloc": (I32, [SZ, PP]),
     "moe_host_free": (I32, [P]),
     "moe_sync_status": (I32, [P, P]),

@@ -346,9 +346,9 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
   stamp(a, 3);
 }
 
-// RMSNorm of token row x into h (src/backend.rs:341-359, unit gain): warp 0,
-// lanes 0..7 run the 8-lane sum of squares; all threads scale.
-__device__ void rms_row(const float *x, float *h, int H, float eps, float *red,
+// RMSNorm of token row x into h (src/backend.rs:341-359; gain w, or 1 when
+// null): warp 0, lanes 0..7 run the 8-lane sum of squares; all threads scale.
+__device__ void rms_row(const float *x, const float *w, float *h, int H, float eps, float *red,
                         uint32_t *status) {
   const int tid = threadIdx.x;
   if (tid < 32) {
@@ -376,7 +376,7 @@ __device__ void rms_row(const float *x, float *h, int H, float eps, float *red,
   bool bad = false;
   for (int j = tid; j < H; j += kFT) {
     const float v = __ldcg(x + j);
-    const float o = __fmul_rn(__fmul_rn(v, inv), 1.0f);
+    const float o = __fmul_rn(__fmul_rn(v, inv), w ? w[j] : 1.0f);
     bad |= !is_finite_f(v) || !is_finite_f(o);
     h[j] = o;
   }
@@ -404,7 +404,8 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
   stamp(a, 0);
   if (a.stacked) {
     for (int t = blockIdx.x; t < T; t += G)
-      rms_row(a.out + (size_t)t * H, a.hbuf + (size_t)t * H, H, a.eps, red, a.status);
+      rms_row(a.out + (size_t)t * H, a.layers[0].norm_w, a.hbuf + (size_t)t * H, H, a.eps, red,
+              a.status);
     ++nbar;
     if (!grid_sync(a.bar, nbar * G, a.status)) return;
     hin = a.hbuf;
@@ -450,7 +451,8 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
         }
         if (bad) set_status(a.status, kStatusNonFinite);
         __syncthreads();
-        if (l + 1 < a.n_layers) rms_row(x, a.hbuf + (size_t)t * H, H, a.eps, red, a.status);
+        if (l + 1 < a.n_layers)
+          rms_row(x, a.layers[l + 1].norm_w, a.hbuf + (size_t)t * H, H, a.eps, red, a.status);
       }
       if (l + 1 < a.n_layers) {
         ++nbar;

@@ -282,7 +282,7 @@ __device__ void router_tasks(const FusedArgs &a, const FusedLayer &L, int layer,
     cp_async_wait_all();
     __syncthreads();
     if (a.stacked) {
-      // RMSNorm of the staged rows (src/backend.rs:341-359, unit gain)
+      // RMSNorm of the staged rows (src/backend.rs:341-359; this layer's gain)
       // whole warps run the folds (the shuffles name all 32 lanes)
       if ((tid >> 5) < (8 * nt + 31) / 32) {
         const int ti = min(tid >> 3, nt - 1), l = tid & 7;
@@ -304,7 +304,8 @@ __device__ void router_tasks(const FusedArgs &a, const FusedLayer &L, int layer,
       const bool write = (task % nte) == 0;
       for (int i = tid; i < nt * H; i += kST) {
         const float v = xs[i];
-        const float o = __fmul_rn(__fmul_rn(v, tb.inv[i / H]), 1.0f);
+        const float o =
+            __fmul_rn(__fmul_rn(v, tb.inv[i / H]), L.norm_w ? L.norm_w[i % H] : 1.0f);
         bad |= !is_finite_f(v) || !is_finite_f(o);
         xs[i] = o;
         if (write) a.hbuf[(size_t)t0 * H + i] = o;

@@ -94,7 +94,7 @@ cudaError_t launch_combine(const float *contrib, const float *resid, float *out,
                            int H, uint32_t *status, cudaStream_t s);
 
 // RMSNorm with unit gain (src/backend.rs:341-359) over [T, H].
-cudaError_t launch_rmsnorm(const float *x, float *out, int T, int H, float eps,
+cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int T, int H, float eps,
                            uint32_t *status, cudaStream_t s);
 
 // Fused decode (decode_fused.cu): a whole layer, or a stack of layers with
@@ -108,6 +108,7 @@ struct FusedLayer {
   const void *router;
   int router_dtype;   // RouterDtype of the stored router
   int prefetch_ok;    // expert bases 16-byte aligned, H and I multiples of 16
+  const float *norm_w;  // stacks: gain [H] of the RMSNorm before this layer, null = 1
 };
 
 struct FusedArgs {

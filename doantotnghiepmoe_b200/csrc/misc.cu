@@ -54,9 +54,10 @@ __global__ void combine_kernel(const float *__restrict__ contrib, const float *_
 
 // One warp per token: sum of squares in the 8-lane order of
 // src/backend.rs:105-120, then scale = sqrt(ss / n + eps), inv = 1 / scale,
-// out = (x * inv) * 1.0  (src/backend.rs:341-359 with unit gain).
-__global__ void rmsnorm_kernel(const float *__restrict__ x, float *__restrict__ out, int T, int H,
-                               float eps, uint32_t *status) {
+// out = (x * inv) * w  (src/backend.rs:341-359; w = 1 without a gain).
+__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                               float *__restrict__ out, int T, int H, float eps,
+                               uint32_t *status) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -81,7 +82,7 @@ __global__ void rmsnorm_kernel(const float *__restrict__ x, float *__restrict__ 
   for (int j = lane; j < H; j += 32) {
     const float v = xr[j];
     bad |= !is_finite_f(v);
-    const float o = __fmul_rn(__fmul_rn(v, inv), 1.0f);
+    const float o = __fmul_rn(__fmul_rn(v, inv), w ? w[j] : 1.0f);
     bad |= !is_finite_f(o);
     orow[j] = o;
   }
@@ -156,10 +157,10 @@ cudaError_t launch_combine(const float *contrib, const float *resid, float *out,
   return cudaGetLastError();
 }
 
-cudaError_t launch_rmsnorm(const float *x, float *out, int T, int H, float eps,
+cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int T, int H, float eps,
                            uint32_t *status, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, out, T, H, eps, status);
+  rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, w, out, T, H, eps, status);
   return cudaGetLastError();
 }
 

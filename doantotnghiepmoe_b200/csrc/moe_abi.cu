@@ -303,7 +303,7 @@ struct LayerSlot {
   bool tc_ok = false;
   CUtensorMap map_gu{}, map_dn{};
   // device copies made by moe_load_layer (owned by the handle)
-  void *own_w = nullptr, *own_s = nullptr, *own_r = nullptr;
+  void *own_w = nullptr, *own_s = nullptr, *own_r = nullptr, *own_n = nullptr;
 };
 }  // namespace
 
@@ -487,6 +487,7 @@ void free_handle(moe_handle *h) {
     cudaFree(l.own_w);
     cudaFree(l.own_s);
     cudaFree(l.own_r);
+    cudaFree(l.own_n);
   }
   void *ptrs[] = {h->logits,  h->gates,     h->r_gate,    h->act,       h->contrib, h->hbuf,
                   h->io_in,   h->io_out,    h->io_resid,  h->ids,       h->status,  h->seg_off,
@@ -1075,6 +1076,28 @@ float half_to_float(uint16_t h) {
 }
 }  // namespace
 
+extern "C" moe_status moe_set_layer_norm(moe_handle *h, int layer, const float *d_norm_w) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (layer < 0 || layer >= (int)h->layers.size() || ((uintptr_t)d_norm_w & 3)) {
+    set_err(h->err, "moe_set_layer_norm: invalid argument");
+    return MOE_ERR_INVALID;
+  }
+  drop_graphs(h);
+  DeviceGuard g(h->device);
+  FusedLayer &F = h->flayers[layer];
+  F.norm_w = d_norm_w;
+  const cudaError_t e =
+      cudaMemcpy(h->d_flayers + layer, &F, sizeof(FusedLayer), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(h, e, "set_layer_norm");
+  LayerSlot &L = h->layers[layer];
+  if (L.own_n && L.own_n != d_norm_w) {  // the slot no longer uses a loaded copy
+    cudaFree(L.own_n);
+    L.own_n = nullptr;
+  }
+  return MOE_OK;
+}
+
 extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_layer,
                                      int layer, int keep_bf16) {
   if (!h || !c || ckpt_layer < 0) return MOE_ERR_INVALID;
@@ -1172,18 +1195,63 @@ extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_
     release();
     return fail(MOE_ERR_CUDA, "moe_load_layer: router upload failed");
   }
+  // the post-attention RMSNorm gain, when the checkpoint has it
+  // (src/olmoe.rs:1057, applied at :2583-2588)
+  const std::string nname =
+      "model.layers." + std::to_string(ckpt_layer) + ".post_attention_layernorm.weight";
+  float *dn = nullptr;
+  if (const CkptTensor *nt = ckpt_find(c, nname)) {
+    if (nt->shape.size() != 1 || (size_t)nt->shape[0] != H ||
+        (nt->dtype != MOE_DT_F32 && nt->dtype != MOE_DT_BF16 && nt->dtype != MOE_DT_F16)) {
+      release();
+      return fail(MOE_ERR_INVALID, nname + ": incorrect shape or dtype");
+    }
+    std::vector<uint8_t> nraw(nt->bytes);
+    std::vector<float> nw(H);
+    if (!ckpt_read(c, *nt, nraw.data())) {
+      release();
+      return fail(MOE_ERR_INVALID, nname + ": short read");
+    }
+    for (size_t i = 0; i < H; ++i) {
+      if (nt->dtype == MOE_DT_F32) {
+        memcpy(&nw[i], &nraw[4 * i], 4);
+      } else {
+        uint16_t b;
+        memcpy(&b, &nraw[2 * i], 2);
+        if (nt->dtype == MOE_DT_F16) {
+          nw[i] = half_to_float(b);
+        } else {
+          const uint32_t bits = (uint32_t)b << 16;
+          memcpy(&nw[i], &bits, 4);
+        }
+      }
+      if (!std::isfinite(nw[i])) {
+        release();
+        return fail(MOE_ERR_NONFINITE, nname + ": non-finite value");
+      }
+    }
+    if (cudaMalloc(&dn, H * 4) != cudaSuccess ||
+        cudaMemcpy(dn, nw.data(), H * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+      cudaFree(dn);
+      release();
+      return fail(MOE_ERR_NOMEM, "moe_load_layer: norm upload failed");
+    }
+  }
   const moe_status st2 =
       moe_set_layer_packed(h, layer, dw, ds, dr, bf16 ? MOE_ROUTER_BF16 : MOE_ROUTER_F32);
   if (st2 != MOE_OK) {
+    cudaFree(dn);
     release();
     return st2;
   }
+  const moe_status st3 = moe_set_layer_norm(h, layer, dn);
   std::lock_guard<std::mutex> lock(h->mu);
   LayerSlot &L = h->layers[layer];
   L.own_w = dw;
   L.own_s = ds;
   L.own_r = dr;
-  return MOE_OK;
+  L.own_n = dn;
+  return st3;
 }
 
 extern "C" moe_status moe_set_layer_packed(moe_handle *h, int layer, const int8_t *d_experts,
@@ -1309,7 +1377,8 @@ moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, fl
   }
   for (int l = first_layer; l < first_layer + n_layers; ++l) {
     cudaEvent_t p0 = h->prof.begin(s);
-    cudaError_t e = launch_rmsnorm(d_x, h->hbuf, T, h->d.hidden, rms_eps, h->status, s);
+    cudaError_t e = launch_rmsnorm(d_x, h->flayers[l].norm_w, h->hbuf, T, h->d.hidden, rms_eps,
+                                   h->status, s);
     h->prof.end("rmsnorm", p0, s);
     if (e != cudaSuccess) return cuda_fail(h, e, "rmsnorm launch");
     h->last_launches += 1;

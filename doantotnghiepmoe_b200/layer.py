@@ -142,6 +142,11 @@ class MoeLayerEngine:
                                                  gates.ctypes.data))
         return out, ids, gates
 
+    def set_layer_norm(self, layer: int, norm_w=None):
+        """Post-attention RMSNorm gain [H] (device tensor) used by stack_forward;
+        None restores the unit gain."""
+        self._check(lib().moe_set_layer_norm(self._h, layer, _ptr(norm_w)))
+
     def load_layer(self, ckpt: "Checkpoint", ckpt_layer: int, layer: int | None = None,
                    keep_bf16: bool = True):
         """moe_load_layer: checkpoint layer -> device copy owned by the engine."""

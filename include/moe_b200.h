@@ -158,10 +158,16 @@ moe_status moe_route_permute(moe_handle *h, int layer, const float *d_h, int T,
 moe_status moe_layer_forward(moe_handle *h, int layer, const float *d_h, const float *d_resid,
                              float *d_out, int T, uint32_t *d_ids, float *d_gates, void *stream);
 
-/* Stacked decode: for l in [first, first+n): x <- x + MoE_l(RMSNorm(x; eps, unit gain)),
- * in place on d_x [T,H] (src/olmoe.rs:2583-2588 then :3147-3157 per layer). */
+/* Stacked decode: for l in [first, first+n): x <- x + MoE_l(RMSNorm_l(x; eps)), in place
+ * on d_x [T,H] (src/olmoe.rs:2583-2588 then :3147-3157 per layer).  RMSNorm_l scales by
+ * layer l's post-attention gain (moe_set_layer_norm), or by 1 when none is set. */
 moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_layers, float *d_x, int T,
                              float rms_eps, void *stream);
+
+/* The post-attention RMSNorm gain of a layer, [H] f32 device memory (borrowed),
+ * used by moe_stack_forward: h = (x * (1 / sqrt(sum x^2 / H + eps))) * w
+ * (src/backend.rs:341-359).  NULL restores the unit gain. */
+moe_status moe_set_layer_norm(moe_handle *h, int layer, const float *d_norm_w);
 
 /* Host-buffer variant of moe_layer_forward (copies in and out inside the
  * call, synchronous, checks the status word like the reference's `finite`).
@@ -281,7 +287,9 @@ moe_status moe_ckpt_read(const moe_ckpt *c, const char *name, void *dst, size_t 
  * The checks are the reference's Int8Expert::load_into
  * (src/int8_expert.rs:90-170): I8 merged_weight of exactly 3*I*H elements,
  * F32 qs of 2*I + H, scales finite and > 0; a router of [E, H] with finite
- * values.  INT4 experts (U8 [3*I*H/2]) are reported as unsupported. */
+ * values.  INT4 experts (U8 [3*I*H/2]) are reported as unsupported.  A
+ * `model.layers.{l}.post_attention_layernorm.weight` [H] becomes the slot's
+ * RMSNorm gain (moe_set_layer_norm), likewise owned by the handle. */
 moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_layer, int layer,
                           int keep_bf16);
 

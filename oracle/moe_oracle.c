@@ -618,7 +618,8 @@ int oracle_stack_forward(const oracle_layer *layers, int nlayers, int T, float *
     int st = ORACLE_OK;
     for (int l = 0; l < nlayers && !st; l++) {
         for (int t = 0; t < T && !st; t++)
-            st = oracle_rms_norm(x + (size_t)t * H, NULL, H, eps, h + (size_t)t * H);
+            st = oracle_rms_norm(x + (size_t)t * H, layers[l].norm_w, H, eps,
+                                 h + (size_t)t * H);
         if (st)
             break;
         st = oracle_layer_forward(&layers[l], T, h, x, nx,

@@ -92,6 +92,7 @@ typedef struct oracle_layer {
     const void *router;
     const int8_t *experts;
     const float *scales;
+    const float *norm_w; /* post-attention RMSNorm gain [H] for stacks, NULL = 1 */
 } oracle_layer;
 
 int oracle_layer_forward(const oracle_layer *L, int T, const float *h,

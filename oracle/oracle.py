@@ -77,7 +77,8 @@ class _Layer(ctypes.Structure):
     _fields_ = [("H", ctypes.c_int), ("I", ctypes.c_int), ("E", ctypes.c_int),
                 ("K", ctypes.c_int), ("norm_topk_prob", ctypes.c_int),
                 ("router_bf16", ctypes.c_int), ("router", ctypes.c_void_p),
-                ("experts", ctypes.c_void_p), ("scales", ctypes.c_void_p)]
+                ("experts", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+                ("norm_w", ctypes.c_void_p)]
 
 
 @dataclass
@@ -97,14 +98,19 @@ class LayerWeights:
     experts: np.ndarray
     scales: np.ndarray
     router_bf16: bool = False
+    norm_w: np.ndarray | None = None  # post-attention RMSNorm gain [H] (stacks); None = 1
 
     def c_struct(self) -> _Layer:
         for name in ("router", "experts", "scales"):
             a = getattr(self, name)
             assert a.flags["C_CONTIGUOUS"], name
+        nw = None
+        if self.norm_w is not None:
+            assert self.norm_w.dtype == np.float32 and self.norm_w.flags["C_CONTIGUOUS"]
+            nw = self.norm_w.ctypes.data
         return _Layer(self.H, self.I, self.E, self.K, int(self.norm_topk_prob),
                       int(self.router_bf16), self.router.ctypes.data,
-                      self.experts.ctypes.data, self.scales.ctypes.data)
+                      self.experts.ctypes.data, self.scales.ctypes.data, nw)
 
 
 class OracleError(RuntimeError):
