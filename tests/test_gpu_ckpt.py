@@ -127,22 +127,18 @@ def test_loaded_stack_with_post_attention_norm(tmp_path, path):
     tensors = []
     rng = np.random.default_rng(77)
     for l in range(3):
-        lw = O.synth_layer(75, l, Hs, Is, Es, Ks, l == 1)
+        lw = O.synth_layer(75, l, Hs, Is, Es, Ks, False)
         lw.norm_w = (1.0 + 0.25 * rng.standard_normal(Hs)).astype(np.float32)
         layers.append(lw)
         tensors += layer_tensors(l, lw, "F32")
         tensors.append((f"model.layers.{l}.post_attention_layernorm.weight", "F32", lw.norm_w))
     write_safetensors(tmp_path / "m.safetensors", tensors)
     ck = M.Checkpoint(str(tmp_path))
-    # norm_topk_prob is a model setting: the oracle layers say it per layer,
-    # the engine per handle -- keep it per layer equal by using one engine per
-    # setting where they differ
     x0 = O.synth_hidden(76, T, Hs)
-    for norm in (False, True):
-        sel = [lw for lw in layers]
-        for lw in sel:
+    for norm in (False, True):  # norm_topk_prob is per engine (a model setting)
+        for lw in layers:
             lw.norm_topk_prob = norm
-        ref_x, ref_ids, _ = O.stack_forward(sel, x0)
+        ref_x, _, _ = O.stack_forward(layers, x0)
         eng = M.MoeLayerEngine(M.MoeConfig(Hs, Is, Es, Ks, norm, T, 3))
         eng.set_path(path)
         for l in range(3):
