@@ -318,6 +318,93 @@ float oracle_dot_i8_scalar(const int8_t *q, const float *x, size_t n)
     return s;
 }
 
+/* --------------------------------------------------------------------------
+ * INT4 x FP32 dot products (src/int8_expert.rs:473-649).  Two signed nibbles
+ * per byte: element 2i is the low nibble of byte i, element 2i+1 the high
+ * one, each sign-extended from 4 bits.
+ *
+ * AVX2 path, :519-637 `dot_i4_f32_avx2` (and the paired :785-952, whose
+ * per-row arithmetic is the same): per 32 elements (16 bytes) the nibbles
+ * are split, interleaved back into element order, sign-extended, and FMA'd
+ * into four 8-lane banks; then the INT8 path's fold, 8-chunks, horizontal
+ * fold and scalar tail.
+ * ------------------------------------------------------------------------ */
+__attribute__((target("avx2,fma"))) static inline __m256 widen8_i4(const uint8_t *q)
+{
+    /* 4 bytes -> 8 sign-extended nibbles in element order (:586-604) */
+    long long v = 0;
+    for (int b = 0; b < 4; b++) {
+        int lo = (int8_t)(q[b] << 4) >> 4, hi = (int8_t)q[b] >> 4;
+        v |= (long long)(uint8_t)lo << (16 * b);
+        v |= (long long)(uint8_t)hi << (16 * b + 8);
+    }
+    return _mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(_mm_cvtsi64_si128(v)));
+}
+
+__attribute__((target("avx2,fma"))) float oracle_dot_i4_avx2(const uint8_t *q,
+                                                             const float *x,
+                                                             size_t n)
+{
+    __m256 b0 = _mm256_setzero_ps(), b1 = _mm256_setzero_ps();
+    __m256 b2 = _mm256_setzero_ps(), b3 = _mm256_setzero_ps();
+    const __m128i m0f = _mm_set1_epi8(0x0F), c8 = _mm_set1_epi8(8);
+    size_t c32 = n / 32;
+    for (size_t c = 0; c < c32; c++) {
+        const __m128i v = _mm_loadu_si128((const __m128i *)(q + 16 * c));
+        const __m128i lo = _mm_and_si128(v, m0f);
+        const __m128i hi = _mm_and_si128(_mm_srli_epi16(v, 4), m0f);
+        const __m128i s_lo = _mm_sub_epi8(_mm_xor_si128(_mm_unpacklo_epi8(lo, hi), c8), c8);
+        const __m128i s_hi = _mm_sub_epi8(_mm_xor_si128(_mm_unpackhi_epi8(lo, hi), c8), c8);
+        const float *xx = x + 32 * c;
+        b0 = _mm256_fmadd_ps(_mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(s_lo)),
+                             _mm256_loadu_ps(xx), b0);
+        b1 = _mm256_fmadd_ps(_mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(_mm_srli_si128(s_lo, 8))),
+                             _mm256_loadu_ps(xx + 8), b1);
+        b2 = _mm256_fmadd_ps(_mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(s_hi)),
+                             _mm256_loadu_ps(xx + 16), b2);
+        b3 = _mm256_fmadd_ps(_mm256_cvtepi32_ps(_mm256_cvtepi8_epi32(_mm_srli_si128(s_hi, 8))),
+                             _mm256_loadu_ps(xx + 24), b3);
+    }
+    __m256 t = _mm256_add_ps(_mm256_add_ps(b0, b1), _mm256_add_ps(b2, b3));
+    size_t i = 32 * c32;
+    for (; i + 8 <= n; i += 8)
+        t = _mm256_fmadd_ps(widen8_i4(q + i / 2), _mm256_loadu_ps(x + i), t);
+    float s = hfold(t);
+    for (; i < n; i++) {
+        const uint8_t b = q[i / 2];
+        const int v = (i & 1) ? (int8_t)b >> 4 : (int8_t)(b << 4) >> 4;
+        float p = (float)v * x[i];
+        s = s + p;
+    }
+    return s;
+}
+
+/* Scalar fallback, :476-516: four scalar accumulators, each taking a pair
+ * of products per 8-chunk, s0 + s1 + s2 + s3 left to right, then the tail. */
+float oracle_dot_i4_scalar(const uint8_t *q, const float *x, size_t n)
+{
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    size_t c8 = n / 8;
+    for (size_t c = 0; c < c8; c++)
+        for (int k = 0; k < 4; k++) {
+            const uint8_t b = q[4 * c + k];
+            const float a = (float)((int8_t)(b << 4) >> 4) * x[8 * c + 2 * k];
+            const float d = (float)((int8_t)b >> 4) * x[8 * c + 2 * k + 1];
+            const float pair = a + d;
+            s[k] = s[k] + pair;
+        }
+    float sum = s[0] + s[1];
+    sum = sum + s[2];
+    sum = sum + s[3];
+    for (size_t i = 8 * c8; i < n; i++) {
+        const uint8_t b = q[i / 2];
+        const int v = (i & 1) ? (int8_t)b >> 4 : (int8_t)(b << 4) >> 4;
+        float p = (float)v * x[i];
+        sum = sum + p;
+    }
+    return sum;
+}
+
 static int have_avx2(void)
 {
     static int cached = -1;
@@ -328,8 +415,13 @@ static int have_avx2(void)
     return cached;
 }
 
-static inline float dot_i8(const int8_t *q, const float *x, size_t n, int mode)
+/* mode 0 = the AVX2 path when the CPU has it, else the scalar fallback;
+ * int4: rows are packed nibbles (n/2 bytes). */
+static inline float dot_q(const int8_t *q, const float *x, size_t n, int mode, int int4)
 {
+    if (int4)
+        return (mode == 0 && have_avx2()) ? oracle_dot_i4_avx2((const uint8_t *)q, x, n)
+                                          : oracle_dot_i4_scalar((const uint8_t *)q, x, n);
     return (mode == 0 && have_avx2()) ? oracle_dot_i8_avx2(q, x, n)
                                       : oracle_dot_i8_scalar(q, x, n);
 }
@@ -337,30 +429,38 @@ static inline float dot_i8(const int8_t *q, const float *x, size_t n, int mode)
 /* src/int8_expert.rs:1058-1101 lane body: g = dot*sg, u = dot*su,
  * act = (g / (1 + exp(-g))) * u. */
 static inline float swiglu_row(const int8_t *wg, const int8_t *wu, float sg, float su,
-                               const float *x, int H, int mode)
+                               const float *x, int H, int mode, int int4)
 {
-    float g = dot_i8(wg, x, (size_t)H, mode) * sg;
-    float u = dot_i8(wu, x, (size_t)H, mode) * su;
+    float g = dot_q(wg, x, (size_t)H, mode, int4) * sg;
+    float u = dot_q(wu, x, (size_t)H, mode, int4) * su;
     float den = 1.0f + expf(-g);
     float silu = g / den;
     return silu * u;
 }
 
-/* Int8Expert::forward_single_threaded, src/int8_expert.rs:301-338. */
-int oracle_expert_forward(const int8_t *w, const float *s, int H, int I,
-                          const float *x, float *act, float *y, int mode)
+/* Int8Expert::forward_single_threaded, src/int8_expert.rs:301-338; INT4
+ * rows are H/2 (gate, up) and I/2 (down) bytes (:312-316). */
+int oracle_expert_forward_q(const int8_t *w, const float *s, int H, int I, const float *x,
+                            float *act, float *y, int mode, int int4)
 {
-    if (H <= 0 || I <= 0)
+    if (H <= 0 || I <= 0 || (int4 && ((H | I) & 1)))
         return ORACLE_ERR_SHAPE;
     if (!all_finite(x, (size_t)H))
         return ORACLE_ERR_NONFINITE;
-    const size_t n = (size_t)H * I;
+    const size_t hs = int4 ? (size_t)H / 2 : (size_t)H, is = int4 ? (size_t)I / 2 : (size_t)I;
+    const size_t n = hs * I;
     for (int r = 0; r < I; r++)
-        act[r] = swiglu_row(w + (size_t)r * H, w + n + (size_t)r * H, s[r], s[I + r], x,
-                            H, mode);
+        act[r] = swiglu_row(w + (size_t)r * hs, w + n + (size_t)r * hs, s[r], s[I + r], x,
+                            H, mode, int4);
     for (int r = 0; r < H; r++)
-        y[r] = dot_i8(w + 2 * n + (size_t)r * I, act, (size_t)I, mode) * s[2 * I + r];
+        y[r] = dot_q(w + 2 * n + (size_t)r * is, act, (size_t)I, mode, int4) * s[2 * I + r];
     return all_finite(y, (size_t)H) ? ORACLE_OK : ORACLE_ERR_NONFINITE;
+}
+
+int oracle_expert_forward(const int8_t *w, const float *s, int H, int I,
+                          const float *x, float *act, float *y, int mode)
+{
+    return oracle_expert_forward_q(w, s, H, I, x, act, y, mode, 0);
 }
 
 /* Int8Expert::forward_reuse (src/int8_expert.rs:260-297): the same rows,
@@ -368,18 +468,19 @@ int oracle_expert_forward(const int8_t *w, const float *s, int H, int I,
  * matrix has >= 262,144 weights). */
 static int expert_forward_rows_parallel(const int8_t *w, const float *s, int H, int I,
                                         const float *x, float *act, float *y, int mode,
-                                        int nthreads)
+                                        int nthreads, int int4)
 {
     if (!all_finite(x, (size_t)H))
         return ORACLE_ERR_NONFINITE;
-    const size_t n = (size_t)H * I;
+    const size_t hs = int4 ? (size_t)H / 2 : (size_t)H, is = int4 ? (size_t)I / 2 : (size_t)I;
+    const size_t n = hs * I;
 #pragma omp parallel for num_threads(nthreads) schedule(static)
     for (int r = 0; r < I; r++)
-        act[r] = swiglu_row(w + (size_t)r * H, w + n + (size_t)r * H, s[r], s[I + r], x,
-                            H, mode);
+        act[r] = swiglu_row(w + (size_t)r * hs, w + n + (size_t)r * hs, s[r], s[I + r], x,
+                            H, mode, int4);
 #pragma omp parallel for num_threads(nthreads) schedule(static)
     for (int r = 0; r < H; r++)
-        y[r] = dot_i8(w + 2 * n + (size_t)r * I, act, (size_t)I, mode) * s[2 * I + r];
+        y[r] = dot_q(w + 2 * n + (size_t)r * is, act, (size_t)I, mode, int4) * s[2 * I + r];
     return all_finite(y, (size_t)H) ? ORACLE_OK : ORACLE_ERR_NONFINITE;
 }
 
@@ -481,7 +582,9 @@ int oracle_layer_forward(const oracle_layer *L, int T, const float *h,
         return ORACLE_ERR_SHAPE;
     if (nthreads < 1)
         nthreads = 1;
-    const size_t wpe = (size_t)3 * H * I, spe = (size_t)2 * I + H;
+    if (L->int4 && ((H | I) & 1))
+        return ORACLE_ERR_SHAPE;
+    const size_t wpe = (size_t)3 * H * I / (L->int4 ? 2 : 1), spe = (size_t)2 * I + H;
     uint32_t *ids = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)T * K + 4);
     float *gates = (float *)malloc(sizeof(float) * (size_t)T * K + 4);
     int st = ORACLE_OK;
@@ -529,9 +632,9 @@ int oracle_layer_forward(const oracle_layer *L, int T, const float *h,
 #pragma omp parallel for num_threads(nthreads) schedule(static, 1) reduction(| : errs)
             for (int s = 0; s < K; s++) {
                 uint32_t e = ids[(size_t)t * K + s];
-                errs |= oracle_expert_forward(L->experts + wpe * e, L->scales + spe * e, H, I,
-                                              ht, act + (size_t)s * I, y + (size_t)s * H,
-                                              mode);
+                errs |= oracle_expert_forward_q(L->experts + wpe * e, L->scales + spe * e, H, I,
+                                                ht, act + (size_t)s * I, y + (size_t)s * H,
+                                                mode, L->int4);
             }
             if (errs) {
                 st = ORACLE_ERR_NONFINITE;
@@ -573,7 +676,7 @@ int oracle_layer_forward(const oracle_layer *L, int T, const float *h,
                 int t = tok[u], s = slot[u];
                 st = expert_forward_rows_parallel(L->experts + wpe * e, L->scales + spe * e, H,
                                                   I, h + (size_t)t * H, act, y, mode,
-                                                  nthreads);
+                                                  nthreads, L->int4);
                 float w = gates[(size_t)t * K + s];
                 float *c = contrib + ((size_t)t * K + s) * H;
                 for (int j = 0; j < H; j++)

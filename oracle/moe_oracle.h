@@ -65,6 +65,10 @@ void oracle_select_topk_then_softmax(const float *scores, int E, int K,
  * mode 1 = scalar fallback (dot_i8_f32_scalar). */
 float oracle_dot_i8_avx2(const int8_t *q, const float *x, size_t n);
 float oracle_dot_i8_scalar(const int8_t *q, const float *x, size_t n);
+float oracle_dot_i4_avx2(const uint8_t *q, const float *x, size_t n);
+float oracle_dot_i4_scalar(const uint8_t *q, const float *x, size_t n);
+int oracle_expert_forward_q(const int8_t *w, const float *s, int H, int I, const float *x,
+                            float *act, float *y, int mode, int int4);
 int oracle_expert_forward(const int8_t *w, const float *s, int H, int I,
                           const float *x, float *act, float *y, int mode);
 
@@ -93,6 +97,7 @@ typedef struct oracle_layer {
     const int8_t *experts;
     const float *scales;
     const float *norm_w; /* post-attention RMSNorm gain [H] for stacks, NULL = 1 */
+    int int4;            /* experts are packed INT4 nibbles (3*H*I/2 bytes each) */
 } oracle_layer;
 
 int oracle_layer_forward(const oracle_layer *L, int T, const float *h,

@@ -49,7 +49,10 @@ def lib():
             "oracle_select_topk_then_softmax": (None, [P, i32, i32, P, P]),
             "oracle_dot_i8_avx2": (f32, [P, P, sz]),
             "oracle_dot_i8_scalar": (f32, [P, P, sz]),
+            "oracle_dot_i4_avx2": (f32, [P, P, sz]),
+            "oracle_dot_i4_scalar": (f32, [P, P, sz]),
             "oracle_expert_forward": (i32, [P, P, i32, i32, P, P, P, i32]),
+            "oracle_expert_forward_q": (i32, [P, P, i32, i32, P, P, P, i32, i32]),
             "oracle_expf_table": (f32, [f32]),
             "oracle_expf_table_mismatches": (u64, [u32, u32, u32]),
             "oracle_expf_libm_range": (None, [u32, sz, P]),
@@ -78,7 +81,7 @@ class _Layer(ctypes.Structure):
                 ("K", ctypes.c_int), ("norm_topk_prob", ctypes.c_int),
                 ("router_bf16", ctypes.c_int), ("router", ctypes.c_void_p),
                 ("experts", ctypes.c_void_p), ("scales", ctypes.c_void_p),
-                ("norm_w", ctypes.c_void_p)]
+                ("norm_w", ctypes.c_void_p), ("int4", ctypes.c_int)]
 
 
 @dataclass
@@ -99,6 +102,7 @@ class LayerWeights:
     scales: np.ndarray
     router_bf16: bool = False
     norm_w: np.ndarray | None = None  # post-attention RMSNorm gain [H] (stacks); None = 1
+    int4: bool = False  # experts are uint8 [E, 3*I*H/2] nibble pairs (src/int8_expert.rs:473)
 
     def c_struct(self) -> _Layer:
         for name in ("router", "experts", "scales"):
@@ -110,7 +114,7 @@ class LayerWeights:
             nw = self.norm_w.ctypes.data
         return _Layer(self.H, self.I, self.E, self.K, int(self.norm_topk_prob),
                       int(self.router_bf16), self.router.ctypes.data,
-                      self.experts.ctypes.data, self.scales.ctypes.data, nw)
+                      self.experts.ctypes.data, self.scales.ctypes.data, nw, int(self.int4))
 
 
 class OracleError(RuntimeError):
@@ -168,14 +172,25 @@ def select_topk_then_softmax(scores, K: int):
 
 
 def expert_forward(w, s, H: int, I: int, x, scalar: bool = False):
-    """Int8Expert::forward_single_threaded.  Returns (act[I], y[H])."""
-    w = np.ascontiguousarray(w, np.int8); s = np.ascontiguousarray(s, np.float32)
+    """Int8Expert::forward_single_threaded.  Returns (act[I], y[H]).  A uint8
+    `w` of 3*H*I/2 bytes is an INT4 expert."""
+    int4 = np.asarray(w).dtype == np.uint8 and np.asarray(w).size * 2 == 3 * H * I
+    w = np.ascontiguousarray(w, np.uint8 if int4 else np.int8)
+    s = np.ascontiguousarray(s, np.float32)
     x = np.ascontiguousarray(x, np.float32)
-    assert w.size == 3 * H * I and s.size == 2 * I + H and x.size == H
+    assert w.size == 3 * H * I // (2 if int4 else 1) and s.size == 2 * I + H and x.size == H
     act = np.empty(I, np.float32); y = np.empty(H, np.float32)
-    _check(lib().oracle_expert_forward(_p(w), _p(s), H, I, _p(x), _p(act), _p(y),
-                                       int(scalar)), "expert_forward")
+    _check(lib().oracle_expert_forward_q(_p(w), _p(s), H, I, _p(x), _p(act), _p(y),
+                                         int(scalar), int(int4)), "expert_forward")
     return act, y
+
+
+def dot_i4(q, x, scalar: bool = False) -> np.float32:
+    """INT4 row dot: q uint8 packed nibbles (element 2i low, 2i+1 high)."""
+    q = np.ascontiguousarray(q, np.uint8); x = np.ascontiguousarray(x, np.float32)
+    assert q.size == (x.size + 1) // 2
+    fn = lib().oracle_dot_i4_scalar if scalar else lib().oracle_dot_i4_avx2
+    return np.float32(fn(_p(q), _p(x), x.size))
 
 
 @dataclass
