@@ -28,6 +28,7 @@ MOE_ROUTE_SOFTMAX_TOPK, MOE_ROUTE_TOPK_SOFTMAX = 0, 1
 MOE_PATH_AUTO, MOE_PATH_GEMV, MOE_PATH_TENSOR, MOE_PATH_GEMV_PHASED = 0, 1, 2, 3
 MOE_PATH_GEMV_FUSED = 4
 MOE_PATH_GEMV_STREAM = 5
+MOE_QUANT_INT8, MOE_QUANT_INT4 = 0, 1
 
 # Every symbol the header declares, with (restype, argtypes).
 P, SZ, I32, U32, U64, F32 = (ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32,
@@ -61,7 +62,9 @@ SIGNATURES = {
     "moe_set_route_mode": (I32, [P, I32]),
     "moe_set_path": (I32, [P, I32]),
     "moe_set_layer": (I32, [P, I32, PP, PP, P, I32]),
+    "moe_set_layer_q": (I32, [P, I32, PP, PP, P, I32, I32]),
     "moe_set_layer_packed": (I32, [P, I32, P, P, P, I32]),
+    "moe_set_layer_packed_q": (I32, [P, I32, P, P, P, I32, I32]),
     "moe_route": (I32, [P, I32, P, I32, P, P, P, P]),
     "moe_route_permute": (I32, [P, I32, P, I32, P, P, P, P, P, P]),
     "moe_layer_forward": (I32, [P, I32, P, P, P, I32, P, P, P]),

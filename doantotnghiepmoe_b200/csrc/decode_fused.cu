@@ -266,7 +266,7 @@ __device__ void build_tables(const FusedArgs &a, Tables &tb) {
 constexpr int kGURowsItem = kGURowsPerWarp * (kFT / 32);  // 32
 constexpr int kDNRowsItem = kDNRowsPerWarp * (kFT / 32);  // 64
 
-template <bool kVec, bool kMulti>
+template <bool kVec, bool kMulti, int kQ>
 __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const float *hin,
                               float *stage, Tables &tb, uint32_t &nbar, bool &alive) {
   const int H = a.H, I = a.I, G = gridDim.x;
@@ -277,20 +277,21 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
   // up front when the layer's active experts fit comfortably in L2 (batch-1
   // decode), otherwise two items ahead of use (larger batches would evict
   // their own prefetches).
-  const bool all_up_front = (size_t)nseg * 3 * I * H <= ((size_t)64 << 20);
+  const size_t hb = (size_t)H * kQ / 8, ib = (size_t)I * kQ / 8;  // bytes per row
+  const bool all_up_front = (size_t)nseg * 3 * I * hb <= ((size_t)64 << 20);
   auto pf_gu = [&](int item) {
     if (threadIdx.x != 0 || !L.prefetch_ok || item >= nseg * nb_gu) return;
     const int e = tb.active[item / nb_gu], row0 = (item % nb_gu) * kGURowsItem;
     const int rows = min(kGURowsItem, I - row0);
     const int8_t *W = L.w_ptr[e];
-    prefetch_l2(W + (size_t)row0 * H, (uint32_t)rows * H);
-    prefetch_l2(W + (size_t)(I + row0) * H, (uint32_t)rows * H);
+    prefetch_l2(W + (size_t)row0 * hb, (uint32_t)(rows * hb));
+    prefetch_l2(W + (size_t)(I + row0) * hb, (uint32_t)(rows * hb));
   };
   auto pf_dn = [&](int item) {
     if (threadIdx.x != 0 || !L.prefetch_ok || item >= nseg * nb_dn) return;
     const int e = tb.active[item / nb_dn], row0 = (item % nb_dn) * kDNRowsItem;
     const int rows = min(kDNRowsItem, H - row0);
-    prefetch_l2(L.w_ptr[e] + (size_t)2 * I * H + (size_t)row0 * I, (uint32_t)rows * I);
+    prefetch_l2(L.w_ptr[e] + 2 * (size_t)I * hb + (size_t)row0 * ib, (uint32_t)(rows * ib));
   };
   if (all_up_front) {
     for (int item = blockIdx.x; item < nseg * nb_gu; item += G) pf_gu(item);
@@ -312,11 +313,11 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
     const int r0 = tb.seg_off[e], r1 = tb.seg_off[e + 1];
     const int row0 = (item % nb_gu) * kGURowsItem;
     if (!kMulti || r1 - r0 == 1)
-      gate_up_item<kVec, 1, 4>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, tb.r_token, hin,
-                               stage, a.act);
+      gate_up_item<kVec, 1, 4, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, tb.r_token, hin,
+                                   stage, a.act);
     else
-      gate_up_item<kVec, 4, 4>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, tb.r_token, hin,
-                               stage, a.act);
+      gate_up_item<kVec, 4, 4, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, tb.r_token, hin,
+                                   stage, a.act);
   }
   ++nbar;
   if (!grid_sync(a.bar, nbar * G, a.status)) {
@@ -334,11 +335,11 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
       a.contrib[((size_t)tb.r_token[r] * a.K + tb.r_slot[r]) * H + row] = __fmul_rn(tb.r_gate[r], y);
     };
     if (!kMulti || r1 - r0 == 1)
-      good &= down_item<kVec, 1, 4>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, a.act, stage,
-                                    emit);
+      good &= down_item<kVec, 1, 4, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, a.act,
+                                        stage, emit);
     else
-      good &= down_item<kVec, 4, 4>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, a.act, stage,
-                                    emit);
+      good &= down_item<kVec, 4, 4, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, a.act,
+                                        stage, emit);
   }
   if (!good) set_status(a.status, kStatusNonFinite);
   ++nbar;
@@ -390,7 +391,8 @@ constexpr size_t align128(size_t n) { return (n + 127) & ~size_t(127); }
 constexpr size_t kSelOff = align128(sizeof(Tables));
 constexpr size_t kStageOff = align128(kSelOff + 8 * sizeof(SelectScratch));
 
-template <bool kVec, bool kMulti>
+// kQ: the weight format of every layer in the launch (8 or 4 bits).
+template <bool kVec, bool kMulti, int kQ>
 __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(FusedArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   Tables &tb = *reinterpret_cast<Tables *>(smem);
@@ -417,7 +419,7 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
     if (!grid_sync(a.bar, nbar * G, a.status)) return;
     if (l == 0) stamp(a, 1);
     build_tables(a, tb);
-    expert_phases<kVec, kMulti>(a, L, hin, stage, tb, nbar, alive);
+    expert_phases<kVec, kMulti, kQ>(a, L, hin, stage, tb, nbar, alive);
     if (!alive) return;
     if (!a.stacked) {
       // C: out = resid + contrib[., 0] + ... + contrib[., K-1] (slot order)
@@ -486,17 +488,25 @@ cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint3
   // A single token per call means every expert segment holds one route:
   // the lighter single-route variant then fits two CTAs per SM.
   const bool multi = a.T > 1;
-  const void *fn = vec ? (multi ? (const void *)fused_decode_kernel<true, true>
-                                : (const void *)fused_decode_kernel<true, false>)
-                       : (multi ? (const void *)fused_decode_kernel<false, true>
-                                : (const void *)fused_decode_kernel<false, false>);
+  const void *fn;
+  if (a.int4)
+    fn = vec ? (multi ? (const void *)fused_decode_kernel<true, true, 4>
+                      : (const void *)fused_decode_kernel<true, false, 4>)
+             : (multi ? (const void *)fused_decode_kernel<false, true, 4>
+                      : (const void *)fused_decode_kernel<false, false, 4>);
+  else
+    fn = vec ? (multi ? (const void *)fused_decode_kernel<true, true, 8>
+                      : (const void *)fused_decode_kernel<true, false, 8>)
+             : (multi ? (const void *)fused_decode_kernel<false, true, 8>
+                      : (const void *)fused_decode_kernel<false, false, 8>);
   // The attribute and occupancy query run once per (device, variant, size).
-  static thread_local int cached_dev = -1, cached_vec = -1, cached_grid = 0, cached_multi = -1;
+  static thread_local int cached_dev = -1, cached_vec = -1, cached_grid = 0, cached_multi = -1,
+                          cached_q = -1;
   static thread_local size_t cached_smem = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != cached_dev || vec != cached_vec || smem != cached_smem ||
-      (int)multi != cached_multi) {
+      (int)multi != cached_multi || a.int4 != cached_q) {
     cudaError_t e =
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -508,6 +518,7 @@ cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint3
     cached_vec = vec;
     cached_smem = smem;
     cached_multi = multi;
+    cached_q = a.int4;
     cached_grid = std::min(per_sm, 2) * sm_count;
   }
   cudaError_t e = cudaMemsetAsync(bar, 0, sizeof(uint32_t), s);

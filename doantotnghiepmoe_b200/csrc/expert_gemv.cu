@@ -1,4 +1,4 @@
-// Grouped INT8 x FP32 GEMV over expert segments, one launch per phase
+// Grouped INT8 (or INT4) x FP32 GEMV over expert segments, one launch per phase
 // (gate/up, then down): the decode-sized expert path used by the layer API
 // and by the GpuExpertKernels drop-in.  The arithmetic lives in
 // gemv_core.cuh; this file only maps work items to CTAs.
@@ -21,7 +21,7 @@ __device__ __forceinline__ int seg_count(const GemvArgs &a) {
   return a.n_active_dev ? *a.n_active_dev : a.n_active_max;
 }
 
-template <bool kVec>
+template <bool kVec, int kQ>
 __global__ void __launch_bounds__(kThreads) gate_up_kernel(GemvArgs a) {
   extern __shared__ float xs[];  // [kTG][H]
   const int rows_per_item = kGURowsPerWarp * (kThreads / 32);
@@ -30,12 +30,12 @@ __global__ void __launch_bounds__(kThreads) gate_up_kernel(GemvArgs a) {
   for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
     const int j = item / nblk, b = item % nblk;
     const int e = a.active ? a.active[j] : j;
-    gate_up_item<kVec>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item, a.seg_off[e],
+    gate_up_item<kVec, kTG, kPF, kQ>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item, a.seg_off[e],
                        a.seg_off[e + 1], a.r_token, a.x, xs, a.act);
   }
 }
 
-template <bool kVec>
+template <bool kVec, int kQ>
 __global__ void __launch_bounds__(kThreads) down_kernel(GemvArgs a) {
   extern __shared__ float xs[];  // [kTG][I]
   const int rows_per_item = kDNRowsPerWarp * (kThreads / 32);
@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(kThreads) down_kernel(GemvArgs a) {
     const int j = item / nblk, b = item % nblk;
     const int e = a.active ? a.active[j] : j;
     if (a.contrib) {
-      good &= down_item<kVec>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item,
+      good &= down_item<kVec, kTG, kPF, kQ>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item,
                               a.seg_off[e], a.seg_off[e + 1], a.act, xs,
                               [&](int r, int row, float y) {
                                 const int tok = a.r_token[r], slot = a.r_slot[r];
@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(kThreads) down_kernel(GemvArgs a) {
                                     __fmul_rn(a.r_gate[r], y);
                               });
     } else {
-      good &= down_item<kVec>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item,
+      good &= down_item<kVec, kTG, kPF, kQ>(a.w_ptr[e], a.s_ptr[e], a.H, a.I, b * rows_per_item,
                               a.seg_off[e], a.seg_off[e + 1], a.act, xs,
                               [&](int r, int row, float y) { a.y[(size_t)r * a.H + row] = y; });
     }
@@ -76,12 +76,17 @@ cudaError_t launch_gate_up(const GemvArgs &a, cudaStream_t s) {
   const int nblk = (a.I + kGURowsPerWarp * 4 - 1) / (kGURowsPerWarp * 4);
   const int grid = grid_for(a.n_active_max * nblk, a.sm_count);
   const size_t smem = sizeof(float) * kTG * a.H;
-  if (a.H % 8 == 0 && a.vec) {
-    ensure_smem(gate_up_kernel<true>, smem);
-    gate_up_kernel<true><<<grid, kThreads, smem, s>>>(a);
+  auto go = [&](auto kernel) {
+    ensure_smem(kernel, smem);
+    kernel<<<grid, kThreads, smem, s>>>(a);
+  };
+  const bool vec = a.H % 8 == 0 && a.vec;
+  if (a.int4) {
+    if (vec) go(gate_up_kernel<true, 4>);
+    else go(gate_up_kernel<false, 4>);
   } else {
-    ensure_smem(gate_up_kernel<false>, smem);
-    gate_up_kernel<false><<<grid, kThreads, smem, s>>>(a);
+    if (vec) go(gate_up_kernel<true, 8>);
+    else go(gate_up_kernel<false, 8>);
   }
   return cudaGetLastError();
 }
@@ -90,12 +95,17 @@ cudaError_t launch_down(const GemvArgs &a, cudaStream_t s) {
   const int nblk = (a.H + kDNRowsPerWarp * 4 - 1) / (kDNRowsPerWarp * 4);
   const int grid = grid_for(a.n_active_max * nblk, a.sm_count);
   const size_t smem = sizeof(float) * kTG * a.I;
-  if (a.I % 8 == 0 && a.vec) {
-    ensure_smem(down_kernel<true>, smem);
-    down_kernel<true><<<grid, kThreads, smem, s>>>(a);
+  auto go = [&](auto kernel) {
+    ensure_smem(kernel, smem);
+    kernel<<<grid, kThreads, smem, s>>>(a);
+  };
+  const bool vec = a.I % 8 == 0 && a.vec;
+  if (a.int4) {
+    if (vec) go(down_kernel<true, 4>);
+    else go(down_kernel<false, 4>);
   } else {
-    ensure_smem(down_kernel<false>, smem);
-    down_kernel<false><<<grid, kThreads, smem, s>>>(a);
+    if (vec) go(down_kernel<true, 8>);
+    else go(down_kernel<false, 8>);
   }
   return cudaGetLastError();
 }

@@ -84,6 +84,7 @@ struct GemvArgs {
   uint32_t *status;
   int sm_count;
   int vec;                     // 1: every expert base pointer is 8-byte aligned
+  int int4;                    // 1: INT4 experts (3*I*H/2 bytes, two nibbles per byte)
 };
 cudaError_t launch_gate_up(const GemvArgs &a, cudaStream_t s);
 cudaError_t launch_down(const GemvArgs &a, cudaStream_t s);
@@ -109,6 +110,7 @@ struct FusedLayer {
   int router_dtype;   // RouterDtype of the stored router
   int prefetch_ok;    // expert bases 16-byte aligned, H and I multiples of 16
   const float *norm_w;  // stacks: gain [H] of the RMSNorm before this layer, null = 1
+  int int4;             // INT4 experts: rows of n/2 bytes, two signed nibbles per byte
 };
 
 struct FusedArgs {
@@ -132,6 +134,7 @@ struct FusedArgs {
   uint32_t *bar;             // grid barrier counter (zeroed by the launcher)
   uint32_t *status;
   int router_async;          // routers of every layer are 16-byte aligned f32 rows
+  int int4;                  // every layer of the launch has INT4 experts
   unsigned long long *phase_ts;  // optional [5] phase timestamps (profiling)
   // streaming decode (decode_stream.cu) only
   uint32_t *ctr;             // counter set of this launch [kStreamCtrWords]

@@ -299,6 +299,7 @@ struct LayerSlot {
   const void *router = nullptr;
   int router_dtype = MOE_ROUTER_F32;
   int vec = 0;  // all expert bases 8-byte aligned -> vector weight loads
+  int int4 = 0;  // INT4 experts (src/int8_expert.rs:473-649): GEMV paths only
   // tensor-core path: only for the packed layout (one 3D tensor map per GEMM)
   bool tc_ok = false;
   CUtensorMap map_gu{}, map_dn{};
@@ -667,8 +668,17 @@ bool use_stream(const moe_handle *h, int T, int first_layer, int n_layers, const
   if (!stream_decode_supported(T, h->d.hidden, h->d.intermediate, h->d.num_experts, h->d.top_k))
     return false;
   for (int l = first_layer; l < first_layer + n_layers; ++l)
-    if (!h->flayers[l].prefetch_ok) return false;
+    if (!h->flayers[l].prefetch_ok || h->flayers[l].int4) return false;
   return true;
+}
+
+// One weight format over layers [first, first + n) (the single-launch kernel
+// is compiled per format); -1 when they differ.
+int layers_quant(const moe_handle *h, int first, int n) {
+  const int q = h->flayers[first].int4;
+  for (int l = first + 1; l < first + n; ++l)
+    if (h->flayers[l].int4 != q) return -1;
+  return q;
 }
 
 // Launch the streaming decode kernel with the handle's next counter set.
@@ -796,6 +806,7 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
     f.out = d_out;
     f.ids_out = d_ids;
     f.gates_out = d_gates;
+    f.int4 = L.int4;
     if (!d_ids || !d_gates) f.ids_out = nullptr;
     const int vec = h->layer_vec[layer] && ((uintptr_t)d_h & 15) == 0;
     f.router_async = h->layer_async[layer] && ((uintptr_t)d_h & 15) == 0;
@@ -839,6 +850,7 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
   a.status = h->status;
   a.sm_count = h->sm_count;
   a.vec = L.vec && ((uintptr_t)d_h & 15) == 0;
+  a.int4 = L.int4;
   cudaEvent_t p0 = h->prof.begin(s);
   cudaError_t e = launch_gate_up(a, s);
   h->prof.end("gate_up_gemv", p0, s);
@@ -985,15 +997,21 @@ extern "C" moe_status moe_set_path(moe_handle *h, int path) {
   return MOE_OK;
 }
 
-extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const *d_weights,
-                                    const void *const *d_scales, const void *d_router,
-                                    int router_dtype) {
+extern "C" moe_status moe_set_layer_q(moe_handle *h, int layer, const void *const *d_weights,
+                                      const void *const *d_scales, const void *d_router,
+                                      int router_dtype, int quant) {
   if (!h) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
   drop_graphs(h);
   if (layer < 0 || layer >= (int)h->layers.size() || !d_weights || !d_scales || !d_router ||
-      (router_dtype != MOE_ROUTER_F32 && router_dtype != MOE_ROUTER_BF16)) {
+      (router_dtype != MOE_ROUTER_F32 && router_dtype != MOE_ROUTER_BF16) ||
+      (quant != MOE_QUANT_INT8 && quant != MOE_QUANT_INT4)) {
     set_err(h->err, "moe_set_layer: invalid argument");
+    return MOE_ERR_INVALID;
+  }
+  const int int4 = quant == MOE_QUANT_INT4;
+  if (int4 && ((h->d.hidden | h->d.intermediate) & 1)) {  // src/int8_expert.rs:116-118
+    set_err(h->err, "hidden and intermediate must be even for INT4");
     return MOE_ERR_INVALID;
   }
   const int E = h->d.num_experts;
@@ -1015,15 +1033,17 @@ extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const 
   L.router = d_router;
   L.router_dtype = router_dtype;
   L.vec = vec;
+  L.int4 = int4;
   // Packed layout (expert e at base + e * 3IH, scales at sbase + e * (2I+H))
-  // enables the tensor-core path.
+  // enables the tensor-core path (INT8 experts only).
   const size_t H = h->d.hidden, I = h->d.intermediate;
+  const size_t wbytes = 3 * I * H / (int4 ? 2 : 1);
   bool packed = true;
   for (int e = 1; e < E && packed; ++e)
-    packed = (const char *)d_weights[e] == (const char *)d_weights[0] + e * 3 * I * H &&
+    packed = (const char *)d_weights[e] == (const char *)d_weights[0] + e * wbytes &&
              (const float *)d_scales[e] == (const float *)d_scales[0] + e * (2 * I + H);
   const char *wb = (const char *)d_weights[0];
-  L.tc_ok = packed && h->tc_ok &&
+  L.tc_ok = packed && !int4 && h->tc_ok &&
             tc::encode_map3d(&L.map_gu, wb, H, 2 * I, E, H, 3 * I * H, 128) &&
             tc::encode_map3d(&L.map_dn, wb + 2 * I * H, I, H, E, I, 3 * I * H, 128);
   bool align16 = true;
@@ -1033,7 +1053,10 @@ extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const 
   F.s_ptr = L.d_sptr;
   F.router = d_router;
   F.router_dtype = router_dtype;
-  F.prefetch_ok = align16 && H % 16 == 0 && I % 16 == 0;
+  F.int4 = int4;
+  // bulk L2 prefetches need 16-byte aligned rows
+  F.prefetch_ok = align16 && (H / (int4 ? 2 : 1)) % 16 == 0 && (I / (int4 ? 2 : 1)) % 16 == 0 &&
+                  (!int4 || (H % 32 == 0 && I % 32 == 0));
   h->layer_vec[layer] = vec;
   h->layer_async[layer] = router_dtype == MOE_ROUTER_F32 && ((uintptr_t)d_router & 15) == 0 &&
                           H % 4 == 0;
@@ -1048,6 +1071,12 @@ extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const 
     L.own_w = L.own_s = L.own_r = nullptr;
   }
   return MOE_OK;
+}
+
+extern "C" moe_status moe_set_layer(moe_handle *h, int layer, const void *const *d_weights,
+                                    const void *const *d_scales, const void *d_router,
+                                    int router_dtype) {
+  return moe_set_layer_q(h, layer, d_weights, d_scales, d_router, router_dtype, MOE_QUANT_INT8);
 }
 
 namespace {
@@ -1110,7 +1139,10 @@ extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_
   };
   if (layer < 0 || layer >= (int)h->layers.size()) return fail(MOE_ERR_INVALID, "layer out of range");
   // descriptors first, no payload read (src/olmoe.rs:1080-1099)
+  // INT8: I8 [3IH]; INT4: U8 [3IH/2] (src/int8_expert.rs:107-122, src/olmoe.rs:1086-1091);
+  // every expert of the layer in the same format
   std::vector<const CkptTensor *> wt(E), st(E);
+  int int4 = -1;
   for (size_t e = 0; e < E; ++e) {
     const std::string pre = "model.layers." + std::to_string(ckpt_layer) + ".mlp.experts." +
                             std::to_string(e);
@@ -1119,13 +1151,17 @@ extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_
     if (!wt[e]) return fail(MOE_ERR_INVALID, "missing tensor: " + pre + ".merged_weight");
     if (!st[e]) return fail(MOE_ERR_INVALID, "missing tensor: " + pre + ".qs");
     const auto &ws = wt[e]->shape;
-    if (wt[e]->dtype == MOE_DT_U8 && ws.size() == 1 && (size_t)ws[0] == wcount / 2)
-      return fail(MOE_ERR_INVALID, pre + ": INT4 experts are not supported on this path");
-    if (wt[e]->dtype != MOE_DT_I8 || ws.size() != 1 || (size_t)ws[0] != wcount ||
-        st[e]->dtype != MOE_DT_F32 || st[e]->shape.size() != 1 ||
-        (size_t)st[e]->shape[0] != scount)
+    int q = -1;
+    if (wt[e]->dtype == MOE_DT_I8 && ws.size() == 1 && (size_t)ws[0] == wcount) q = 0;
+    else if (wt[e]->dtype == MOE_DT_U8 && ws.size() == 1 && (size_t)ws[0] == wcount / 2 &&
+             H % 2 == 0 && I % 2 == 0)
+      q = 1;
+    if (q < 0 || (int4 >= 0 && q != int4) || st[e]->dtype != MOE_DT_F32 ||
+        st[e]->shape.size() != 1 || (size_t)st[e]->shape[0] != scount)
       return fail(MOE_ERR_INVALID, pre + ": invalid merged expert layout");
+    int4 = q;
   }
+  const size_t wbytes = int4 ? wcount / 2 : wcount;
   const std::string rname = "model.layers." + std::to_string(ckpt_layer) + ".mlp.gate.weight";
   const CkptTensor *rt = ckpt_find(c, rname);
   if (!rt) return fail(MOE_ERR_INVALID, "missing tensor: " + rname);
@@ -1163,15 +1199,15 @@ extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_
     cudaFree(dr);
     cudaFreeHost(stage);
   };
-  if (cudaMalloc(&dw, E * wcount) != cudaSuccess || cudaMalloc(&ds, E * scount * 4) != cudaSuccess ||
+  if (cudaMalloc(&dw, E * wbytes) != cudaSuccess || cudaMalloc(&ds, E * scount * 4) != cudaSuccess ||
       cudaMalloc(&dr, bf16 ? E * H * 2 : E * H * 4) != cudaSuccess ||
-      cudaMallocHost(&stage, wcount + scount * 4) != cudaSuccess) {
+      cudaMallocHost(&stage, wbytes + scount * 4) != cudaSuccess) {
     release();
     return fail(MOE_ERR_NOMEM, "moe_load_layer: out of memory");
   }
   // experts one by one through a pinned staging buffer
   for (size_t e = 0; e < E; ++e) {
-    float *sc = reinterpret_cast<float *>(stage + wcount);
+    float *sc = reinterpret_cast<float *>(stage + wbytes);
     if (!ckpt_read(c, *wt[e], stage) || !ckpt_read(c, *st[e], sc)) {
       release();
       return fail(MOE_ERR_INVALID, "expert " + std::to_string(e) + ": short read");
@@ -1181,7 +1217,7 @@ extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_
         release();
         return fail(MOE_ERR_INVALID, "expert scales must be finite and positive");
       }
-    if (cudaMemcpy(dw + e * wcount, stage, wcount, cudaMemcpyHostToDevice) != cudaSuccess ||
+    if (cudaMemcpy(dw + e * wbytes, stage, wbytes, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(ds + e * scount, sc, scount * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
       release();
       return fail(MOE_ERR_CUDA, "moe_load_layer: upload failed");
@@ -1237,8 +1273,9 @@ extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_
       return fail(MOE_ERR_NOMEM, "moe_load_layer: norm upload failed");
     }
   }
-  const moe_status st2 =
-      moe_set_layer_packed(h, layer, dw, ds, dr, bf16 ? MOE_ROUTER_BF16 : MOE_ROUTER_F32);
+  const moe_status st2 = moe_set_layer_packed_q(h, layer, dw, ds, dr,
+                                                bf16 ? MOE_ROUTER_BF16 : MOE_ROUTER_F32,
+                                                int4 ? MOE_QUANT_INT4 : MOE_QUANT_INT8);
   if (st2 != MOE_OK) {
     cudaFree(dn);
     release();
@@ -1254,17 +1291,25 @@ extern "C" moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_
   return st3;
 }
 
+extern "C" moe_status moe_set_layer_packed_q(moe_handle *h, int layer, const void *d_experts,
+                                             const float *d_scales, const void *d_router,
+                                             int router_dtype, int quant) {
+  if (!h || !d_experts || !d_scales) return MOE_ERR_INVALID;
+  const size_t E = h->d.num_experts, H = h->d.hidden, I = h->d.intermediate;
+  const size_t wbytes = 3 * I * H / (quant == MOE_QUANT_INT4 ? 2 : 1);
+  std::vector<const void *> w(E), s(E);
+  for (size_t e = 0; e < E; ++e) {
+    w[e] = static_cast<const int8_t *>(d_experts) + e * wbytes;
+    s[e] = d_scales + e * (2 * I + H);
+  }
+  return moe_set_layer_q(h, layer, w.data(), s.data(), d_router, router_dtype, quant);
+}
+
 extern "C" moe_status moe_set_layer_packed(moe_handle *h, int layer, const int8_t *d_experts,
                                            const float *d_scales, const void *d_router,
                                            int router_dtype) {
-  if (!h || !d_experts || !d_scales) return MOE_ERR_INVALID;
-  const size_t E = h->d.num_experts, H = h->d.hidden, I = h->d.intermediate;
-  std::vector<const void *> w(E), s(E);
-  for (size_t e = 0; e < E; ++e) {
-    w[e] = d_experts + e * 3 * I * H;
-    s[e] = d_scales + e * (2 * I + H);
-  }
-  return moe_set_layer(h, layer, w.data(), s.data(), d_router, router_dtype);
+  return moe_set_layer_packed_q(h, layer, d_experts, d_scales, d_router, router_dtype,
+                                MOE_QUANT_INT8);
 }
 
 extern "C" moe_status moe_route(moe_handle *h, int layer, const float *d_h, int T,
@@ -1354,10 +1399,12 @@ moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, fl
                                 float rms_eps, cudaStream_t s) {
   bool vec_all = ((uintptr_t)d_x & 15) == 0;
   for (int l = first_layer; l < first_layer + n_layers; ++l) vec_all = vec_all && h->layer_vec[l];
-  if (h->path != MOE_PATH_TENSOR && use_fused(h, T)) {
+  const int quant = layers_quant(h, first_layer, n_layers);
+  if (h->path != MOE_PATH_TENSOR && use_fused(h, T) && quant >= 0) {
     FusedArgs f = fused_args(h, T);
     f.n_layers = n_layers;
     f.stacked = 1;
+    f.int4 = quant;
     f.layers = h->d_flayers + first_layer;
     f.out = d_x;
     f.hbuf = h->hbuf;

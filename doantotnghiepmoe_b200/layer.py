@@ -78,13 +78,16 @@ class MoeLayerEngine:
         self._check(lib().moe_set_path(self._h, path))
 
     def set_layer_packed(self, layer: int, experts, scales, router):
-        """experts: CUDA int8 [E, 3*I*H]; scales: CUDA f32 [E, 2I+H]; router: CUDA
-        f32 [E, H] or int16/uint16-viewed bf16 bits [E, H]."""
+        """experts: CUDA int8 [E, 3*I*H] (or uint8 [E, 3*I*H/2]: INT4 nibble
+        pairs); scales: CUDA f32 [E, 2I+H]; router: CUDA f32 [E, H] or
+        int16/uint16-viewed bf16 bits [E, H]."""
         import torch
         dtype = MOE_ROUTER_F32 if router.dtype == torch.float32 else MOE_ROUTER_BF16
+        quant = 1 if experts.dtype == torch.uint8 else 0
         self._keep[layer] = (experts, scales, router)
-        self._check(lib().moe_set_layer_packed(self._h, layer, experts.data_ptr(),
-                                               scales.data_ptr(), router.data_ptr(), dtype))
+        self._check(lib().moe_set_layer_packed_q(self._h, layer, experts.data_ptr(),
+                                                 scales.data_ptr(), router.data_ptr(), dtype,
+                                                 quant))
 
     def set_layer(self, layer: int, expert_weights: list, expert_scales: list, router):
         """Per-expert device pointers (pool slots) -- the GpuExpertWeights borrow."""

@@ -93,6 +93,12 @@ enum {
   MOE_ROUTER_BF16 = 1, /* bf16 bits [E,H] (src/dense.rs:58-73) */
 };
 
+/* Expert weight formats (src/int8_expert.rs:14-17, :107-122). */
+enum {
+  MOE_QUANT_INT8 = 0, /* int8 per weight: 3*I*H bytes per expert */
+  MOE_QUANT_INT4 = 1  /* two signed nibbles per byte, element 2i low: 3*I*H/2 bytes */
+};
+
 /* Routing semantics. */
 enum {
   MOE_ROUTE_SOFTMAX_TOPK = 0, /* OlmoeModel (default): softmax over E, top-k, optional renorm */
@@ -138,6 +144,20 @@ moe_status moe_set_layer(moe_handle *h, int layer, const void *const *d_weights,
  * d_scales + e*(2*I+H). */
 moe_status moe_set_layer_packed(moe_handle *h, int layer, const int8_t *d_experts,
                                 const float *d_scales, const void *d_router, int router_dtype);
+
+/* The same two calls with the experts' weight format (MOE_QUANT_*).  INT4
+ * experts (H and I even) run on the exact GEMV paths -- the per-phase
+ * launches and the single-launch decode kernel -- bit-identical to the
+ * reference's INT4 AVX2 path (src/int8_expert.rs:519-637, :785-952); the
+ * tensor-core prefill path and the streaming kernel take INT8 layers only,
+ * so an INT4 layer uses the GEMV path at every T.  A stack mixing formats
+ * runs one launch per phase. */
+moe_status moe_set_layer_q(moe_handle *h, int layer, const void *const *d_weights,
+                           const void *const *d_scales, const void *d_router, int router_dtype,
+                           int quant);
+moe_status moe_set_layer_packed_q(moe_handle *h, int layer, const void *d_experts,
+                                  const float *d_scales, const void *d_router, int router_dtype,
+                                  int quant);
 
 /* Routing only: ids/gates [T,K] (device).  probs (optional, device [T,E])
  * receives the post-softmax probabilities. */
@@ -287,7 +307,8 @@ moe_status moe_ckpt_read(const moe_ckpt *c, const char *name, void *dst, size_t 
  * The checks are the reference's Int8Expert::load_into
  * (src/int8_expert.rs:90-170): I8 merged_weight of exactly 3*I*H elements,
  * F32 qs of 2*I + H, scales finite and > 0; a router of [E, H] with finite
- * values.  INT4 experts (U8 [3*I*H/2]) are reported as unsupported.  A
+ * values.  INT4 experts (U8 [3*I*H/2], every expert of the layer) load as
+ * MOE_QUANT_INT4.  A
  * `model.layers.{l}.post_attention_layernorm.weight` [H] becomes the slot's
  * RMSNorm gain (moe_set_layer_norm), likewise owned by the handle. */
 moe_status moe_load_layer(moe_handle *h, const moe_ckpt *c, int ckpt_layer, int layer,

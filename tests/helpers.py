@@ -42,7 +42,7 @@ def rel_err(a, b) -> float:
 
 def to_device(lw: "O.LayerWeights", device="cuda"):
     import torch
-    experts = torch.from_numpy(np.ascontiguousarray(lw.experts)).to(device)
+    experts = torch.from_numpy(np.ascontiguousarray(lw.experts)).to(device)  # uint8 = INT4
     scales = torch.from_numpy(np.ascontiguousarray(lw.scales)).to(device)
     if lw.router_bf16:
         router = torch.from_numpy(lw.router.view(np.int16).copy()).to(device)

@@ -4,8 +4,9 @@ A checkpoint written here in the converter's layout (tools/prepare_olmoe.py:
 85-94) is loaded into engine slots and run: routing and outputs are
 bit-identical to the oracle on the same weights, for an f32 router, a BF16
 router kept as BF16 and the same widened to f32.  The loader's checks
-(src/int8_expert.rs:90-170) reject missing tensors, INT4-shaped experts and
-non-positive scales; a slot set again by the caller releases the loaded copy.
+(src/int8_expert.rs:90-170) reject missing tensors, formats mixed within a
+layer and non-positive scales; a slot set again by the caller releases the
+loaded copy.
 """
 import numpy as np
 import pytest
@@ -85,18 +86,18 @@ def test_loaded_layers_bit_exact(tmp_path):
 def test_loader_rejects_bad_layers(tmp_path):
     lw = O.synth_layer(73, 0, H, I, E, K, False)
     eng = M.MoeLayerEngine(M.MoeConfig(H, I, E, K, False, 4, 1))
-    # INT4-shaped experts (U8, half the bytes)
-    d = tmp_path / "int4"
+    # INT8 and INT4 experts mixed in one layer
+    d = tmp_path / "mixed"
     d.mkdir()
     t = [(f"model.layers.0.mlp.gate.weight", "F32", lw.router)]
     for e in range(E):
-        t.append((f"model.layers.0.mlp.experts.{e}.merged_weight", "U8",
-                  lw.experts[e][: 3 * I * H // 2].view(np.uint8)))
+        w = lw.experts[e][: 3 * I * H // 2].view(np.uint8) if e == 3 else lw.experts[e]
+        t.append((f"model.layers.0.mlp.experts.{e}.merged_weight", "U8" if e == 3 else "I8", w))
         t.append((f"model.layers.0.mlp.experts.{e}.qs", "F32", lw.scales[e]))
     write_safetensors(d / "m.safetensors", t)
     with pytest.raises(M.MoeError) as ei:
         eng.load_layer(M.Checkpoint(str(d)), 0)
-    assert ei.value.status == _lib.MOE_ERR_INVALID and "INT4" in ei.value.message
+    assert ei.value.status == _lib.MOE_ERR_INVALID and "layout" in ei.value.message
     # a zero scale
     d = tmp_path / "scale"
     d.mkdir()
