@@ -129,16 +129,39 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def algorithmic_bytes(cfg, D: float, T: int) -> dict:
+def algorithmic_bytes(cfg, D: float, T: int, wdiv: int = 1) -> dict:
     """Per-layer algorithmic bytes: active expert weights + scales once, the
-    router once, the hidden states in and the outputs out."""
+    router once, the hidden states in and the outputs out.  wdiv = 2 for INT4
+    experts (two weights per byte)."""
     H, I, E, K = cfg["H"], cfg["I"], cfg["E"], cfg["K"]
     R = T * K
-    layer = D * (3 * I * H + 4 * (2 * I + H)) + 4 * E * H + 8 * T * H
-    gate_up = D * (2 * I * H + 8 * I) + 4 * T * H + 4 * R * I
-    down = D * (I * H + 4 * H) + 4 * R * I + 4 * R * H
+    layer = D * (3 * I * H // wdiv + 4 * (2 * I + H)) + 4 * E * H + 8 * T * H
+    gate_up = D * (2 * I * H // wdiv + 8 * I) + 4 * T * H + 4 * R * I
+    down = D * (I * H // wdiv + 4 * H) + 4 * R * I + 4 * R * H
     return {"layer": layer, "gate_up_gemv": gate_up, "down_gemv": down,
             "gate_up_tc": gate_up, "down_tc": down}
+
+
+def int4_from_int8(w8):
+    """Synthetic INT4 experts from the INT8 generator: each weight keeps its
+    top four bits (w >> 4, in [-8, 7]); element 2i goes to the low nibble of
+    byte i (src/int8_expert.rs:473-516).  numpy or torch, any leading shape."""
+    lo, hi = (w8[..., 0::2] >> 4) & 0xF, (w8[..., 1::2] >> 4) & 0xF
+    packed = lo | (hi << 4)  # int8 bit patterns
+    if isinstance(packed, np.ndarray):
+        return packed.view(np.uint8)
+    import torch
+    return packed.contiguous().view(torch.uint8)
+
+
+def oracle_layer(cfg, quant):
+    from oracle import oracle as O
+    H, I, E, K = cfg["H"], cfg["I"], cfg["E"], cfg["K"]
+    L = O.synth_layer(SEED, 0, H, I, E, K, cfg["norm"])
+    if quant == "int4":
+        L = O.LayerWeights(H, I, E, K, cfg["norm"], L.router, int4_from_int8(L.experts),
+                           (L.scales * 16.0).astype(np.float32), int4=True)
+    return L
 
 
 def run_reference(args, cfg, rank, world):
@@ -148,7 +171,7 @@ def run_reference(args, cfg, rank, world):
     from oracle import oracle as O
     threads = os.cpu_count() or 1
     H, I, E, K, T = cfg["H"], cfg["I"], cfg["E"], cfg["K"], cfg["T"]
-    L = O.synth_layer(SEED, 0, H, I, E, K, cfg["norm"])
+    L = oracle_layer(cfg, args.quant)
     sample = min(T, 32)
     h = O.synth_hidden(SEED, sample, H)
     for _ in range(max(1, args.warmup)):
@@ -166,8 +189,9 @@ def run_reference(args, cfg, rank, world):
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": cfg["workload"], "hidden": H, "intermediate": I,
-                       "experts": E, "top_k": K, "tokens": T, "layers": cfg["stack"]},
+            "config": {"workload": workload_name(cfg, args.quant), "hidden": H,
+                       "intermediate": I, "experts": E, "top_k": K, "tokens": T,
+                       "layers": cfg["stack"], "weights": args.quant},
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": f"{sample} of {T} tokens per step, "
                                        f"{cfg['stack']} layer(s)"},
@@ -176,12 +200,16 @@ def run_reference(args, cfg, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline(cfg) -> dict:
+def workload_name(cfg, quant):
+    return cfg["workload"] + ("_int4" if quant == "int4" else "")
+
+
+def cpu_baseline(cfg, quant="int8") -> dict:
     """Oracle (C restatement of the reference CPU path) on a bounded sample."""
     from oracle import oracle as O
     threads = min(8, os.cpu_count() or 1)  # the reference's default pool, src/backend.rs:21-24
     H, I, E, K, T = cfg["H"], cfg["I"], cfg["E"], cfg["K"], cfg["T"]
-    L = O.synth_layer(SEED, 0, H, I, E, K, cfg["norm"])
+    L = oracle_layer(cfg, quant)
     sample = min(T, 32)
     h = O.synth_hidden(SEED, sample, H)
     O.layer_forward(L, h[:1], nthreads=threads)
@@ -209,6 +237,8 @@ def main():
     ap.add_argument("--path", default="auto", choices=["auto", "gemv", "tensor", "gemv_fused",
                                                           "gemv_stream"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quant", default="int8", choices=["int8", "int4"],
+                    help="expert weight format (int4: two signed nibbles per byte)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     rank, world, local = dist_env()
@@ -230,7 +260,10 @@ def main():
         return run_ep(args, cfg, rank, world, local)
     H, I, E, K, T = cfg["H"], cfg["I"], cfg["E"], cfg["K"], cfg["T"]
     n_stack = cfg["stack"]
-    layer_bytes = E * (3 * I * H + 4 * (2 * I + H))
+    wdiv = 2 if args.quant == "int4" else 1
+    if wdiv == 2 and args.path in ("tensor", "gemv_stream"):
+        raise SystemExit("--quant int4 runs on the exact GEMV paths only")
+    layer_bytes = E * (3 * I * H // wdiv + 4 * (2 * I + H))
     # Rotation of distinct layers so that consecutive steps never hit L2.
     n_layers = max(n_stack, int(np.ceil(3 * 126e6 / layer_bytes)) + 1)
     if n_stack > 1:
@@ -247,6 +280,8 @@ def main():
             sc = torch.empty((E, 2 * I + H), dtype=torch.float32, device="cuda")
             for e in range(E):
                 M.synth_expert(SEED, l, e, H, I, ex[e], sc[e], stream=stream)
+            if wdiv == 2:
+                ex, sc = int4_from_int8(ex), sc * 16.0
             rt = torch.from_numpy(synthetic.router(SEED, l, E, H, cfg.get("zipf", False))).cuda()
             eng.set_layer_packed(l, ex, sc, rt)
             keep.append((ex, sc, rt))
@@ -361,7 +396,7 @@ def main():
 
     # ---- roofline of the dominant kernel --------------------------------
     hbm_peak, _, peak_kind = measured_peaks()
-    alg = algorithmic_bytes(cfg, D, T)
+    alg = algorithmic_bytes(cfg, D, T, wdiv)
     alg["fused_decode"] = alg["layer"] * n_stack  # one launch runs the whole step
     alg["stream_decode"] = alg["layer"] * n_stack
     phases = {k: v for k, v in prof.items() if ":" in k}
@@ -376,7 +411,7 @@ def main():
     if os.path.exists(tp):
         with open(tp) as f:
             tj = json.load(f)
-        ent = tj.get(cfg["workload"], {}).get(kname)
+        ent = tj.get(workload_name(cfg, args.quant), {}).get(kname)
         if ent:
             traffic = ent.get("bytes_per_launch")
     roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm_peak,
@@ -391,7 +426,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_baseline(cfg)
+            cpu = cpu_baseline(cfg, args.quant)
         except Exception as exc:  # the baseline is reported, never required
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "port",
                    "sample": f"failed: {exc}"}
@@ -401,7 +436,8 @@ def main():
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": cfg["workload"], "hidden": H, "intermediate": I,
+                "config": {"workload": workload_name(cfg, args.quant), "hidden": H,
+                           "intermediate": I, "weights": args.quant,
                            "experts": E, "top_k": K, "norm_topk_prob": cfg["norm"],
                            "tokens_per_rank": T, "layers_per_step": n_stack,
                            "distinct_experts_per_layer": D,
