@@ -263,6 +263,12 @@ __device__ void build_tables(const FusedArgs &a, Tables &tb) {
   }
 }
 
+// Weight loads stream in register batches of kDecodePF chunk-steps, two in
+// flight.  Deeper batches did not help: on B200 the phases are bound by
+// the grid barriers (every CTA waits for the slowest item), not by the
+// per-thread load chain -- INT4 (half the bytes) runs at INT8 speed, and an
+// 8-deep INT4 batch made the multi-route variant slower.
+constexpr int kDecodePF = 4;
 constexpr int kGURowsItem = kGURowsPerWarp * (kFT / 32);  // 32
 constexpr int kDNRowsItem = kDNRowsPerWarp * (kFT / 32);  // 64
 
@@ -313,11 +319,11 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
     const int r0 = tb.seg_off[e], r1 = tb.seg_off[e + 1];
     const int row0 = (item % nb_gu) * kGURowsItem;
     if (!kMulti || r1 - r0 == 1)
-      gate_up_item<kVec, 1, 4, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, tb.r_token, hin,
-                                   stage, a.act);
+      gate_up_item<kVec, 1, kDecodePF, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0,
+                                                       r1, tb.r_token, hin, stage, a.act);
     else
-      gate_up_item<kVec, 4, 4, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, tb.r_token, hin,
-                                   stage, a.act);
+      gate_up_item<kVec, 4, kDecodePF, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0,
+                                                      r1, tb.r_token, hin, stage, a.act);
   }
   ++nbar;
   if (!grid_sync(a.bar, nbar * G, a.status)) {
@@ -335,11 +341,11 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
       a.contrib[((size_t)tb.r_token[r] * a.K + tb.r_slot[r]) * H + row] = __fmul_rn(tb.r_gate[r], y);
     };
     if (!kMulti || r1 - r0 == 1)
-      good &= down_item<kVec, 1, 4, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, a.act,
-                                        stage, emit);
+      good &= down_item<kVec, 1, kDecodePF, kQ>(L.w_ptr[e], L.s_ptr[e], H, I,
+                                                            row0, r0, r1, a.act, stage, emit);
     else
-      good &= down_item<kVec, 4, 4, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0, r1, a.act,
-                                        stage, emit);
+      good &= down_item<kVec, 4, kDecodePF, kQ>(L.w_ptr[e], L.s_ptr[e], H, I,
+                                                           row0, r0, r1, a.act, stage, emit);
   }
   if (!good) set_status(a.status, kStatusNonFinite);
   ++nbar;
