@@ -27,6 +27,7 @@
 #include <algorithm>
 
 #include "gemv_core.cuh"
+#include "gemv_tiles.cuh"
 #include "kernels.h"
 #include "route_core.cuh"
 
@@ -41,6 +42,7 @@ constexpr int kRTE = 4;           // router task: experts
 constexpr long long kBarrierCycles = 2000000000LL;  // ~1 s
 
 struct Tables {
+  uint64_t tile_full[kTileStages];  // weight-tile ring mbarriers
   int32_t seg_off[kMaxExperts + 1];
   int32_t active[kMaxExperts];
   int32_t run[kMaxExperts];
@@ -271,10 +273,16 @@ __device__ void build_tables(const FusedArgs &a, Tables &tb) {
 constexpr int kDecodePF = 4;
 constexpr int kGURowsItem = kGURowsPerWarp * (kFT / 32);  // 32
 constexpr int kDNRowsItem = kDNRowsPerWarp * (kFT / 32);  // 64
+static_assert(kGURowsItem == kTileGURows && kDNRowsItem == kTileDNRows,
+              "a decode work item is one weight tile");
+constexpr int kTensorMapBytes = 128;  // sizeof(CUtensorMap)
 
-template <bool kVec, bool kMulti, int kQ>
+// kTiles: weights stream through the TMA tile ring (every layer of the
+// launch has tile maps); otherwise each thread loads its own weights.
+template <bool kVec, bool kMulti, int kQ, bool kTiles>
 __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const float *hin,
-                              float *stage, Tables &tb, uint32_t &nbar, bool &alive) {
+                              float *stage, Tables &tb, TileRing &rg, uint32_t &nbar,
+                              bool &alive) {
   const int H = a.H, I = a.I, G = gridDim.x;
   const int nseg = tb.n_active;
   const int nb_gu = (I + kGURowsItem - 1) / kGURowsItem;
@@ -285,6 +293,8 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
   // their own prefetches).
   const size_t hb = (size_t)H * kQ / 8, ib = (size_t)I * kQ / 8;  // bytes per row
   const bool all_up_front = (size_t)nseg * 3 * I * hb <= ((size_t)64 << 20);
+  const char *map_gu = static_cast<const char *>(L.tmaps);
+  const char *map_dn = map_gu + kTensorMapBytes;
   auto pf_gu = [&](int item) {
     if (threadIdx.x != 0 || !L.prefetch_ok || item >= nseg * nb_gu) return;
     const int e = tb.active[item / nb_gu], row0 = (item % nb_gu) * kGURowsItem;
@@ -318,7 +328,16 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
     const int e = tb.active[item / nb_gu];
     const int r0 = tb.seg_off[e], r1 = tb.seg_off[e + 1];
     const int row0 = (item % nb_gu) * kGURowsItem;
-    if (!kMulti || r1 - r0 == 1)
+    if constexpr (kTiles) {
+      if (rg.dead) continue;
+      const bool ok =
+          (!kMulti || r1 - r0 == 1)
+              ? gate_up_tile_item<1, kQ>(rg, map_gu, e, L.s_ptr[e], H, I, row0, r0, r1,
+                                         tb.r_token, hin, stage, a.act)
+              : gate_up_tile_item<kTG, kQ>(rg, map_gu, e, L.s_ptr[e], H, I, row0, r0, r1,
+                                           tb.r_token, hin, stage, a.act);
+      if (!ok) set_status(a.status, kStatusTimeout);
+    } else if (!kMulti || r1 - r0 == 1)
       gate_up_item<kVec, 1, kDecodePF, kQ>(L.w_ptr[e], L.s_ptr[e], H, I, row0, r0,
                                                        r1, tb.r_token, hin, stage, a.act);
     else
@@ -340,7 +359,16 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
     auto emit = [&](int r, int row, float y) {
       a.contrib[((size_t)tb.r_token[r] * a.K + tb.r_slot[r]) * H + row] = __fmul_rn(tb.r_gate[r], y);
     };
-    if (!kMulti || r1 - r0 == 1)
+    if constexpr (kTiles) {
+      if (rg.dead) continue;
+      const bool ok =
+          (!kMulti || r1 - r0 == 1)
+              ? down_tile_item<1, kQ>(rg, map_dn, e, L.s_ptr[e], H, I, row0, r0, r1, a.act,
+                                      stage, good, emit)
+              : down_tile_item<kTG, kQ>(rg, map_dn, e, L.s_ptr[e], H, I, row0, r0, r1, a.act,
+                                        stage, good, emit);
+      if (!ok) set_status(a.status, kStatusTimeout);
+    } else if (!kMulti || r1 - r0 == 1)
       good &= down_item<kVec, 1, kDecodePF, kQ>(L.w_ptr[e], L.s_ptr[e], H, I,
                                                             row0, r0, r1, a.act, stage, emit);
     else
@@ -398,7 +426,7 @@ constexpr size_t kSelOff = align128(sizeof(Tables));
 constexpr size_t kStageOff = align128(kSelOff + 8 * sizeof(SelectScratch));
 
 // kQ: the weight format of every layer in the launch (8 or 4 bits).
-template <bool kVec, bool kMulti, int kQ>
+template <bool kVec, bool kMulti, int kQ, bool kTiles>
 __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(FusedArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   Tables &tb = *reinterpret_cast<Tables *>(smem);
@@ -410,6 +438,15 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
   bool alive = true;
   const float *hin = a.h_in;
   stamp(a, 0);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTileStages; ++i) tma::mbar_init(&tb.tile_full[i], 1);
+    tma::fence_mbar_init();
+  }
+  __syncthreads();
+  const uintptr_t ring_at =
+      reinterpret_cast<uintptr_t>(stage) + (size_t)kTG * (size_t)max(H, a.I) * sizeof(float);
+  TileRing rg{reinterpret_cast<uint8_t *>((ring_at + 1023) & ~uintptr_t(1023)), tb.tile_full, 0u,
+              false};
   if (a.stacked) {
     for (int t = blockIdx.x; t < T; t += G)
       rms_row(a.out + (size_t)t * H, a.layers[0].norm_w, a.hbuf + (size_t)t * H, H, a.eps, red,
@@ -425,7 +462,7 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
     if (!grid_sync(a.bar, nbar * G, a.status)) return;
     if (l == 0) stamp(a, 1);
     build_tables(a, tb);
-    expert_phases<kVec, kMulti, kQ>(a, L, hin, stage, tb, nbar, alive);
+    expert_phases<kVec, kMulti, kQ, kTiles>(a, L, hin, stage, tb, rg, nbar, alive);
     if (!alive) return;
     if (!a.stacked) {
       // C: out = resid + contrib[., 0] + ... + contrib[., K-1] (slot order)
@@ -472,9 +509,12 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
   stamp(a, 4);
 }
 
-size_t fused_smem_bytes(int H, int I) {
+size_t fused_smem_bytes(int H, int I, bool tiles) {
   const size_t router = (size_t)(kRTT + kRTE) * H * sizeof(float);
-  const size_t gemv = (size_t)kTG * std::max(H, I) * sizeof(float);
+  // token rows, then (tile variants) the weight-tile ring on a 1024-byte
+  // boundary
+  const size_t gemv = (size_t)kTG * std::max(H, I) * sizeof(float) +
+                      (tiles ? 1024 + kTileRingBytes : 0);
   return kStageOff + std::max(router, gemv);
 }
 
@@ -482,37 +522,48 @@ size_t fused_smem_bytes(int H, int I) {
 
 bool fused_decode_supported(int T, int H, int I, int E, int K) {
   return T >= 1 && T * K <= kFusedMaxRoutes && H <= kFusedMaxH && I <= kFusedMaxH &&
-         E <= kMaxExperts && fused_smem_bytes(H, I) <= 113 * 1024;
+         E <= kMaxExperts && fused_smem_bytes(H, I, true) <= 113 * 1024;
 }
 
 cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint32_t *bar,
                                 cudaStream_t s) {
-  const size_t smem = fused_smem_bytes(a.H, a.I);
+  const bool multi = a.T > 1;
+  const bool tiles = a.tiles != 0 && !multi;
+  const size_t smem = fused_smem_bytes(a.H, a.I, tiles);
   // vector loads need 8-byte weight rows (H, I multiples of 8) on top of the
   // caller's pointer-alignment check
   vec = vec && a.H % 8 == 0 && a.I % 8 == 0;
   // A single token per call means every expert segment holds one route:
   // the lighter single-route variant then fits two CTAs per SM.
-  const bool multi = a.T > 1;
   const void *fn;
-  if (a.int4)
-    fn = vec ? (multi ? (const void *)fused_decode_kernel<true, true, 4>
-                      : (const void *)fused_decode_kernel<true, false, 4>)
-             : (multi ? (const void *)fused_decode_kernel<false, true, 4>
-                      : (const void *)fused_decode_kernel<false, false, 4>);
-  else
-    fn = vec ? (multi ? (const void *)fused_decode_kernel<true, true, 8>
-                      : (const void *)fused_decode_kernel<true, false, 8>)
-             : (multi ? (const void *)fused_decode_kernel<false, true, 8>
-                      : (const void *)fused_decode_kernel<false, false, 8>);
+  // Weight tiles serve single-token launches, where they measured faster
+  // than per-thread loads (C0 47.7 vs 51.0 us per layer on B200).  With
+  // several tokens each CTA runs several short items and restarting the
+  // ring per item cost more than it saved (C2 4.28 vs 3.88 ms), so those
+  // launches keep per-thread loads.  The tile variants stage their inputs
+  // with 16-byte loads (the caller checked the alignment).
+  if (tiles) {
+    fn = a.int4 ? (const void *)fused_decode_kernel<true, false, 4, true>
+                : (const void *)fused_decode_kernel<true, false, 8, true>;
+  } else if (a.int4) {
+    fn = vec ? (multi ? (const void *)fused_decode_kernel<true, true, 4, false>
+                      : (const void *)fused_decode_kernel<true, false, 4, false>)
+             : (multi ? (const void *)fused_decode_kernel<false, true, 4, false>
+                      : (const void *)fused_decode_kernel<false, false, 4, false>);
+  } else {
+    fn = vec ? (multi ? (const void *)fused_decode_kernel<true, true, 8, false>
+                      : (const void *)fused_decode_kernel<true, false, 8, false>)
+             : (multi ? (const void *)fused_decode_kernel<false, true, 8, false>
+                      : (const void *)fused_decode_kernel<false, false, 8, false>);
+  }
   // The attribute and occupancy query run once per (device, variant, size).
   static thread_local int cached_dev = -1, cached_vec = -1, cached_grid = 0, cached_multi = -1,
-                          cached_q = -1;
+                          cached_q = -1, cached_tiles = -1;
   static thread_local size_t cached_smem = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev != cached_dev || vec != cached_vec || smem != cached_smem ||
-      (int)multi != cached_multi || a.int4 != cached_q) {
+      (int)multi != cached_multi || a.int4 != cached_q || (int)tiles != cached_tiles) {
     cudaError_t e =
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -525,6 +576,7 @@ cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint3
     cached_smem = smem;
     cached_multi = multi;
     cached_q = a.int4;
+    cached_tiles = tiles;
     cached_grid = std::min(per_sm, 2) * sm_count;
   }
   cudaError_t e = cudaMemsetAsync(bar, 0, sizeof(uint32_t), s);

@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "expert_tc.h"
+#include "tma_ptx.cuh"
 
 namespace moe {
 namespace tc {
@@ -44,56 +45,19 @@ constexpr int BK = 128;          // int8 K elements per stage (= 128 B swizzle r
 constexpr int UK = 32;           // K per tcgen05.mma kind::i8
 constexpr int kThreads = 192;
 constexpr uint32_t kTileBytes = BM * BK;  // 16 KB weight tile; a digit tile is BN * 128 B
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 // ---------------------------------------------------------------------------
-// PTX wrappers
+// PTX wrappers (mbarrier and TMA pieces live in tma_ptx.cuh)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t su32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(su32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: false on timeout, or (when abort_flag is given) as soon as
-// another role has aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          volatile int *abort_flag) {
-  const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
-    if (abort_flag && *abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) return false;
-  }
-  return true;
-}
+using tma::mbar_expect_tx;
+using tma::mbar_init;
+using tma::mbar_try;
+using tma::mbar_wait;
+using tma::su32;
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(su32(dst)),
-      "l"(map), "r"(su32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
+  tma::load_3d(dst, map, bar, c0, c1, c2);
 }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
@@ -477,9 +441,7 @@ __device__ __forceinline__ bool epi_any(bool v) {
   return r != 0;
 }
 
-__device__ __forceinline__ void mbar_arrive_plain(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
-}
+__device__ __forceinline__ void mbar_arrive_plain(uint64_t *bar) { tma::mbar_arrive(bar); }
 
 __device__ __forceinline__ void psetup(PPipe &pp, int stages, uint32_t ncols) {
   if (threadIdx.x == 0) {

@@ -111,6 +111,10 @@ struct FusedLayer {
   int prefetch_ok;    // expert bases 16-byte aligned, H and I multiples of 16
   const float *norm_w;  // stacks: gain [H] of the RMSNorm before this layer, null = 1
   int int4;             // INT4 experts: rows of n/2 bytes, two signed nibbles per byte
+  // Device array of two 128-byte CUtensorMaps over the packed expert weights
+  // (gate/up rows: 128 B x 32-row boxes; down rows: 128 B x 64-row boxes,
+  // 128-byte swizzle), or null: the decode GEMV then loads weights per thread.
+  const void *tmaps;
 };
 
 struct FusedArgs {
@@ -135,6 +139,7 @@ struct FusedArgs {
   uint32_t *status;
   int router_async;          // routers of every layer are 16-byte aligned f32 rows
   int int4;                  // every layer of the launch has INT4 experts
+  int tiles;                 // every layer has weight-tile maps; 16-byte aligned inputs
   unsigned long long *phase_ts;  // optional [5] phase timestamps (profiling)
   // streaming decode (decode_stream.cu) only
   uint32_t *ctr;             // counter set of this launch [kStreamCtrWords]

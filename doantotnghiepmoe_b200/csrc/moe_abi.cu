@@ -303,9 +303,12 @@ struct LayerSlot {
   // tensor-core path: only for the packed layout (one 3D tensor map per GEMM)
   bool tc_ok = false;
   CUtensorMap map_gu{}, map_dn{};
+  // decode weight-tile maps (FusedLayer::tmaps, two maps of 128 bytes), device copy
+  void *d_tmaps = nullptr;
   // device copies made by moe_load_layer (owned by the handle)
   void *own_w = nullptr, *own_s = nullptr, *own_r = nullptr, *own_n = nullptr;
 };
+static_assert(sizeof(CUtensorMap) == 128, "FusedLayer::tmaps holds 128-byte maps");
 }  // namespace
 
 namespace {
@@ -485,6 +488,7 @@ void free_handle(moe_handle *h) {
   for (auto &l : h->layers) {
     cudaFree(l.d_wptr);
     cudaFree(l.d_sptr);
+    cudaFree(l.d_tmaps);
     cudaFree(l.own_w);
     cudaFree(l.own_s);
     cudaFree(l.own_r);
@@ -807,6 +811,7 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
     f.ids_out = d_ids;
     f.gates_out = d_gates;
     f.int4 = L.int4;
+    f.tiles = h->flayers[layer].tmaps != nullptr && ((uintptr_t)d_h & 15) == 0;
     if (!d_ids || !d_gates) f.ids_out = nullptr;
     const int vec = h->layer_vec[layer] && ((uintptr_t)d_h & 15) == 0;
     f.router_async = h->layer_async[layer] && ((uintptr_t)d_h & 15) == 0;
@@ -1057,6 +1062,23 @@ extern "C" moe_status moe_set_layer_q(moe_handle *h, int layer, const void *cons
   // bulk L2 prefetches need 16-byte aligned rows
   F.prefetch_ok = align16 && (H / (int4 ? 2 : 1)) % 16 == 0 && (I / (int4 ? 2 : 1)) % 16 == 0 &&
                   (!int4 || (H % 32 == 0 && I % 32 == 0));
+  // Decode weight tiles: TMA boxes of 128 bytes x 32 (gate/up) or 64 (down)
+  // rows over the packed layout; rows of whole 32-element chunks.
+  // MOE_DECODE_TILES=0 keeps the per-thread weight loads.
+  F.tmaps = nullptr;
+  const size_t hb = int4 ? H / 2 : H, ib = int4 ? I / 2 : I;
+  const char *tiles_env = getenv("MOE_DECODE_TILES");
+  if (packed && align16 && H % 32 == 0 && I % 32 == 0 && hb >= 128 && ib >= 128 && H >= 64 &&
+      !(tiles_env && tiles_env[0] == '0')) {
+    CUtensorMap m[2];
+    if (tc::encode_map3d(&m[0], wb, hb, 2 * I, E, hb, wbytes, 32) &&
+        tc::encode_map3d(&m[1], wb + 2 * I * hb, ib, H, E, ib, wbytes, 64)) {
+      if (!L.d_tmaps && cudaMalloc(&L.d_tmaps, sizeof m) != cudaSuccess) return MOE_ERR_NOMEM;
+      const cudaError_t em = cudaMemcpy(L.d_tmaps, m, sizeof m, cudaMemcpyHostToDevice);
+      if (em != cudaSuccess) return cuda_fail(h, em, "set_layer");
+      F.tmaps = L.d_tmaps;
+    }
+  }
   h->layer_vec[layer] = vec;
   h->layer_async[layer] = router_dtype == MOE_ROUTER_F32 && ((uintptr_t)d_router & 15) == 0 &&
                           H % 4 == 0;
@@ -1405,6 +1427,9 @@ moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, fl
     f.n_layers = n_layers;
     f.stacked = 1;
     f.int4 = quant;
+    f.tiles = 1;
+    for (int l = first_layer; l < first_layer + n_layers; ++l)
+      f.tiles = f.tiles && h->flayers[l].tmaps != nullptr;
     f.layers = h->d_flayers + first_layer;
     f.out = d_x;
     f.hbuf = h->hbuf;
