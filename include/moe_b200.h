@@ -136,7 +136,12 @@ moe_status moe_set_path(moe_handle *h, int path);
 /* Register one layer's weights by borrowing device pointers (the pool owns
  * them, as with GpuExpertWeights).  d_weights[e] -> 3*I*H int8
  * [gate I*H | up I*H | down H*I] (src/int8_expert.rs:90-97), d_scales[e] ->
- * 2*I+H f32 [gate | up | down]; d_router -> [E,H] in router_dtype. */
+ * 2*I+H f32 [gate | up | down]; d_router -> [E,H] in router_dtype.
+ * When the experts form one packed allocation (expert e at d_weights[0] +
+ * e*3*I*H), the handle builds the layer's TMA tensor maps (a 256-byte device
+ * buffer per slot): the tensor-core path and the batch-1 decode weight-tile
+ * ring need them.  MOE_DECODE_TILES=0 in the environment at this call keeps
+ * batch-1 decode on per-thread weight loads (bit-identical results). */
 moe_status moe_set_layer(moe_handle *h, int layer, const void *const *d_weights,
                          const void *const *d_scales, const void *d_router, int router_dtype);
 
