@@ -21,7 +21,12 @@ from doantotnghiepmoe_b200 import _lib
 from tests.helpers import write_safetensors
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
-FIXTURES = "/root/reference/tests/fixtures"
+# the reference checkout: MOE_REFERENCE_ROOT, or a `reference` directory
+# beside this repository (present only where the reference is mounted)
+_REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+FIXTURES = os.path.join(os.environ.get("MOE_REFERENCE_ROOT",
+                                       os.path.join(os.path.dirname(_REPO), "reference")),
+                        "tests", "fixtures")
 
 
 def test_round_trip_all_dtypes_two_shards(tmp_path):
