@@ -265,10 +265,11 @@ __device__ void build_tables(const FusedArgs &a, Tables &tb) {
   }
 }
 
-// Weight loads stream in register batches of kDecodePF chunk-steps, two in
-// flight.  Deeper batches did not help: on B200 the phases are bound by
-// the grid barriers (every CTA waits for the slowest item), not by the
-// per-thread load chain -- INT4 (half the bytes) runs at INT8 speed, and an
+// Per-thread weight loads stream in register batches of kDecodePF
+// chunk-steps, two in flight.  Deeper batches did not help: on B200 a
+// phase is bound by the exact FMA chains' issue rate (about 0.7 us per four
+// chunk-steps, with or without the weights in L2) and by the grid barriers,
+// not by the loads -- INT4 (half the bytes) runs at INT8 speed, and an
 // 8-deep INT4 batch made the multi-route variant slower.
 constexpr int kDecodePF = 4;
 constexpr int kGURowsItem = kGURowsPerWarp * (kFT / 32);  // 32
