@@ -89,28 +89,33 @@ __device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// R: router logits for task tiles of kRTT tokens x kRTE experts, then the
-// last-arriving CTA of each token runs its selection.
+// R: router logits for task tiles of up to kRTT tokens x RE experts, then
+// the last-arriving CTA of each token runs its selection.  RE = kRTE when
+// that gives every CTA work; with fewer tasks than half the grid (small T)
+// RE = 1, which spreads the router rows over 4x more CTAs and shortens each
+// task's staging and dot.
 __device__ void router_phase(const FusedArgs &a, const FusedLayer &L, const float *hin,
                              float *stage, Tables &tb, SelectScratch *sel) {
   const int T = a.T, E = a.E, H = a.H, tid = threadIdx.x;
   const int TT = min(T, kRTT);
-  const int ntt = (T + TT - 1) / TT, nte = (E + kRTE - 1) / kRTE;
+  const int ntt = (T + TT - 1) / TT;
+  const int RE = ntt * ((E + kRTE - 1) / kRTE) * 2 < (int)gridDim.x ? 1 : kRTE;
+  const int nte = (E + RE - 1) / RE;
   const int tasks = ntt * nte;
   const int full = H / 8;
   // Router::select_top_k (src/router.rs:59-62) uses a plain sequential dot
   const bool seq = a.route_mode == kRouteTopkSoftmax && L.router_dtype == kRouterF32;
   for (int task = blockIdx.x; task < tasks; task += gridDim.x) {
-    const int t0 = (task / nte) * TT, e0 = (task % nte) * kRTE;
+    const int t0 = (task / nte) * TT, e0 = (task % nte) * RE;
     const int nt = min(TT, T - t0);
-    // stage rows: [0, TT) tokens, [TT, TT + kRTE) experts
-    const int total = (TT + kRTE) * H;
+    // stage rows: [0, TT) tokens, [TT, TT + RE) experts
+    const int total = (TT + RE) * H;
     bool bad = false;
     if (a.router_async) {
       // 16-byte cp.async copies, all issued before the single wait: one
       // memory round trip for the whole task.
       const int q = H / 4;
-      for (int i = tid; i < (TT + kRTE) * q; i += kFT) {
+      for (int i = tid; i < (TT + RE) * q; i += kFT) {
         const int r = i / q, c = (i % q) * 4;
         float *dst = stage + (size_t)r * H + c;
         const float *src = nullptr;
@@ -161,9 +166,14 @@ __device__ void router_phase(const FusedArgs &a, const FusedLayer &L, const floa
     }
     if (bad) set_status(a.status, kStatusNonFinite);
     __syncthreads();
-    if (tid < 8 * TT * kRTE) {
+    // 8 lanes per (token, expert) pair.  The lane fold below is a warp
+    // shuffle, so whole warps enter: lanes past the last pair compute on row
+    // 0 and write nothing (8 * TT * RE is not a multiple of 32 when RE = 1).
+    const int npairs = TT * RE;
+    if (tid < ((8 * npairs + 31) & ~31)) {
       const int lane = tid & 7, pair = tid >> 3;
-      const int ti = pair / kRTE, ei = pair % kRTE;
+      const bool live = pair < npairs;
+      const int ti = live ? pair / RE : 0, ei = live ? pair % RE : 0;
       const float *hs = stage + (size_t)ti * H;
       const float *w = stage + (size_t)(TT + ei) * H;
       float logit;
@@ -185,7 +195,7 @@ __device__ void router_phase(const FusedArgs &a, const FusedLayer &L, const floa
         logit = s;
       }
       const int t = t0 + ti, e = e0 + ei;
-      if (lane == 0 && ti < nt && e < E) {
+      if (live && lane == 0 && ti < nt && e < E) {
         a.logits[(size_t)t * E + e] = logit;
         if (!is_finite_f(logit)) set_status(a.status, kStatusNonFinite);
       }
@@ -223,17 +233,32 @@ __device__ void build_tables(const FusedArgs &a, Tables &tb) {
     if (e < (uint32_t)E) atomicAdd(&tb.run[e], 1);
   }
   __syncthreads();
-  if (tid == 0) {
+  if (warp == 0) {
+    // exclusive prefix of the counts and the ascending list of active
+    // experts, 32 experts per round
     int acc = 0, na = 0;
-    for (int e = 0; e < E; ++e) {
-      const int c = tb.run[e];
-      tb.seg_off[e] = acc;
-      tb.run[e] = acc;
-      if (c > 0) tb.active[na++] = e;
-      acc += c;
+    for (int base = 0; base < E; base += 32) {
+      const int e = base + lane;
+      const int c = e < E ? tb.run[e] : 0;
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += v;
+      }
+      const unsigned act = __ballot_sync(0xffffffffu, c > 0);
+      if (e < E) {
+        tb.seg_off[e] = acc + inc - c;
+        tb.run[e] = acc + inc - c;
+        if (c > 0) tb.active[na + __popc(act & ((1u << lane) - 1u))] = e;
+      }
+      acc += __shfl_sync(0xffffffffu, inc, 31);
+      na += __popc(act);
     }
-    tb.seg_off[E] = acc;
-    tb.n_active = na;
+    if (lane == 0) {
+      tb.seg_off[E] = acc;
+      tb.n_active = na;
+    }
   }
   __syncthreads();
   for (int base = 0; base < R; base += kFT) {
