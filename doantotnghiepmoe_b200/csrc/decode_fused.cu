@@ -4,14 +4,17 @@
 // kernels (route_core.cuh, gemv_core.cuh), so results stay bit-identical to
 // the CPU path; what changes is scheduling:
 //
-//   R  router logits, tasks of (<= 4 tokens x 4 experts) over all CTAs; the
-//      CTA that completes the last task of a token runs its softmax/top-k
-//      (per-token arrival counter, no barrier);
+//   R  router logits, tasks of (<= 4 tokens x 4 experts, or x 1 expert when
+//      tasks are scarce) over all CTAs; the CTA that completes the last task
+//      of a token runs its softmax/top-k (per-token arrival counter, no
+//      barrier);
 //   -- grid barrier --
 //   P  every CTA rebuilds the by-expert permutation in shared memory from the
 //      routing (small: T*K <= 1024 routes), then issues bulk L2 prefetches for
 //      the weight rows of all its gate/up and down items so HBM streams from
 //      here on;
+//   (single-token launches stream G and D weights through the TMA tile ring
+//   of gemv_tiles.cuh; larger ones load them per thread)
 //   G  gate/up GEMV items (expert segment x 32 rows) -> activations;
 //   -- grid barrier --
 //   D  down GEMV items (expert segment x 64 rows) -> gate-weighted
