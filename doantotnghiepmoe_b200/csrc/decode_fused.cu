@@ -324,6 +324,8 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
   const bool all_up_front = (size_t)nseg * 3 * I * hb <= ((size_t)64 << 20);
   const char *map_gu = static_cast<const char *>(L.tmaps);
   const char *map_dn = map_gu + kTensorMapBytes;
+  // Scale slices go with their weight blocks when whole 16-byte runs
+  // (full 32- or 64-row items of 16-byte aligned scale vectors).
   auto pf_gu = [&](int item) {
     if (threadIdx.x != 0 || !L.prefetch_ok || item >= nseg * nb_gu) return;
     const int e = tb.active[item / nb_gu], row0 = (item % nb_gu) * kGURowsItem;
@@ -331,13 +333,29 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
     const int8_t *W = L.w_ptr[e];
     prefetch_l2(W + (size_t)row0 * hb, (uint32_t)(rows * hb));
     prefetch_l2(W + (size_t)(I + row0) * hb, (uint32_t)(rows * hb));
+    const float *S = L.s_ptr[e];
+    if (rows == kGURowsItem && I % 4 == 0 && ((uintptr_t)S & 15) == 0) {
+      prefetch_l2(S + row0, kGURowsItem * sizeof(float));
+      prefetch_l2(S + I + row0, kGURowsItem * sizeof(float));
+    }
   };
   auto pf_dn = [&](int item) {
     if (threadIdx.x != 0 || !L.prefetch_ok || item >= nseg * nb_dn) return;
     const int e = tb.active[item / nb_dn], row0 = (item % nb_dn) * kDNRowsItem;
     const int rows = min(kDNRowsItem, H - row0);
     prefetch_l2(L.w_ptr[e] + 2 * (size_t)I * hb + (size_t)row0 * ib, (uint32_t)(rows * ib));
+    const float *S = L.s_ptr[e];
+    if (rows == kDNRowsItem && I % 2 == 0 && ((uintptr_t)S & 15) == 0)
+      prefetch_l2(S + 2 * I + row0, kDNRowsItem * sizeof(float));
   };
+  // The tile ring overlaps the router's staging rows: every thread orders
+  // its generic-proxy writes there before the ring's TMA writes (thread 0
+  // issues them after the barrier).  Within the expert phases only TMA
+  // writes the ring.
+  if constexpr (kTiles) {
+    tma::fence_proxy_async_smem();
+    __syncthreads();
+  }
   if (all_up_front) {
     for (int item = blockIdx.x; item < nseg * nb_gu; item += G) pf_gu(item);
     for (int item = blockIdx.x; item < nseg * nb_dn; item += G) pf_dn(item);
@@ -486,6 +504,13 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
   }
   for (int l = 0; l < a.n_layers; ++l) {
     const FusedLayer L = a.layers[l];
+    // the tile maps' descriptors are fetched while the router runs
+    if (kTiles && threadIdx.x == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(L.tmaps) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(static_cast<const char *>(L.tmaps) +
+                                                   kTensorMapBytes)
+                   : "memory");
+    }
     router_phase(a, L, hin, stage, tb, sel);
     ++nbar;
     if (!grid_sync(a.bar, nbar * G, a.status)) return;

@@ -16,6 +16,10 @@
 // stored at unit u ^ (r & 7)); each warp's lanes are assigned to rows so that
 // its weight reads from a stage hit every shared-memory bank equally.
 //
+// The caller orders earlier generic-proxy writes to the ring's memory (the
+// router's staging rows) with one proxy fence per layer; within the expert
+// phases only TMA writes the ring.
+//
 // Pipeline (one pass = one token group of one item): thread 0 issues the
 // pass's first kTileStages stages, each counted on its slot's mbarrier
 // (transaction bytes); all threads wait on the slot, run the stage's
@@ -174,7 +178,6 @@ __device__ __forceinline__ bool gate_up_tile_item(TileRing &rg, const void *map,
   auto issue = [&](int s, uint32_t u) { issue_gu(rg, map, e, row0, I, s, u); };
   for (int g0 = r0; g0 < r1; g0 += TG) {
     const int ng = min(TG, r1 - g0);
-    tma::fence_proxy_async_smem();
     __syncthreads();
     if (threadIdx.x == 0) tile_prologue(rg, nst, issue);
     stage_rows<true>(xs, x, r_token, g0, ng, H);
@@ -223,7 +226,6 @@ __device__ __forceinline__ bool down_tile_item(TileRing &rg, const void *map, in
   auto issue = [&](int s, uint32_t u) { issue_dn(rg, map, e, row0, s, u); };
   for (int g0 = r0; g0 < r1; g0 += TG) {
     const int ng = min(TG, r1 - g0);
-    tma::fence_proxy_async_smem();
     __syncthreads();
     if (threadIdx.x == 0) tile_prologue(rg, nst, issue);
     stage_rows<true>(xs, act, nullptr, g0, ng, I);
