@@ -1073,10 +1073,16 @@ extern "C" moe_status moe_set_layer_q(moe_handle *h, int layer, const void *cons
     CUtensorMap m[2];
     if (tc::encode_map3d(&m[0], wb, hb, 2 * I, E, hb, wbytes, 32) &&
         tc::encode_map3d(&m[1], wb + 2 * I * hb, ib, H, E, ib, wbytes, 64)) {
-      if (!L.d_tmaps && cudaMalloc(&L.d_tmaps, sizeof m) != cudaSuccess) return MOE_ERR_NOMEM;
-      const cudaError_t em = cudaMemcpy(L.d_tmaps, m, sizeof m, cudaMemcpyHostToDevice);
-      if (em != cudaSuccess) return cuda_fail(h, em, "set_layer");
-      F.tmaps = L.d_tmaps;
+      // the maps are an optimisation: without room for them the layer keeps
+      // per-thread weight loads
+      if (L.d_tmaps || cudaMalloc(&L.d_tmaps, sizeof m) == cudaSuccess) {
+        const cudaError_t em = cudaMemcpy(L.d_tmaps, m, sizeof m, cudaMemcpyHostToDevice);
+        if (em != cudaSuccess) return cuda_fail(h, em, "set_layer");
+        F.tmaps = L.d_tmaps;
+      } else {
+        L.d_tmaps = nullptr;
+        cudaGetLastError();  // clear the (non-sticky) allocation error
+      }
     }
   }
   h->layer_vec[layer] = vec;
