@@ -141,25 +141,10 @@ struct FusedArgs {
   int int4;                  // every layer of the launch has INT4 experts
   int tiles;                 // every layer has weight-tile maps; 16-byte aligned inputs
   unsigned long long *phase_ts;  // optional [5] phase timestamps (profiling)
-  // streaming decode (decode_stream.cu) only
-  uint32_t *ctr;             // counter set of this launch [kStreamCtrWords]
-  uint32_t *ctr_next;        // the other set, zeroed by this launch for the next
-  int rtt, rte;              // router task tile (set by the launcher)
-  int stream_ns, stream_xbytes;  // ring slots, staged-input bytes (set by the launcher)
 };
 bool fused_decode_supported(int T, int H, int I, int E, int K);
 cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint32_t *bar,
                                 cudaStream_t s);
-
-// Streaming decode (decode_stream.cu): same contract as the fused decode
-// kernel; needs 16-byte aligned expert bases, H and I multiples of 32, f32
-// inputs 16-byte aligned.  Two counter sets of kStreamCtrWords words each,
-// zero before the first launch; launches alternate between them.
-constexpr int kStreamCtrWords = 32 + kFusedMaxRoutes + kFusedMaxH / 64;
-constexpr int kStreamMaxT = 256;
-bool stream_decode_supported(int T, int H, int I, int E, int K);
-cudaError_t launch_stream_decode(const FusedArgs &a, int sm_count, cudaStream_t s);
-const char *stream_decode_diag();  // launch configuration of the last attribute query
 
 // Expert parallelism (ep.cu): one route on the wire = two int8 digit planes
 // of its token row + {s1, s2, gate, destination-local expert id}.

@@ -4,31 +4,18 @@
 // pointers (GpuExpertWeights, src/gpu.rs:1552-1566); the handle owns its
 // device scratch and serialises calls with a mutex (src/gpu_expert.rs:241-261).
 #include <dlfcn.h>
-#include <nccl.h>
 
-#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
-#include <cstring>
-#include <mutex>
-#include <string>
-#include <vector>
 
-#include "../../include/moe_b200.h"
-#include "common.cuh"
-#include "expert_tc.h"
-#include "kernels.h"
 #include "ckpt.h"
+#include "handle.h"
 
 using namespace moe;
 
-namespace {
-// Prefill-sized calls (T >= this) take the tensor-core path under MOE_PATH_AUTO.
-constexpr int kTcMinTokens = 128;
-}  // namespace
-
-namespace {
+namespace moe {
+namespace host {
 
 void set_err(std::string &dst, const char *fmt, ...) {
   char buf[512];
@@ -45,25 +32,32 @@ int sm_count_of(int device) {
   return n;
 }
 
-template <typename T>
-cudaError_t dalloc(T **p, size_t count) {
-  return cudaMalloc(reinterpret_cast<void **>(p), std::max<size_t>(count, 1) * sizeof(T));
+const NcclApi &nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) return;
+    auto sym = [&](const char *n) { return dlsym(lib, n); };
+    api.get_unique_id = (decltype(api.get_unique_id))sym("ncclGetUniqueId");
+    api.comm_init_rank = (decltype(api.comm_init_rank))sym("ncclCommInitRank");
+    api.comm_destroy = (decltype(api.comm_destroy))sym("ncclCommDestroy");
+    api.send = (decltype(api.send))sym("ncclSend");
+    api.recv = (decltype(api.recv))sym("ncclRecv");
+    api.group_start = (decltype(api.group_start))sym("ncclGroupStart");
+    api.group_end = (decltype(api.group_end))sym("ncclGroupEnd");
+    api.error_string = (decltype(api.error_string))sym("ncclGetErrorString");
+    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.send &&
+             api.recv && api.group_start && api.group_end && api.error_string;
+  });
+  return api;
 }
 
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    cudaGetDevice(&prev);
-    if (prev != dev) cudaSetDevice(dev);
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-  }
-};
+}  // namespace host
+}  // namespace moe
 
-}  // namespace
+using namespace moe::host;
 
 // ---------------------------------------------------------------------------
 // GpuExpertKernels drop-in
@@ -254,261 +248,12 @@ extern "C" moe_status moe_expert_forward(moe_expert_kernels *k, const void *cons
 // ---------------------------------------------------------------------------
 // MoE layer handle
 // ---------------------------------------------------------------------------
-namespace {
-// CUDA-event bracketing of kernel launches (moe_profile_*).
-struct Profiler {
-  bool on = false;
-  struct Rec {
-    const char *name;
-    cudaEvent_t a, b;
-  };
-  std::vector<cudaEvent_t> pool;
-  size_t used = 0;
-  std::vector<Rec> recs;
-  cudaEvent_t take() {
-    if (used == pool.size()) {
-      cudaEvent_t e;
-      if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
-      pool.push_back(e);
-    }
-    return pool[used++];
-  }
-  // Returns the start event (or null when off / out of events).
-  cudaEvent_t begin(cudaStream_t s) {
-    if (!on || recs.size() >= 1 << 16) return nullptr;
-    cudaEvent_t a = take();
-    if (a) cudaEventRecord(a, s);
-    return a;
-  }
-  void end(const char *name, cudaEvent_t a, cudaStream_t s) {
-    if (!a) return;
-    cudaEvent_t b = take();
-    if (!b) return;
-    cudaEventRecord(b, s);
-    recs.push_back({name, a, b});
-  }
-  ~Profiler() {
-    for (auto e : pool) cudaEventDestroy(e);
-  }
-};
-
-struct LayerSlot {
-  bool set = false;
-  const int8_t **d_wptr = nullptr;  // device array [E]
-  const float **d_sptr = nullptr;   // device array [E]
-  const void *router = nullptr;
-  int router_dtype = MOE_ROUTER_F32;
-  int vec = 0;  // all expert bases 8-byte aligned -> vector weight loads
-  int int4 = 0;  // INT4 experts (src/int8_expert.rs:473-649): GEMV paths only
-  // tensor-core path: only for the packed layout (one 3D tensor map per GEMM)
-  bool tc_ok = false;
-  CUtensorMap map_gu{}, map_dn{};
-  // decode weight-tile maps (FusedLayer::tmaps, two maps of 128 bytes), device copy
-  void *d_tmaps = nullptr;
-  // device copies made by moe_load_layer (owned by the handle)
-  void *own_w = nullptr, *own_s = nullptr, *own_r = nullptr, *own_n = nullptr;
-};
-static_assert(sizeof(CUtensorMap) == 128, "FusedLayer::tmaps holds 128-byte maps");
-}  // namespace
-
-namespace {
-// NCCL, resolved at run time: the process normally has it loaded already
-// (PyTorch's copy); otherwise the system libnccl.so.2 is opened.
-struct NcclApi {
-  bool ok = false;
-  ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
-  ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
-  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
-  ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t,
-                       cudaStream_t) = nullptr;
-  ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
-  ncclResult_t (*group_start)() = nullptr;
-  ncclResult_t (*group_end)() = nullptr;
-  const char *(*error_string)(ncclResult_t) = nullptr;
-};
-
-const NcclApi &nccl() {
-  static NcclApi api;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
-    if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-    if (!lib) return;
-    auto sym = [&](const char *n) { return dlsym(lib, n); };
-    api.get_unique_id = (decltype(api.get_unique_id))sym("ncclGetUniqueId");
-    api.comm_init_rank = (decltype(api.comm_init_rank))sym("ncclCommInitRank");
-    api.comm_destroy = (decltype(api.comm_destroy))sym("ncclCommDestroy");
-    api.send = (decltype(api.send))sym("ncclSend");
-    api.recv = (decltype(api.recv))sym("ncclRecv");
-    api.group_start = (decltype(api.group_start))sym("ncclGroupStart");
-    api.group_end = (decltype(api.group_end))sym("ncclGroupEnd");
-    api.error_string = (decltype(api.error_string))sym("ncclGetErrorString");
-    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.send &&
-             api.recv && api.group_start && api.group_end && api.error_string;
-  });
-  return api;
-}
-
-struct EpLayer {
-  bool set = false;
-  const float **d_sptr = nullptr;  // [E_local] local scale rows
-  CUtensorMap map_gu{}, map_dn{};  // over the packed local experts
-};
-
-struct EpState {
-  bool on = false;
-  int rank = 0, nranks = 1, E_local = 0;
-  ncclComm_t comm = nullptr;
-  int32_t *d_owner = nullptr, *d_dest_local = nullptr;  // [E]
-  std::vector<EpLayer> layers;
-  size_t r_local_cap = 0, r_recv_cap = 0;
-  int max_tiles = 0;
-  // dispatch side
-  uint32_t *dest = nullptr;
-  int32_t *seg_dest = nullptr, *act_dest = nullptr, *n_dest = nullptr, *stok = nullptr,
-          *sslot = nullptr, *spos = nullptr, *scount = nullptr, *rcount = nullptr;
-  float *sgate = nullptr, *ret = nullptr;
-  uint8_t *send = nullptr, *recv = nullptr;
-  int32_t *h_counts = nullptr;  // pinned [2 * nranks]
-  // expert side
-  uint32_t *ids_l = nullptr;
-  float *gates_l = nullptr, *rgate_l = nullptr, *ybuf = nullptr, *act = nullptr;
-  int32_t *seg_l = nullptr, *active_l = nullptr, *n_active_l = nullptr, *rtok_l = nullptr,
-          *rslot_l = nullptr, *rpos_l = nullptr;
-  int8_t *xq = nullptr, *aq = nullptr;
-  float *xs1 = nullptr, *xs2 = nullptr, *as1 = nullptr, *as2 = nullptr;
-  uint32_t *act_amax = nullptr;
-  int32_t *tile_expert = nullptr, *tile_row0 = nullptr, *tile_rows = nullptr, *n_tiles = nullptr;
-  // the down GEMM's tile list when its width differs from the gate/up one
-  int32_t *dtile_expert = nullptr, *dtile_row0 = nullptr, *dtile_rows = nullptr,
-          *n_dtiles = nullptr;
-  CUtensorMap map_x64{}, map_x128{}, map_a64{}, map_a128{};
-  std::vector<void *> allocs;
-  // device-driven exchange over NVLink peer memory (CUDA IPC)
-  bool p2p = false;
-  std::string transport_note;       // why the collective-library path is in use
-  void *region = nullptr;           // this rank's peer-visible region
-  std::vector<void *> peer_maps;    // opened peer regions (closed at finalize)
-  EpP2P P{};
-  uint32_t *epoch = nullptr;        // device: calls so far (flag values)
-  uint32_t *done = nullptr;         // dispatch completion counter (monotonic)
-  int32_t *n_recv = nullptr;        // device count of received routes
-  int dispatch_grid = 0;
-};
-}  // namespace
-
-struct moe_handle {
-  int device = 0;
-  moe_dims d{};
-  int sm_count = 148;
-  cudaStream_t own_stream = nullptr, stream = nullptr;
-  int route_mode = MOE_ROUTE_SOFTMAX_TOPK;
-  int path = MOE_PATH_AUTO;
-  std::mutex mu;
-  std::string err;
-  std::vector<LayerSlot> layers;
-  // scratch
-  float *logits = nullptr, *gates = nullptr, *r_gate = nullptr, *act = nullptr,
-        *contrib = nullptr, *hbuf = nullptr, *io_in = nullptr, *io_out = nullptr,
-        *io_resid = nullptr;
-  uint32_t *ids = nullptr, *status = nullptr;
-  int32_t *seg_off = nullptr, *active = nullptr, *n_active = nullptr, *r_token = nullptr,
-          *r_slot = nullptr, *r_pos = nullptr;
-  float *h_pin_in = nullptr, *h_pin_out = nullptr;
-  uint32_t *h_pin_status = nullptr;
-  float *h_pin_meta = nullptr;  // [2][max_tokens * top_k]: ids, gates
-  cudaEvent_t stage_ev[16] = {};  // chunked staging of pageable host outputs
-  int last_launches = 0;
-  Profiler prof;
-  // tensor-core path scratch
-  bool tc_ok = false;
-  int max_tiles = 0;
-  int8_t *xq = nullptr, *aq = nullptr;  // [2][R][H], [2][R][I] digit planes
-  float *xs1 = nullptr, *xs2 = nullptr, *as1 = nullptr, *as2 = nullptr;
-  uint32_t *act_amax = nullptr;
-  int32_t *tile_expert = nullptr, *tile_row0 = nullptr, *tile_rows = nullptr, *n_tiles = nullptr;
-  // the down GEMM's tile list when its width differs from the gate/up one
-  int32_t *dtile_expert = nullptr, *dtile_row0 = nullptr, *dtile_rows = nullptr,
-          *n_dtiles = nullptr;
-  CUtensorMap map_x64{}, map_x128{}, map_a64{}, map_a128{};  // digit planes, box 64/128 rows
-  // fused decode
-  FusedLayer *d_flayers = nullptr;  // [num_layers]
-  std::vector<FusedLayer> flayers;
-  std::vector<int> layer_vec;
-  uint32_t *tok_cnt = nullptr, *fbar = nullptr;
-  uint32_t *sctr = nullptr;                // streaming decode: 2 counter sets
-  int32_t *perm_scratch = nullptr;         // multi-CTA permutation
-  size_t perm_scratch_words = 0;
-  uint32_t sctr_parity = 0;                // set used by the next launch
-  std::vector<int> layer_async;            // router rows are 16-byte aligned f32
-  unsigned long long *phase_ts = nullptr;  // [8] single-launch kernel phase stamps
-  bool phase_pending = false;
-  int phase_kind = 0;                      // 0: register-prefetch kernel, 1: streaming
-  // replayed launch sequences (see graphed())
-  struct GraphEntry {
-    uint64_t key[10];
-    cudaGraphExec_t exec;
-    int launches;
-    uint64_t last_use;
-  };
-  std::vector<GraphEntry> graphs;
-  uint64_t graph_clock = 0;
-  bool graphs_on = true;
-  EpState ep;
-};
-
-namespace {
-
-void free_ep(moe_handle *h) {
-  EpState &ep = h->ep;
-  for (void *m : ep.peer_maps) cudaIpcCloseMemHandle(m);
-  ep.peer_maps.clear();
-  if (ep.region) cudaFree(ep.region);
-  ep.region = nullptr;
-  ep.p2p = false;
-  if (ep.comm && nccl().ok) nccl().comm_destroy(ep.comm);
-  ep.comm = nullptr;
-  for (auto &l : ep.layers) cudaFree(l.d_sptr);
-  ep.layers.clear();
-  for (void *p : ep.allocs) cudaFree(p);
-  ep.allocs.clear();
-  cudaFreeHost(ep.h_counts);
-  ep.h_counts = nullptr;
-  ep.on = false;
-}
+namespace moe {
+namespace host {
 
 void drop_graphs(moe_handle *h) {
   for (auto &g : h->graphs) cudaGraphExecDestroy(g.exec);
   h->graphs.clear();
-}
-
-void free_handle(moe_handle *h) {
-  drop_graphs(h);
-  free_ep(h);
-  for (auto &l : h->layers) {
-    cudaFree(l.d_wptr);
-    cudaFree(l.d_sptr);
-    cudaFree(l.d_tmaps);
-    cudaFree(l.own_w);
-    cudaFree(l.own_s);
-    cudaFree(l.own_r);
-    cudaFree(l.own_n);
-  }
-  void *ptrs[] = {h->logits,  h->gates,     h->r_gate,    h->act,       h->contrib, h->hbuf,
-                  h->io_in,   h->io_out,    h->io_resid,  h->ids,       h->status,  h->seg_off,
-                  h->active,  h->n_active,  h->r_token,   h->r_slot,    h->r_pos,   h->xq,
-                  h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
-                  h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles, h->d_flayers,
-                  h->dtile_expert, h->dtile_row0, h->dtile_rows, h->n_dtiles,
-                  h->tok_cnt, h->fbar, h->phase_ts, h->sctr, h->perm_scratch};
-  for (void *p : ptrs) cudaFree(p);
-  cudaFreeHost(h->h_pin_in);
-  cudaFreeHost(h->h_pin_out);
-  cudaFreeHost(h->h_pin_status);
-  cudaFreeHost(h->h_pin_meta);
-  for (auto ev : h->stage_ev)
-    if (ev) cudaEventDestroy(ev);
-  if (h->own_stream) cudaStreamDestroy(h->own_stream);
 }
 
 cudaStream_t pick(moe_handle *h, void *stream) {
@@ -520,66 +265,12 @@ moe_status cuda_fail(moe_handle *h, cudaError_t e, const char *what) {
   return MOE_ERR_CUDA;
 }
 
-// Replay a call's launch sequence as a CUDA graph.  The sequence is captured
-// once per key (call kind, layer, token count, buffers, stream, path) and
-// replayed afterwards, which removes the host launch cost and most of the
-// gaps between the kernels.  Captures are only kept when every launch in the
-// sequence takes its sizes from device memory or from the key; the cache is
-// dropped whenever weights, path or routing mode change.  Profiling (events
-// between kernels) and a caller's own stream capture use direct launches.
-template <typename F>
-moe_status graphed(moe_handle *h, const uint64_t (&key)[10], cudaStream_t s, F &&launch_all) {
-  if (!h->graphs_on || h->prof.on) return launch_all();
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return launch_all();
-  }
-  for (auto &g : h->graphs) {
-    if (memcmp(g.key, key, sizeof key) != 0) continue;
-    g.last_use = ++h->graph_clock;
-    h->last_launches = g.launches;
-    const cudaError_t e = cudaGraphLaunch(g.exec, s);
-    return e == cudaSuccess ? MOE_OK : cuda_fail(h, e, "graph launch");
-  }
-  if (cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed) != cudaSuccess) {
-    cudaGetLastError();
-    return launch_all();
-  }
-  const moe_status st = launch_all();
-  cudaGraph_t graph = nullptr;
-  const cudaError_t ec = cudaStreamEndCapture(s, &graph);
-  cudaGraphExec_t exec = nullptr;
-  const bool ok = st == MOE_OK && ec == cudaSuccess && graph &&
-                  cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
-  if (graph) cudaGraphDestroy(graph);
-  if (!ok) {
-    cudaGetLastError();
-    if (st != MOE_OK) return st;
-    return launch_all();  // nothing ran during the failed capture
-  }
-  if (h->graphs.size() >= 32) {
-    auto old = std::min_element(h->graphs.begin(), h->graphs.end(),
-                                [](const auto &a, const auto &b) { return a.last_use < b.last_use; });
-    cudaGraphExecDestroy(old->exec);
-    h->graphs.erase(old);
-  }
-  moe_handle::GraphEntry g{};
-  memcpy(g.key, key, sizeof key);
-  g.exec = exec;
-  g.launches = h->last_launches;
-  g.last_use = ++h->graph_clock;
-  h->graphs.push_back(g);
-  const cudaError_t e = cudaGraphLaunch(exec, s);
-  return e == cudaSuccess ? MOE_OK : cuda_fail(h, e, "graph launch");
-}
-
 // Router + top-k + permutation for T tokens of `layer`.
 // bn_gu > 0: the permutation also writes the tensor-core tile list of the
 // gate/up GEMM, and (bn_dn > 0, != bn_gu) the down GEMM's.
 moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T, uint32_t *ids,
-                     float *gates, float *probs, cudaStream_t s, bool permute, int bn_gu = 0,
-                     int bn_dn = 0) {
+                     float *gates, float *probs, cudaStream_t s, bool permute, int bn_gu,
+                     int bn_dn) {
   RouteArgs ra{};
   ra.h = d_h;
   ra.router = L.router;
@@ -633,6 +324,40 @@ moe_status run_route(moe_handle *h, const LayerSlot &L, const float *d_h, int T,
   return MOE_OK;
 }
 
+}  // namespace host
+}  // namespace moe
+
+namespace {
+
+void free_handle(moe_handle *h) {
+  drop_graphs(h);
+  free_ep(h);
+  for (auto &l : h->layers) {
+    cudaFree(l.d_wptr);
+    cudaFree(l.d_sptr);
+    cudaFree(l.d_tmaps);
+    cudaFree(l.own_w);
+    cudaFree(l.own_s);
+    cudaFree(l.own_r);
+    cudaFree(l.own_n);
+  }
+  void *ptrs[] = {h->logits,  h->gates,     h->r_gate,    h->act,       h->contrib, h->hbuf,
+                  h->io_in,   h->io_out,    h->io_resid,  h->ids,       h->status,  h->seg_off,
+                  h->active,  h->n_active,  h->r_token,   h->r_slot,    h->r_pos,   h->xq,
+                  h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
+                  h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles, h->d_flayers,
+                  h->dtile_expert, h->dtile_row0, h->dtile_rows, h->n_dtiles,
+                  h->tok_cnt, h->fbar, h->phase_ts, h->perm_scratch};
+  for (void *p : ptrs) cudaFree(p);
+  cudaFreeHost(h->h_pin_in);
+  cudaFreeHost(h->h_pin_out);
+  cudaFreeHost(h->h_pin_status);
+  cudaFreeHost(h->h_pin_meta);
+  for (auto ev : h->stage_ev)
+    if (ev) cudaEventDestroy(ev);
+  if (h->own_stream) cudaStreamDestroy(h->own_stream);
+}
+
 moe_status check_layer(moe_handle *h, int layer, int T) {
   if (layer < 0 || layer >= (int)h->layers.size()) {
     set_err(h->err, "layer %d out of range [0, %d)", layer, (int)h->layers.size());
@@ -653,7 +378,7 @@ bool use_tensor_path(const moe_handle *h, const LayerSlot &L, int T, const float
   const bool avail = h->tc_ok && L.tc_ok && ((uintptr_t)d_h & 15) == 0;
   if (h->path == MOE_PATH_TENSOR) return avail;
   if (h->path == MOE_PATH_GEMV || h->path == MOE_PATH_GEMV_PHASED ||
-      h->path == MOE_PATH_GEMV_FUSED || h->path == MOE_PATH_GEMV_STREAM)
+      h->path == MOE_PATH_GEMV_FUSED)
     return false;
   return avail && T >= kTcMinTokens;
 }
@@ -664,18 +389,6 @@ bool use_fused(const moe_handle *h, int T) {
                                 h->d.top_k);
 }
 
-// The streaming decode kernel: every layer's experts 16-byte aligned (bulk
-// copies), f32 routers in 16-byte rows or bf16, aligned f32 activations.
-bool use_stream(const moe_handle *h, int T, int first_layer, int n_layers, const void *d_x) {
-  if (h->path != MOE_PATH_GEMV_STREAM) return false;
-  if (((uintptr_t)d_x & 15) != 0) return false;
-  if (!stream_decode_supported(T, h->d.hidden, h->d.intermediate, h->d.num_experts, h->d.top_k))
-    return false;
-  for (int l = first_layer; l < first_layer + n_layers; ++l)
-    if (!h->flayers[l].prefetch_ok || h->flayers[l].int4) return false;
-  return true;
-}
-
 // One weight format over layers [first, first + n) (the single-launch kernel
 // is compiled per format); -1 when they differ.
 int layers_quant(const moe_handle *h, int first, int n) {
@@ -683,17 +396,6 @@ int layers_quant(const moe_handle *h, int first, int n) {
   for (int l = first + 1; l < first + n; ++l)
     if (h->flayers[l].int4 != q) return -1;
   return q;
-}
-
-// Launch the streaming decode kernel with the handle's next counter set.
-cudaError_t launch_stream(moe_handle *h, FusedArgs f, cudaStream_t s) {
-  if (f.phase_ts) cudaMemsetAsync(f.phase_ts, 0, 16 * sizeof(unsigned long long), s);
-  f.ctr = h->sctr + (size_t)h->sctr_parity * kStreamCtrWords;
-  f.ctr_next = h->sctr + (size_t)(h->sctr_parity ^ 1u) * kStreamCtrWords;
-  const cudaError_t e = launch_stream_decode(f, h->sm_count, s);
-  if (e == cudaSuccess) h->sctr_parity ^= 1u;
-  else fprintf(stderr, "moe_b200: %s: %s\n", cudaGetErrorString(e), stream_decode_diag());
-  return e;
 }
 
 FusedArgs fused_args(moe_handle *h, int T) {
@@ -815,13 +517,9 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
     if (!d_ids || !d_gates) f.ids_out = nullptr;
     const int vec = h->layer_vec[layer] && ((uintptr_t)d_h & 15) == 0;
     f.router_async = h->layer_async[layer] && ((uintptr_t)d_h & 15) == 0;
-    const bool stream = use_stream(h, T, layer, 1, d_h) &&
-                        (!d_resid || ((uintptr_t)d_resid & 15) == 0);
-    h->phase_kind = stream ? 1 : 0;
     cudaEvent_t p0 = h->prof.begin(s);
-    cudaError_t e = stream ? launch_stream(h, f, s)
-                           : launch_fused_decode(f, vec, h->sm_count, h->fbar, s);
-    h->prof.end(stream ? "stream_decode" : "fused_decode", p0, s);
+    cudaError_t e = launch_fused_decode(f, vec, h->sm_count, h->fbar, s);
+    h->prof.end("fused_decode", p0, s);
     if (e != cudaSuccess) return cuda_fail(h, e, "fused decode launch");
     h->last_launches += 1;
     if (d_ids && !d_gates) cudaMemcpyAsync(d_ids, h->ids, (size_t)T * h->d.top_k * 4,
@@ -936,10 +634,8 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && dalloc(&h->tok_cnt, T) == cudaSuccess && dalloc(&h->fbar, 1) == cudaSuccess;
   ok = ok && cudaMemset(h->tok_cnt, 0, T * sizeof(uint32_t)) == cudaSuccess;
   ok = ok && dalloc(&h->phase_ts, 16) == cudaSuccess;
-  ok = ok && dalloc(&h->sctr, 2 * kStreamCtrWords) == cudaSuccess;
   h->perm_scratch_words = permute_scratch_words((int)(T * K), (int)E);
   ok = ok && dalloc(&h->perm_scratch, h->perm_scratch_words) == cudaSuccess;
-  ok = ok && cudaMemset(h->sctr, 0, 2 * kStreamCtrWords * sizeof(uint32_t)) == cudaSuccess;
   h->flayers.assign(d.num_layers, FusedLayer{});
   h->layer_vec.assign(d.num_layers, 0);
   h->layer_async.assign(d.num_layers, 0);
@@ -996,7 +692,7 @@ extern "C" moe_status moe_set_route_mode(moe_handle *h, int mode) {
 }
 
 extern "C" moe_status moe_set_path(moe_handle *h, int path) {
-  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_GEMV_STREAM) return MOE_ERR_INVALID;
+  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_GEMV_FUSED) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
   h->path = path;
   return MOE_OK;
@@ -1383,9 +1079,6 @@ extern "C" moe_status moe_layer_forward(moe_handle *h, int layer, const float *d
   DeviceGuard g(h->device);
   h->last_launches = 0;
   cudaStream_t s = pick(h, stream);
-  // the streaming decode kernel alternates counter sets from the host: direct launches
-  if (h->path == MOE_PATH_GEMV_STREAM)
-    return layer_forward_locked(h, layer, d_h, d_resid, d_out, T, d_ids, d_gates, s);
   const uint64_t key[10] = {1, (uint64_t)layer, (uint64_t)T, (uint64_t)d_h, (uint64_t)d_resid,
                             (uint64_t)d_out, (uint64_t)d_ids, (uint64_t)d_gates, (uint64_t)s,
                             (uint64_t)(h->path * 16 + h->route_mode)};
@@ -1410,8 +1103,6 @@ extern "C" moe_status moe_stack_forward(moe_handle *h, int first_layer, int n_la
   DeviceGuard g(h->device);
   cudaStream_t s = pick(h, stream);
   h->last_launches = 0;
-  if (h->path == MOE_PATH_GEMV_STREAM)
-    return stack_forward_locked(h, first_layer, n_layers, d_x, T, rms_eps, s);
   uint32_t eps_bits;
   memcpy(&eps_bits, &rms_eps, 4);
   const uint64_t key[10] = {2, (uint64_t)first_layer, (uint64_t)n_layers, (uint64_t)T,
@@ -1443,12 +1134,9 @@ moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, fl
     f.router_async = 1;
     for (int l = first_layer; l < first_layer + n_layers; ++l)
       f.router_async = f.router_async && h->layer_async[l];
-    const bool stream = use_stream(h, T, first_layer, n_layers, d_x);
-    h->phase_kind = stream ? 1 : 0;
     cudaEvent_t p0 = h->prof.begin(s);
-    cudaError_t e = stream ? launch_stream(h, f, s)
-                           : launch_fused_decode(f, vec_all ? 1 : 0, h->sm_count, h->fbar, s);
-    h->prof.end(stream ? "stream_decode" : "fused_decode", p0, s);
+    cudaError_t e = launch_fused_decode(f, vec_all ? 1 : 0, h->sm_count, h->fbar, s);
+    h->prof.end("fused_decode", p0, s);
     if (e != cudaSuccess) return cuda_fail(h, e, "fused decode launch");
     h->last_launches += 1;
     return MOE_OK;
@@ -1663,37 +1351,15 @@ extern "C" moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int 
     // last entry runs to the end of the launch)
     unsigned long long ts[16] = {};
     if (cudaMemcpy(ts, h->phase_ts, sizeof ts, cudaMemcpyDeviceToHost) == cudaSuccess) {
-      static const char *names_f[4] = {"fused:router", "fused:gate_up", "fused:down",
-                                       "fused:rest"};
-      static const char *names_s[6] = {"fused:route_task", "fused:route_wait", "fused:select",
-                                       "fused:gate_up",    "fused:down",       "fused:rest"};
-      const char *const *names = h->phase_kind ? names_s : names_f;
-      const int nph = h->phase_kind ? 6 : 4;
-      for (int i = 0; i < nph; ++i) {
+      static const char *names[4] = {"fused:router", "fused:gate_up", "fused:down",
+                                     "fused:rest"};
+      for (int i = 0; i < 4; ++i) {
         moe_kernel_time k{};
         snprintf(k.name, sizeof k.name, "%s", names[i]);
         k.launches = 1;
         k.total_ms = ts[i + 1] > ts[i] ? (float)((ts[i + 1] - ts[i]) * 1e-6) : 0.0f;
         acc.push_back(k);
       }
-      // selection alone (streaming kernel): stamp 7 follows the top-k
-      if (h->phase_kind && ts[7] > ts[2]) {
-        moe_kernel_time k{};
-        snprintf(k.name, sizeof k.name, "fused:select_topk");
-        k.launches = 1;
-        k.total_ms = (float)((ts[7] - ts[2]) * 1e-6);
-        acc.push_back(k);
-      }
-      // second layer of a stack (streaming kernel), stamps 8..13
-      if (h->phase_kind && ts[8] != 0)
-        for (int i = 0; i < 5; ++i) {
-          moe_kernel_time k{};
-          snprintf(k.name, sizeof k.name, "%s1", names[i]);
-          k.launches = 1;
-          k.total_ms =
-              ts[9 + i] > ts[8 + i] ? (float)((ts[9 + i] - ts[8 + i]) * 1e-6) : 0.0f;
-          acc.push_back(k);
-        }
     }
     h->phase_pending = false;
   }
@@ -1727,606 +1393,3 @@ extern "C" moe_status moe_synth_normal_host(uint64_t seed, uint32_t kind, uint32
   return MOE_OK;
 }
 
-// ---------------------------------------------------------------------------
-// Expert parallelism
-// ---------------------------------------------------------------------------
-namespace {
-template <typename T>
-bool ep_alloc(EpState &ep, T **p, size_t count) {
-  if (dalloc(p, count) != cudaSuccess) return false;
-  ep.allocs.push_back(*p);
-  return true;
-}
-
-moe_status nccl_fail(moe_handle *h, ncclResult_t r, const char *what) {
-  set_err(h->err, "%s: %s", what, nccl().error_string ? nccl().error_string(r) : "nccl");
-  return MOE_ERR_NCCL;
-}
-}  // namespace
-
-namespace {
-size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
-
-// Peer-memory transport: one region per rank holding everything peers write
-// (flags, count matrix, the expert-sorted receive side of the tensor-core
-// input, the [T, K, H] contribution buffer), shared through CUDA IPC handles
-// that are exchanged once over the communicator.  On any failure the
-// collective-library transport stays in use and the reason is kept.
-void ep_setup_p2p(moe_handle *h, size_t Tm) {
-  EpState &ep = h->ep;
-  const int N = ep.nranks, E = h->d.num_experts, H = h->d.hidden, K = h->d.top_k;
-  const char *env = getenv("MOE_EP_TRANSPORT");
-  if (env && strcmp(env, "nccl") == 0) {
-    ep.transport_note = "MOE_EP_TRANSPORT=nccl";
-    return;
-  }
-  if (N > kEpMaxRanks) {
-    ep.transport_note = "more ranks than the peer-memory transport supports";
-    return;
-  }
-  const size_t RR = ep.r_recv_cap;
-  EpP2P P{};
-  size_t off = 0;
-  P.off_flags = off;   off = align_up(off + 3 * kEpMaxRanks * 4, 1024);
-  P.off_counts = off;  off = align_up(off + (size_t)2 * N * E * 4, 1024);
-  P.off_xq = off;      P.plane = RR * H; off = align_up(off + 2 * RR * H, 1024);
-  P.off_s1 = off;      off = align_up(off + RR * 4, 1024);
-  P.off_s2 = off;      off = align_up(off + RR * 4, 1024);
-  P.off_gate = off;    off = align_up(off + RR * 4, 1024);
-  P.off_rank = off;    off = align_up(off + RR * 4, 1024);
-  P.off_tok = off;     off = align_up(off + RR * 4, 1024);
-  P.off_slot = off;    off = align_up(off + RR * 4, 1024);
-  P.off_amax = off;    off = align_up(off + RR * 4, 1024);
-  P.off_contrib = off; off = align_up(off + Tm * K * H * 4, 1024);
-  P.rank = ep.rank;
-  P.nranks = N;
-  void *region = nullptr;
-  if (cudaMalloc(&region, off) != cudaSuccess || cudaMemset(region, 0, off) != cudaSuccess) {
-    cudaGetLastError();
-    if (region) cudaFree(region);
-    ep.transport_note = "peer region allocation failed";
-    return;
-  }
-  cudaIpcMemHandle_t mine{};
-  if (cudaIpcGetMemHandle(&mine, region) != cudaSuccess) {
-    cudaGetLastError();
-    cudaFree(region);
-    ep.transport_note = "cudaIpcGetMemHandle failed";
-    return;
-  }
-  // exchange the handles: every rank sends its 64 bytes to every other rank
-  const size_t HB = sizeof(cudaIpcMemHandle_t);
-  uint8_t *dh = nullptr;
-  std::vector<uint8_t> all(N * HB);
-  bool ok = cudaMalloc(&dh, N * HB) == cudaSuccess &&
-            cudaMemcpy(dh + ep.rank * HB, &mine, HB, cudaMemcpyHostToDevice) == cudaSuccess;
-  cudaStream_t s = h->stream;
-  if (ok) {
-    const NcclApi &api = nccl();
-    ncclResult_t nr = api.group_start();
-    for (int q = 0; q < N && nr == ncclSuccess; ++q) {
-      if (q == ep.rank) continue;
-      nr = api.send(dh + ep.rank * HB, HB, ncclUint8, q, ep.comm, s);
-      if (nr == ncclSuccess) nr = api.recv(dh + q * HB, HB, ncclUint8, q, ep.comm, s);
-    }
-    const ncclResult_t ng = api.group_end();
-    ok = nr == ncclSuccess && ng == ncclSuccess && cudaStreamSynchronize(s) == cudaSuccess &&
-         cudaMemcpy(all.data(), dh, N * HB, cudaMemcpyDeviceToHost) == cudaSuccess;
-  }
-  if (dh) cudaFree(dh);
-  std::vector<void *> maps;
-  for (int q = 0; q < N && ok; ++q) {
-    if (q == ep.rank) {
-      P.base[q] = (uint8_t *)region;
-      continue;
-    }
-    cudaIpcMemHandle_t hq;
-    memcpy(&hq, all.data() + q * HB, HB);
-    void *ptr = nullptr;
-    if (cudaIpcOpenMemHandle(&ptr, hq, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-      cudaGetLastError();
-      ok = false;
-      break;
-    }
-    maps.push_back(ptr);
-    P.base[q] = (uint8_t *)ptr;
-  }
-  // the tensor-core input maps now point at the region's receive side
-  uint8_t *xq = (uint8_t *)region + P.off_xq;
-  ok = ok && tc::encode_map3d(&ep.map_x64, xq, H, RR, 2, H, RR * H, 64) &&
-       tc::encode_map3d(&ep.map_x128, xq, H, RR, 2, H, RR * H, 128) &&
-       ep_alloc(ep, &ep.done, 1) && ep_alloc(ep, &ep.n_recv, 1) &&
-       ep_alloc(ep, &ep.epoch, 1) && cudaMemset(ep.done, 0, 4) == cudaSuccess &&
-       cudaMemset(ep.epoch, 0, 4) == cudaSuccess;
-  if (!ok) {
-    for (void *m : maps) cudaIpcCloseMemHandle(m);
-    cudaFree(region);
-    ep.transport_note = "CUDA IPC handle exchange / mapping failed";
-    // restore the collective-library path's maps
-    tc::encode_map3d(&ep.map_x64, ep.xq, H, RR, 2, H, RR * H, 64);
-    tc::encode_map3d(&ep.map_x128, ep.xq, H, RR, 2, H, RR * H, 128);
-    return;
-  }
-  ep.region = region;
-  ep.peer_maps = maps;
-  ep.P = P;
-  ep.p2p = true;
-  ep.dispatch_grid = 2 * h->sm_count;
-  ep.transport_note.clear();
-}
-}  // namespace
-
-extern "C" moe_status moe_ep_unique_id(unsigned char id_out[128]) {
-  if (!id_out) return MOE_ERR_INVALID;
-  if (!nccl().ok) return MOE_ERR_NCCL;
-  ncclUniqueId id;
-  if (nccl().get_unique_id(&id) != ncclSuccess) return MOE_ERR_NCCL;
-  memcpy(id_out, id.internal, 128);
-  return MOE_OK;
-}
-
-extern "C" moe_status moe_ep_init(moe_handle *h, int rank, int nranks,
-                                  const unsigned char id[128], const int32_t *expert_owner) {
-  if (!h || !id || !expert_owner || nranks < 1 || rank < 0 || rank >= nranks)
-    return MOE_ERR_INVALID;
-  std::lock_guard<std::mutex> lock(h->mu);
-  drop_graphs(h);
-  if (!nccl().ok) {
-    set_err(h->err, "libnccl.so.2 not available");
-    return MOE_ERR_NCCL;
-  }
-  const int E = h->d.num_experts, H = h->d.hidden, I = h->d.intermediate, K = h->d.top_k;
-  if (H % 16 || I % 16 || !h->tc_ok) {
-    set_err(h->err, "expert parallelism needs the tensor-core path (H, I multiples of 16)");
-    return MOE_ERR_INVALID;
-  }
-  std::vector<int32_t> counts(nranks, 0), dest_local(E, -1);
-  for (int e = 0; e < E; ++e) {
-    const int o = expert_owner[e];
-    if (o < 0 || o >= nranks) {
-      set_err(h->err, "expert %d has owner %d outside [0, %d)", e, o, nranks);
-      return MOE_ERR_INVALID;
-    }
-    dest_local[e] = counts[o]++;  // local index = rank of e among its owner's experts
-  }
-  DeviceGuard g(h->device);
-  free_ep(h);
-  EpState &ep = h->ep;
-  ep.rank = rank;
-  ep.nranks = nranks;
-  ep.E_local = counts[rank];
-  ncclUniqueId uid;
-  memcpy(uid.internal, id, 128);
-  const ncclResult_t nr = nccl().comm_init_rank(&ep.comm, nranks, uid, rank);
-  if (nr != ncclSuccess) {
-    ep.comm = nullptr;
-    return nccl_fail(h, nr, "ncclCommInitRank");
-  }
-  const size_t Tm = h->d.max_tokens;
-  ep.r_local_cap = Tm * K;
-  ep.r_recv_cap = (size_t)nranks * Tm * K;
-  const size_t RL = ep.r_local_cap, RR = ep.r_recv_cap, ROW = ep_row_bytes(H);
-  ep.max_tiles = (int)((RR + 63) / 64 + std::min<size_t>(std::max(ep.E_local, 1), RR));
-  bool ok = ep_alloc(ep, &ep.d_owner, E) && ep_alloc(ep, &ep.d_dest_local, E) &&
-            ep_alloc(ep, &ep.dest, RL) && ep_alloc(ep, &ep.seg_dest, nranks + 1) &&
-            ep_alloc(ep, &ep.act_dest, nranks) && ep_alloc(ep, &ep.n_dest, 1) &&
-            ep_alloc(ep, &ep.stok, RL) && ep_alloc(ep, &ep.sslot, RL) &&
-            ep_alloc(ep, &ep.spos, RL) && ep_alloc(ep, &ep.sgate, RL) &&
-            ep_alloc(ep, &ep.scount, nranks) && ep_alloc(ep, &ep.rcount, nranks) &&
-            ep_alloc(ep, &ep.send, RL * ROW) && ep_alloc(ep, &ep.recv, RR * ROW) &&
-            ep_alloc(ep, &ep.ret, RL * H) && ep_alloc(ep, &ep.ids_l, RR) &&
-            ep_alloc(ep, &ep.gates_l, RR) && ep_alloc(ep, &ep.rgate_l, RR) &&
-            ep_alloc(ep, &ep.ybuf, RR * H) && ep_alloc(ep, &ep.act, RR * I) &&
-            ep_alloc(ep, &ep.seg_l, std::max(ep.E_local, 1) + 1) &&
-            ep_alloc(ep, &ep.active_l, std::max(ep.E_local, 1)) &&
-            ep_alloc(ep, &ep.n_active_l, 1) && ep_alloc(ep, &ep.rtok_l, RR) &&
-            ep_alloc(ep, &ep.rslot_l, RR) && ep_alloc(ep, &ep.rpos_l, RR) &&
-            ep_alloc(ep, &ep.xq, 2 * RR * H) && ep_alloc(ep, &ep.aq, 2 * RR * I) &&
-            ep_alloc(ep, &ep.xs1, RR) && ep_alloc(ep, &ep.xs2, RR) && ep_alloc(ep, &ep.as1, RR) &&
-            ep_alloc(ep, &ep.as2, RR) && ep_alloc(ep, &ep.act_amax, RR) &&
-            ep_alloc(ep, &ep.tile_expert, ep.max_tiles) &&
-            ep_alloc(ep, &ep.tile_row0, ep.max_tiles) &&
-            ep_alloc(ep, &ep.tile_rows, ep.max_tiles) && ep_alloc(ep, &ep.n_tiles, 1) &&
-            ep_alloc(ep, &ep.dtile_expert, ep.max_tiles) &&
-            ep_alloc(ep, &ep.dtile_row0, ep.max_tiles) &&
-            ep_alloc(ep, &ep.dtile_rows, ep.max_tiles) && ep_alloc(ep, &ep.n_dtiles, 1) &&
-            cudaMallocHost(&ep.h_counts, 2 * nranks * sizeof(int32_t)) == cudaSuccess;
-  if (!ok) {
-    free_ep(h);
-    return MOE_ERR_NOMEM;
-  }
-  cudaMemcpy(ep.d_owner, expert_owner, E * sizeof(int32_t), cudaMemcpyHostToDevice);
-  cudaMemcpy(ep.d_dest_local, dest_local.data(), E * sizeof(int32_t), cudaMemcpyHostToDevice);
-  ok = tc::encode_map3d(&ep.map_x64, ep.xq, H, RR, 2, H, RR * H, 64) &&
-       tc::encode_map3d(&ep.map_x128, ep.xq, H, RR, 2, H, RR * H, 128) &&
-       tc::encode_map3d(&ep.map_a64, ep.aq, I, RR, 2, I, RR * I, 64) &&
-       tc::encode_map3d(&ep.map_a128, ep.aq, I, RR, 2, I, RR * I, 128);
-  if (!ok) {
-    free_ep(h);
-    set_err(h->err, "tensor map encoding failed for the expert-parallel buffers");
-    return MOE_ERR_CUDA;
-  }
-  ep.layers.assign(h->d.num_layers, EpLayer{});
-  ep.on = true;
-  ep_setup_p2p(h, Tm);
-  return MOE_OK;
-}
-
-extern "C" int moe_ep_transport(const moe_handle *h) {
-  if (!h || !h->ep.on) return -1;
-  return h->ep.p2p ? 1 : 0;
-}
-
-extern "C" moe_status moe_ep_finalize(moe_handle *h) {
-  if (!h) return MOE_ERR_INVALID;
-  std::lock_guard<std::mutex> lock(h->mu);
-  DeviceGuard g(h->device);
-  drop_graphs(h);
-  free_ep(h);
-  return MOE_OK;
-}
-
-extern "C" moe_status moe_ep_set_layer(moe_handle *h, int layer, const int8_t *d_experts_local,
-                                       const float *d_scales_local, const void *d_router,
-                                       int router_dtype) {
-  if (!h || !d_router || (router_dtype != MOE_ROUTER_F32 && router_dtype != MOE_ROUTER_BF16))
-    return MOE_ERR_INVALID;
-  std::lock_guard<std::mutex> lock(h->mu);
-  drop_graphs(h);
-  EpState &ep = h->ep;
-  if (!ep.on || layer < 0 || layer >= (int)ep.layers.size()) {
-    set_err(h->err, "moe_ep_set_layer: call moe_ep_init first / layer out of range");
-    return MOE_ERR_STATE;
-  }
-  const size_t H = h->d.hidden, I = h->d.intermediate;
-  const int EL = ep.E_local;
-  if (EL > 0 && (!d_experts_local || !d_scales_local || ((uintptr_t)d_experts_local & 15) ||
-                 ((uintptr_t)d_scales_local & 3))) {
-    set_err(h->err, "local experts: null or misaligned pointers");
-    return MOE_ERR_INVALID;
-  }
-  DeviceGuard g(h->device);
-  EpLayer &L = ep.layers[layer];
-  if (!L.d_sptr && dalloc(&L.d_sptr, std::max(EL, 1)) != cudaSuccess) return MOE_ERR_NOMEM;
-  std::vector<const float *> sp(std::max(EL, 1), nullptr);
-  for (int e = 0; e < EL; ++e) sp[e] = d_scales_local + e * (2 * I + H);
-  cudaMemcpy(L.d_sptr, sp.data(), sp.size() * sizeof(void *), cudaMemcpyHostToDevice);
-  if (EL > 0) {
-    const char *wb = (const char *)d_experts_local;
-    if (!tc::encode_map3d(&L.map_gu, wb, H, 2 * I, EL, H, 3 * I * H, 128) ||
-        !tc::encode_map3d(&L.map_dn, wb + 2 * I * H, I, H, EL, I, 3 * I * H, 128)) {
-      set_err(h->err, "tensor map encoding failed for the local experts");
-      return MOE_ERR_CUDA;
-    }
-  }
-  // the router (replicated on every rank) lives in the ordinary layer slot
-  LayerSlot &S = h->layers[layer];
-  S.router = d_router;
-  S.router_dtype = router_dtype;
-  L.set = true;
-  return MOE_OK;
-}
-
-namespace {
-// One layer over the peer-memory transport; see ep.cu for the protocol.
-moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const float *d_resid,
-                          float *d_out, int T, cudaStream_t s) {
-  EpState &ep = h->ep;
-  const int H = h->d.hidden, I = h->d.intermediate, K = h->d.top_k, E = h->d.num_experts;
-  const int R = T * K;
-  const size_t RR = ep.r_recv_cap;
-  const LayerSlot &LS = h->layers[layer];
-  const EpLayer &EL = ep.layers[layer];
-  const EpP2P &P = ep.P;
-  uint32_t *epoch = ep.epoch;  // advanced on the device by the publish kernel
-  cudaError_t e = cudaSuccess;
-  // 1. route and bucket the local routes by global expert
-  cudaEvent_t p0 = nullptr;
-  if (T > 0) {
-    moe_status st = run_route(h, LS, d_h, T, h->ids, h->gates, nullptr, s, false);
-    if (st != MOE_OK) return st;
-    p0 = h->prof.begin(s);
-    PermuteArgs pa{};
-    pa.ids = h->ids;
-    pa.gates = h->gates;
-    pa.T = T;
-    pa.K = K;
-    pa.E = E;
-    pa.seg_off = h->seg_off;
-    pa.active = h->active;
-    pa.n_active = h->n_active;
-    pa.r_token = h->r_token;
-    pa.r_slot = h->r_slot;
-    pa.r_gate = h->r_gate;
-    pa.r_pos = h->r_pos;
-    pa.status = h->status;
-    pa.scratch = h->perm_scratch;
-    pa.scratch_words = h->perm_scratch_words;
-    e = launch_permute(pa, s);
-    h->prof.end("permute", p0, s);
-    h->last_launches += permute_launches(pa);
-  } else {
-    e = cudaMemsetAsync(h->seg_off, 0, (E + 1) * sizeof(int32_t), s);
-  }
-  // 2. counts to every peer, 3. routes straight into the owners' buffers
-  cudaEvent_t p1 = h->prof.begin(s);
-  if (e == cudaSuccess) e = launch_ep_publish(h->seg_off, E, P, epoch, s);
-  if (e == cudaSuccess)
-    e = launch_ep_dispatch(d_h, h->seg_off, h->ids, h->gates, h->r_pos, ep.d_owner, E, T, K, H,
-                           P, epoch, ep.done, ep.dispatch_grid, h->status, s);
-  h->prof.end("ep_dispatch", p1, s);
-  if (e != cudaSuccess) return cuda_fail(h, e, "ep dispatch");
-  // 4. wait for every rank's routes; expert segments from the count matrix
-  cudaEvent_t p2 = h->prof.begin(s);
-  e = launch_ep_recv_prep(ep.d_owner, E, P, epoch, ep.seg_l, ep.active_l, ep.n_active_l,
-                          ep.n_recv, h->status, s);
-  // tile widths from the expected receive count (this rank's own route
-  // count: the ranks route equal token counts)
-  const int bn = tc::tc_block_n(std::max(R, 1), std::max(ep.E_local, 1));
-  const int dbn = tc::tc_block_n_down(std::max(R, 1), std::max(ep.E_local, 1));
-  if (e == cudaSuccess && ep.E_local > 0)
-    e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, bn, ep.tile_expert,
-                               ep.tile_row0, ep.tile_rows, ep.n_tiles, ep.max_tiles, s);
-  if (e == cudaSuccess && ep.E_local > 0 && dbn != bn)
-    e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, dbn, ep.dtile_expert,
-                               ep.dtile_row0, ep.dtile_rows, ep.n_dtiles, ep.max_tiles, s);
-  h->prof.end("ep_recv", p2, s);
-  if (e != cudaSuccess) return cuda_fail(h, e, "ep receive");
-  // 5. experts; the down epilogue writes each output row to its source rank
-  if (ep.E_local > 0) {
-    uint8_t *me = P.base[P.rank];
-    tc::TcArgs a{};
-    a.H = H;
-    a.I = I;
-    a.K = K;
-    a.tile_expert = ep.tile_expert;
-    a.tile_row0 = ep.tile_row0;
-    a.tile_rows = ep.tile_rows;
-    a.n_tiles = ep.n_tiles;
-    a.s_ptr = EL.d_sptr;
-    a.xs1 = (const float *)(me + P.off_s1);
-    a.xs2 = (const float *)(me + P.off_s2);
-    a.act = ep.act;
-    a.act_amax = (uint32_t *)(me + P.off_amax);
-    a.as1 = ep.as1;
-    a.as2 = ep.as2;
-    a.r_token = (const int32_t *)(me + P.off_tok);
-    a.r_slot = (const int32_t *)(me + P.off_slot);
-    a.r_gate = (const float *)(me + P.off_gate);
-    a.r_rank = (const int32_t *)(me + P.off_rank);
-    for (int q = 0; q < P.nranks; ++q) a.peer_contrib[q] = (float *)(P.base[q] + P.off_contrib);
-    a.contrib = a.peer_contrib[P.rank];
-    a.status = h->status;
-    cudaEvent_t p3 = h->prof.begin(s);
-    e = tc::launch_gate_up_tc(EL.map_gu, bn == 64 ? ep.map_x64 : ep.map_x128, a, bn,
-                              ep.max_tiles, s);
-    h->prof.end("gate_up_tc", p3, s);
-    p3 = h->prof.begin(s);
-    if (e == cudaSuccess)
-      e = tc::launch_quantize_rows(ep.act, nullptr, a.act_amax, (int)RR, I, ep.aq, RR * I,
-                                   ep.as1, ep.as2, nullptr, s, ep.n_recv);
-    h->prof.end("tc_act_digits", p3, s);
-    if (dbn != bn) {
-      a.tile_expert = ep.dtile_expert;
-      a.tile_row0 = ep.dtile_row0;
-      a.tile_rows = ep.dtile_rows;
-      a.n_tiles = ep.n_dtiles;
-    }
-    p3 = h->prof.begin(s);
-    if (e == cudaSuccess)
-      e = tc::launch_down_tc(EL.map_dn, dbn == 64 ? ep.map_a64 : ep.map_a128, a, dbn,
-                             ep.max_tiles, s);
-    h->prof.end("down_tc", p3, s);
-    if (e != cudaSuccess) return cuda_fail(h, e, "ep experts");
-  }
-  // 6. outputs are in: signal the sources; 7. combine this rank's tokens
-  cudaEvent_t p4 = h->prof.begin(s);
-  e = launch_ep_signal(P, epoch, s);
-  if (e == cudaSuccess)
-    e = launch_ep_wait_combine(P, epoch, d_resid, d_out, T, K, H, h->status, s);
-  h->prof.end("ep_combine", p4, s);
-  if (e != cudaSuccess) return cuda_fail(h, e, "ep combine");
-  // publish, dispatch, receive, signal, combine; tile lists and the three
-  // expert kernels when this rank owns experts
-  h->last_launches += 5 + (ep.E_local > 0 ? 4 + (dbn != bn ? 1 : 0) : 0);
-  return MOE_OK;
-}
-}  // namespace
-
-extern "C" moe_status moe_ep_layer_forward(moe_handle *h, int layer, const float *d_h,
-                                           const float *d_resid, float *d_out, int T,
-                                           void *stream) {
-  if (!h || !d_h || !d_out || ((uintptr_t)d_h & 15)) return MOE_ERR_INVALID;
-  std::lock_guard<std::mutex> lock(h->mu);
-  EpState &ep = h->ep;
-  if (!ep.on || layer < 0 || layer >= (int)ep.layers.size() || !ep.layers[layer].set) {
-    set_err(h->err, "expert-parallel layer %d not ready", layer);
-    return MOE_ERR_STATE;
-  }
-  if (T < 0 || T > h->d.max_tokens) {
-    set_err(h->err, "token count %d outside [0, %d]", T, h->d.max_tokens);
-    return MOE_ERR_INVALID;
-  }
-  DeviceGuard g(h->device);
-  cudaStream_t s = pick(h, stream);
-  h->last_launches = 0;
-  const int H = h->d.hidden, I = h->d.intermediate, K = h->d.top_k, E = h->d.num_experts;
-  const int N = ep.nranks, R = T * K;
-  const size_t ROW = ep_row_bytes(H), RR = ep.r_recv_cap;
-  const LayerSlot &LS = h->layers[layer];
-  const EpLayer &EL = ep.layers[layer];
-  cudaError_t e = cudaSuccess;
-  moe_status st = MOE_OK;
-  if (ep.p2p) {
-    const uint64_t key[10] = {3, (uint64_t)layer, (uint64_t)T, (uint64_t)d_h, (uint64_t)d_resid,
-                              (uint64_t)d_out, (uint64_t)s, (uint64_t)h->route_mode, 0, 0};
-    return graphed(h, key, s, [&] {
-      h->last_launches = 0;
-      return ep_forward_p2p(h, layer, d_h, d_resid, d_out, T, s);
-    });
-  }
-  // 1. route the local tokens and bucket the routes by owner rank
-  if (T > 0) {
-    st = run_route(h, LS, d_h, T, h->ids, h->gates, nullptr, s, false);
-    if (st != MOE_OK) return st;
-    e = launch_ep_dest(h->ids, ep.d_owner, R, E, ep.dest, h->status, s);
-    PermuteArgs pa{};
-    pa.ids = ep.dest;
-    pa.gates = h->gates;
-    pa.T = T;
-    pa.K = K;
-    pa.E = N;
-    pa.seg_off = ep.seg_dest;
-    pa.active = ep.act_dest;
-    pa.n_active = ep.n_dest;
-    pa.r_token = ep.stok;
-    pa.r_slot = ep.sslot;
-    pa.r_gate = ep.sgate;
-    pa.r_pos = ep.spos;
-    pa.status = h->status;
-    pa.scratch = h->perm_scratch;
-    pa.scratch_words = h->perm_scratch_words;
-    cudaEvent_t p0 = h->prof.begin(s);
-    if (e == cudaSuccess) e = launch_permute(pa, s);
-    if (e == cudaSuccess)
-      e = launch_ep_pack(d_h, ep.stok, ep.sslot, ep.sgate, h->ids, ep.d_dest_local, R, K, H,
-                         ep.send, s);
-    if (e == cudaSuccess) e = launch_seg_counts(ep.seg_dest, N, ep.scount, s);
-    h->prof.end("ep_dispatch_prep", p0, s);
-  } else {
-    e = cudaMemsetAsync(ep.scount, 0, N * sizeof(int32_t), s);
-  }
-  if (e != cudaSuccess) return cuda_fail(h, e, "ep dispatch prep");
-  // 2. exchange counts, then the payload (the one host synchronisation)
-  const NcclApi &api = nccl();
-  cudaEvent_t p1 = h->prof.begin(s);
-  ncclResult_t nr = api.group_start();
-  for (int p = 0; p < N && nr == ncclSuccess; ++p) {
-    nr = api.send(ep.scount + p, 1, ncclInt32, p, ep.comm, s);
-    if (nr == ncclSuccess) nr = api.recv(ep.rcount + p, 1, ncclInt32, p, ep.comm, s);
-  }
-  const ncclResult_t ng = api.group_end();
-  if (nr != ncclSuccess || ng != ncclSuccess) return nccl_fail(h, nr ? nr : ng, "count exchange");
-  cudaMemcpyAsync(ep.h_counts, ep.scount, N * sizeof(int32_t), cudaMemcpyDeviceToHost, s);
-  cudaMemcpyAsync(ep.h_counts + N, ep.rcount, N * sizeof(int32_t), cudaMemcpyDeviceToHost, s);
-  e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return cuda_fail(h, e, "count exchange");
-  std::vector<size_t> soff(N + 1, 0), roff(N + 1, 0);
-  for (int p = 0; p < N; ++p) {
-    soff[p + 1] = soff[p] + ep.h_counts[p];
-    roff[p + 1] = roff[p] + ep.h_counts[N + p];
-  }
-  const size_t Rr = roff[N];
-  if (Rr > RR || soff[N] != (size_t)R) {
-    set_err(h->err, "expert-parallel exchange sizes inconsistent (%zu received, cap %zu)", Rr, RR);
-    return MOE_ERR_STATE;
-  }
-  nr = api.group_start();
-  for (int p = 0; p < N && nr == ncclSuccess; ++p) {
-    if (ep.h_counts[p])
-      nr = api.send(ep.send + soff[p] * ROW, ep.h_counts[p] * ROW, ncclUint8, p, ep.comm, s);
-    if (nr == ncclSuccess && ep.h_counts[N + p])
-      nr = api.recv(ep.recv + roff[p] * ROW, ep.h_counts[N + p] * ROW, ncclUint8, p, ep.comm, s);
-  }
-  const ncclResult_t ng2 = api.group_end();
-  h->prof.end("ep_dispatch_comm", p1, s);
-  if (nr != ncclSuccess || ng2 != ncclSuccess) return nccl_fail(h, nr ? nr : ng2, "dispatch");
-  // 3. experts on the received routes (tensor cores)
-  const int Rri = (int)Rr;
-  if (Rri > 0 && ep.E_local > 0) {
-    cudaEvent_t p2 = h->prof.begin(s);
-    e = launch_ep_unpack_meta(ep.recv, Rri, H, ep.E_local, ep.ids_l, ep.gates_l, h->status, s);
-    PermuteArgs pl{};
-    pl.ids = ep.ids_l;
-    pl.gates = ep.gates_l;
-    pl.T = Rri;
-    pl.K = 1;
-    pl.E = ep.E_local;
-    pl.seg_off = ep.seg_l;
-    pl.active = ep.active_l;
-    pl.n_active = ep.n_active_l;
-    pl.r_token = ep.rtok_l;
-    pl.r_slot = ep.rslot_l;
-    pl.r_gate = ep.rgate_l;
-    pl.r_pos = ep.rpos_l;
-    pl.status = h->status;
-    if (e == cudaSuccess) e = launch_permute(pl, s);
-    if (e == cudaSuccess)
-      e = launch_ep_unpack_digits(ep.recv, ep.rtok_l, Rri, H, ep.xq, RR * H, ep.xs1, ep.xs2,
-                                  ep.act_amax, s);
-    const int bn = tc::tc_block_n(Rri, ep.E_local);
-    const int dbn = tc::tc_block_n_down(Rri, ep.E_local);
-    if (e == cudaSuccess)
-      e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, bn, ep.tile_expert,
-                                 ep.tile_row0, ep.tile_rows, ep.n_tiles, ep.max_tiles, s);
-    if (e == cudaSuccess && dbn != bn)
-      e = tc::launch_build_tiles(ep.seg_l, ep.active_l, ep.n_active_l, dbn, ep.dtile_expert,
-                                 ep.dtile_row0, ep.dtile_rows, ep.n_dtiles, ep.max_tiles, s);
-    h->prof.end("ep_unpack", p2, s);
-    tc::TcArgs a{};
-    a.H = H;
-    a.I = I;
-    a.K = 1;  // outputs go to ybuf[received row]
-    a.tile_expert = ep.tile_expert;
-    a.tile_row0 = ep.tile_row0;
-    a.tile_rows = ep.tile_rows;
-    a.n_tiles = ep.n_tiles;
-    a.s_ptr = EL.d_sptr;
-    a.xs1 = ep.xs1;
-    a.xs2 = ep.xs2;
-    a.act = ep.act;
-    a.act_amax = ep.act_amax;
-    a.as1 = ep.as1;
-    a.as2 = ep.as2;
-    a.r_token = ep.rtok_l;
-    a.r_slot = ep.rslot_l;
-    a.r_gate = ep.rgate_l;
-    a.contrib = ep.ybuf;
-    a.status = h->status;
-    const int tiles =
-        std::min(ep.max_tiles, (Rri + bn - 1) / bn + std::min(ep.E_local, Rri));
-    cudaEvent_t p3 = h->prof.begin(s);
-    if (e == cudaSuccess)
-      e = tc::launch_gate_up_tc(EL.map_gu, bn == 64 ? ep.map_x64 : ep.map_x128, a, bn, tiles, s);
-    h->prof.end("gate_up_tc", p3, s);
-    p3 = h->prof.begin(s);
-    if (e == cudaSuccess)
-      e = tc::launch_quantize_rows(ep.act, nullptr, ep.act_amax, Rri, I, ep.aq, RR * I, ep.as1,
-                                   ep.as2, nullptr, s);
-    h->prof.end("tc_act_digits", p3, s);
-    int dtiles = tiles;
-    if (dbn != bn) {
-      a.tile_expert = ep.dtile_expert;
-      a.tile_row0 = ep.dtile_row0;
-      a.tile_rows = ep.dtile_rows;
-      a.n_tiles = ep.n_dtiles;
-      dtiles = std::min(ep.max_tiles, (Rri + dbn - 1) / dbn + std::min(ep.E_local, Rri));
-    }
-    p3 = h->prof.begin(s);
-    if (e == cudaSuccess)
-      e = tc::launch_down_tc(EL.map_dn, dbn == 64 ? ep.map_a64 : ep.map_a128, a, dbn, dtiles, s);
-    h->prof.end("down_tc", p3, s);
-    if (e != cudaSuccess) return cuda_fail(h, e, "ep experts");
-  }
-  // 4. send the gate-weighted outputs back; combine on the owner in slot order
-  cudaEvent_t p4 = h->prof.begin(s);
-  nr = api.group_start();
-  for (int p = 0; p < N && nr == ncclSuccess; ++p) {
-    if (ep.h_counts[N + p])
-      nr = api.send(ep.ybuf + roff[p] * H, ep.h_counts[N + p] * (size_t)H, ncclFloat32, p,
-                    ep.comm, s);
-    if (nr == ncclSuccess && ep.h_counts[p])
-      nr = api.recv(ep.ret + soff[p] * H, ep.h_counts[p] * (size_t)H, ncclFloat32, p, ep.comm, s);
-  }
-  const ncclResult_t ng3 = api.group_end();
-  h->prof.end("ep_combine_comm", p4, s);
-  if (nr != ncclSuccess || ng3 != ncclSuccess) return nccl_fail(h, nr ? nr : ng3, "combine");
-  if (T > 0) {
-    cudaEvent_t p5 = h->prof.begin(s);
-    e = launch_ep_gather_combine(ep.ret, ep.spos, d_resid, d_out, T, K, H, h->status, s);
-    h->prof.end("combine", p5, s);
-    if (e != cudaSuccess) return cuda_fail(h, e, "ep combine");
-  }
-  h->last_launches += 12;
-  return MOE_OK;
-}

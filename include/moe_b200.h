@@ -112,11 +112,7 @@ enum {
                                small T the whole layer runs as one cooperative launch */
   MOE_PATH_TENSOR = 2,      /* tcgen05 grouped GEMM (within the 1e-3 tolerance) */
   MOE_PATH_GEMV_PHASED = 3, /* exact-order GEMV, one launch per phase (no fusion) */
-  MOE_PATH_GEMV_FUSED = 4,  /* same as MOE_PATH_GEMV: the register-prefetch single launch */
-  MOE_PATH_GEMV_STREAM = 5  /* exact-order GEMV, one launch, weights staged through a
-                               shared-memory ring with cp.async (needs 16-byte aligned
-                               experts, H and I multiples of 32); falls back to the
-                               register-prefetch launch otherwise */
+  MOE_PATH_GEMV_FUSED = 4   /* same as MOE_PATH_GEMV: the register-prefetch single launch */
 };
 
 moe_status moe_create(int device, const moe_dims *dims, moe_handle **out);
@@ -125,8 +121,8 @@ const char *moe_last_error(const moe_handle *h);
 /* Replay each call's launch sequence as a CUDA graph (default on).  The
  * sequence is captured once per (call, layer, token count, buffers, stream,
  * path) and replayed afterwards; captures are dropped when weights, path or
- * routing mode change.  Calls run with direct launches while profiling is on,
- * inside a caller's own stream capture, and on MOE_PATH_GEMV_STREAM. */
+ * routing mode change.  Calls run with direct launches while profiling is on
+ * and inside a caller's own stream capture. */
 moe_status moe_set_graphs(moe_handle *h, int enable);
 /* Default stream for calls that pass stream == NULL. */
 moe_status moe_set_stream(moe_handle *h, void *cuda_stream);

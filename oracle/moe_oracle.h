@@ -106,7 +106,7 @@ int oracle_layer_forward(const oracle_layer *L, int T, const float *h,
                          int32_t *use_slot, float *use_gate, int mode,
                          int nthreads);
 
-/* Stacked layers (BASELINE configs 2 and 3): x <- x + MoE(RMSNorm(x; w=1)).
+/* Stacked decode layers: x <- x + MoE(RMSNorm(x; w=1)) per layer.
  * x: [T,H] updated in place.  ids/gates (optional): [nlayers,T,K]. */
 int oracle_stack_forward(const oracle_layer *layers, int nlayers, int T,
                          float *x, float eps, uint32_t *ids, float *gates,

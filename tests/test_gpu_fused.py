@@ -1,8 +1,6 @@
-"""GPU tests of the single-launch decode kernels: the register-prefetch kernel
-(MOE_PATH_GEMV, the default) and the streaming kernel (weights staged through
-a shared-memory ring, MOE_PATH_GEMV_STREAM).  Both use the phased kernels' arithmetic, so
-everything is compared bit for bit: against the oracle and against
-MOE_PATH_GEMV_PHASED."""
+"""GPU tests of the single-launch exact decode kernel (MOE_PATH_GEMV).  It
+uses the phased kernels' arithmetic, so everything is compared bit for bit:
+against the oracle and against MOE_PATH_GEMV_PHASED."""
 import numpy as np
 import pytest
 
@@ -15,7 +13,7 @@ torch = pytest.importorskip("torch")
 import doantotnghiepmoe_b200 as M  # noqa: E402
 from doantotnghiepmoe_b200 import _lib  # noqa: E402
 
-KERNELS = [(_lib.MOE_PATH_GEMV_STREAM, "stream_decode"), (_lib.MOE_PATH_GEMV, "fused_decode")]
+KERNELS = [(_lib.MOE_PATH_GEMV, "fused_decode")]
 
 
 def bits(a):
@@ -59,7 +57,7 @@ def test_single_launch_equals_phased_and_oracle(T, path, kernel):
     cfg = M.MoeConfig(2048, 1024, 64, 8, T == 5, T, 1)
     eng, of = check_layer(lw, h, resid, path, kernel, cfg)
     op, _, _, pp = layer_out(eng, h, _lib.MOE_PATH_GEMV_PHASED, resid)
-    assert "fused_decode" not in pp and "stream_decode" not in pp
+    assert "fused_decode" not in pp
     assert np.array_equal(bits(of), bits(op))
 
 
@@ -95,62 +93,6 @@ def test_qwen3_stack_t64(path, kernel):
     xg = x.cpu().numpy()
     assert helpers.rel_err(xg, q["ref"]) < 1e-3
     assert np.array_equal(bits(xg), bits(q["ref"]))
-
-
-@pytest.mark.parametrize("T", [1, 8, 32])
-def test_stream_olmoe_stack(T):
-    """Config-2 shapes (OLMoE layers, RMSNorm + residual between them) through
-    one streaming launch per stack of three layers; repeated twice so the
-    alternating counter sets are both exercised."""
-    layers = [O.synth_layer(231, l, 2048, 1024, 64, 8, False) for l in range(3)]
-    x0 = O.synth_hidden(231, T, 2048)
-    ref_x, ref_ids, _ = O.stack_forward(layers, x0, nthreads=8)
-    eng = M.MoeLayerEngine(M.MoeConfig(2048, 1024, 64, 8, False, T, 3))
-    keep = [helpers.to_device(lw) for lw in layers]
-    for l, t in enumerate(keep):
-        eng.set_layer_packed(l, *t)
-    eng.set_path(_lib.MOE_PATH_GEMV_STREAM)
-    for _ in range(2):
-        x = torch.from_numpy(x0).cuda()
-        eng.profile(True)
-        eng.stack_forward(0, 3, x, 1e-5)
-        eng.sync_status()
-        assert "stream_decode" in eng.profile_read()
-        assert np.array_equal(bits(x.cpu().numpy()), bits(ref_x))
-
-
-def test_stream_many_routes_per_expert():
-    """Few experts, many tokens: experts hold more routes than one segment
-    (4), and windows straddle two segments with up to eight staged token
-    rows."""
-    H, I, E, K, T = 512, 256, 8, 2, 24
-    lw = O.synth_layer(241, 0, H, I, E, K, True)
-    h = O.synth_hidden(241, T, H)
-    resid = O.synth_hidden(242, T, H)
-    check_layer(lw, h, resid, _lib.MOE_PATH_GEMV_STREAM, "stream_decode",
-                M.MoeConfig(H, I, E, K, True, T, 1))
-
-
-def test_stream_bf16_router():
-    """A bf16 router (rows staged with scalar loads) through the streaming
-    kernel."""
-    H, I, E, K, T = 512, 256, 32, 4, 3
-    lw = O.synth_layer(251, 0, H, I, E, K, False)
-    rb = (lw.router.view(np.uint32) >> 16).astype(np.uint16)
-    lw = O.LayerWeights(H, I, E, K, False, rb, lw.experts, lw.scales, router_bf16=True)
-    h = O.synth_hidden(251, T, H)
-    check_layer(lw, h, None, _lib.MOE_PATH_GEMV_STREAM, "stream_decode",
-                M.MoeConfig(H, I, E, K, False, T, 1))
-
-
-def test_stream_falls_back_on_odd_shapes():
-    """I not a multiple of 32: the streaming kernel declines and the
-    register-prefetch kernel runs instead, still bit-exact."""
-    H, I, E, K, T = 256, 200, 16, 4, 2
-    lw = O.synth_layer(261, 0, H, I, E, K, True)
-    h = O.synth_hidden(261, T, H)
-    check_layer(lw, h, None, _lib.MOE_PATH_GEMV_STREAM, "fused_decode",
-                M.MoeConfig(H, I, E, K, True, T, 1))
 
 
 @pytest.mark.parametrize("path,kernel", KERNELS)
