@@ -96,6 +96,8 @@ SIGNATURES = {
     "moe_ep_finalize": (I32, [P]),
     "moe_ep_transport": (I32, [P]),
     "moe_set_graphs": (I32, [P, I32]),
+    "moe_set_wait_limit": (I32, [P, U64]),
+    "moe_debug_wait_flag": (I32, [P, P]),
 }
 
 _lib = None

@@ -42,7 +42,6 @@ using namespace gemv;
 constexpr int kFT = 256;          // threads per CTA (8 warps)
 constexpr int kRTT = 4;           // router task: tokens
 constexpr int kRTE = 4;           // router task: experts
-constexpr long long kBarrierCycles = 2000000000LL;  // ~1 s
 
 struct Tables {
   uint64_t tile_full[kTileStages];  // weight-tile ring mbarriers
@@ -57,7 +56,11 @@ struct Tables {
   int32_t wcnt[kFT / 32][kMaxExperts];
 };
 
-__device__ __forceinline__ bool grid_sync(uint32_t *bar, uint32_t target, uint32_t *status) {
+// Grid barrier; each wait gives up after `limit` SM clock cycles
+// (FusedArgs::wait_cycles, the handle's wait bound) and records
+// kStatusTimeout.
+__device__ __forceinline__ bool grid_sync(uint32_t *bar, uint32_t target, uint32_t *status,
+                                          long long limit) {
   __shared__ int ok;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -66,7 +69,7 @@ __device__ __forceinline__ bool grid_sync(uint32_t *bar, uint32_t target, uint32
     const long long t0 = clock64();
     int good = 1;
     while (*(volatile uint32_t *)bar < target) {
-      if (clock64() - t0 > kBarrierCycles) {
+      if (clock64() - t0 > limit) {
         good = 0;
         set_status(status, kStatusTimeout);
         break;
@@ -392,7 +395,7 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
                                                       r1, tb.r_token, hin, stage, a.act);
   }
   ++nbar;
-  if (!grid_sync(a.bar, nbar * G, a.status)) {
+  if (!grid_sync(a.bar, nbar * G, a.status, a.wait_cycles)) {
     alive = false;
     return;
   }
@@ -424,7 +427,7 @@ __device__ void expert_phases(const FusedArgs &a, const FusedLayer &L, const flo
   }
   if (!good) set_status(a.status, kStatusNonFinite);
   ++nbar;
-  if (!grid_sync(a.bar, nbar * G, a.status)) alive = false;
+  if (!grid_sync(a.bar, nbar * G, a.status, a.wait_cycles)) alive = false;
   stamp(a, 3);
 }
 
@@ -499,7 +502,7 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
       rms_row(a.out + (size_t)t * H, a.layers[0].norm_w, a.hbuf + (size_t)t * H, H, a.eps, red,
               a.status);
     ++nbar;
-    if (!grid_sync(a.bar, nbar * G, a.status)) return;
+    if (!grid_sync(a.bar, nbar * G, a.status, a.wait_cycles)) return;
     hin = a.hbuf;
   }
   for (int l = 0; l < a.n_layers; ++l) {
@@ -513,11 +516,15 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
     }
     router_phase(a, L, hin, stage, tb, sel);
     ++nbar;
-    if (!grid_sync(a.bar, nbar * G, a.status)) return;
+    if (!grid_sync(a.bar, nbar * G, a.status, a.wait_cycles)) return;
     if (l == 0) stamp(a, 1);
     build_tables(a, tb);
     expert_phases<kVec, kMulti, kQ, kTiles>(a, L, hin, stage, tb, rg, nbar, alive);
-    if (!alive) return;
+    // A dead ring (a stage wait gave up; kStatusTimeout is set) may still
+    // have a copy in flight into its shared memory, which the next layer's
+    // router staging overlaps: this CTA stops here, and the others' bounded
+    // barrier waits end the launch.
+    if (!alive || rg.dead) return;
     if (!a.stacked) {
       // C: out = resid + contrib[., 0] + ... + contrib[., K-1] (slot order)
       bool bad = false;
@@ -555,7 +562,7 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
       }
       if (l + 1 < a.n_layers) {
         ++nbar;
-        if (!grid_sync(a.bar, nbar * G, a.status)) return;
+        if (!grid_sync(a.bar, nbar * G, a.status, a.wait_cycles)) return;
       }
     }
   }

@@ -219,17 +219,24 @@ cudaError_t launch_seg_counts(const int32_t *seg, int n, int32_t *cnt, cudaStrea
 namespace moe {
 namespace {
 
-constexpr long long kEpWaitCycles = 4000000000LL;  // ~2 s
-
-__device__ __forceinline__ bool ep_wait_flags(const uint32_t *flags, int n, uint32_t epoch) {
+// Wait until flags[0..n) all reach epoch; false once `limit` SM clock
+// cycles have passed (the handle's wait bound, EpP2P::wait_cycles).
+__device__ __forceinline__ bool ep_wait_flags(const uint32_t *flags, int n, uint32_t epoch,
+                                              long long limit) {
   const long long t0 = clock64();
   for (int q = 0; q < n; ++q) {
     const volatile uint32_t *f = flags + q;
     while (*f < epoch)
-      if (clock64() - t0 > kEpWaitCycles) return false;
+      if (clock64() - t0 > limit) return false;
   }
   __threadfence_system();
   return true;
+}
+
+__global__ void wait_probe_kernel(const uint32_t *flags, int n, uint32_t target, long long limit,
+                                  uint32_t *status) {
+  if (threadIdx.x == 0 && !ep_wait_flags(flags, n, target, limit))
+    set_status(status, kStatusTimeout);
 }
 
 __device__ __forceinline__ uint8_t *peer_at(const EpP2P &p, int rank, size_t off) {
@@ -299,7 +306,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
   if (threadIdx.x == 0) {
     ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
                            0 * kEpMaxRanks,
-                       p.nranks, epoch);
+                       p.nranks, epoch, p.wait_cycles);
     if (!ok) set_status(status, kStatusTimeout);
   }
   for (int e = threadIdx.x; e <= E; e += blockDim.x) segs[e] = seg_off[e];
@@ -412,7 +419,7 @@ __global__ void __launch_bounds__(256) ep_recv_prep_kernel(const int32_t *__rest
   if (threadIdx.x == 0) {
     ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
                            1 * kEpMaxRanks,
-                       p.nranks, epoch);
+                       p.nranks, epoch, p.wait_cycles);
     if (!ok) set_status(status, kStatusTimeout);
   }
   __syncthreads();
@@ -459,7 +466,7 @@ __global__ void ep_wait_combine_kernel(EpP2P p, const uint32_t *epoch_p,
   if (threadIdx.x == 0) {
     ok = ep_wait_flags(reinterpret_cast<const uint32_t *>(p.base[p.rank] + p.off_flags) +
                            2 * kEpMaxRanks,
-                       p.nranks, epoch);
+                       p.nranks, epoch, p.wait_cycles);
     if (!ok) set_status(status, kStatusTimeout);
   }
   __syncthreads();
@@ -532,6 +539,12 @@ cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p,
                                 int32_t *n_recv, uint32_t *status, cudaStream_t s) {
   ep_recv_prep_kernel<<<1, 256, 0, s>>>(owner, E, p, epoch, seg_l, active_l, n_active_l, n_recv,
                                         status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wait_probe(const uint32_t *flags, int n, uint32_t target,
+                              long long wait_cycles, uint32_t *status, cudaStream_t s) {
+  wait_probe_kernel<<<1, 32, 0, s>>>(flags, n, target, wait_cycles, status);
   return cudaGetLastError();
 }
 

@@ -84,6 +84,7 @@ void ep_setup_p2p(moe_handle *h, size_t Tm) {
   P.off_contrib = off; off = align_up(off + Tm * K * H * 4, 1024);
   P.rank = ep.rank;
   P.nranks = N;
+  P.wait_cycles = h->wait_flag_cycles;
   void *region = nullptr;
   if (cudaMalloc(&region, off) != cudaSuccess || cudaMemset(region, 0, off) != cudaSuccess) {
     cudaGetLastError();

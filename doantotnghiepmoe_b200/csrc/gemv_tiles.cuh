@@ -142,6 +142,10 @@ __device__ __forceinline__ bool tile_pass(TileRing &rg, int nst, int nc, int til
           tma::mbar_wait(&rg.full[ud % kTileStages], (ud / kTileStages) & 1u, nullptr);
         }
       __syncthreads();
+      // If a drain wait gave up too, a copy may still land in the ring: the
+      // ring's shared memory is never read or reused after this (callers
+      // skip every later item, and the decode kernel returns at the end of
+      // the layer).
       rg.dead = true;
       return false;
     }

@@ -23,6 +23,11 @@ namespace host {
 
 // Prefill-sized calls (T >= this) take the tensor-core path under MOE_PATH_AUTO.
 constexpr int kTcMinTokens = 128;
+// Default bounds of the device-side waits, in SM clock cycles: about 1 s for
+// the single-launch kernels' grid barriers and 2 s for the expert-parallel
+// flag waits at the maximum SM clock.
+constexpr long long kDefaultBarrierWaitCycles = 2000000000LL;
+constexpr long long kDefaultFlagWaitCycles = 4000000000LL;
 
 void set_err(std::string &dst, const char *fmt, ...);
 
@@ -222,6 +227,10 @@ struct moe_handle {
   std::vector<GraphEntry> graphs;
   uint64_t graph_clock = 0;
   bool graphs_on = true;
+  // device-side wait bounds, in SM clock cycles (moe_set_wait_limit)
+  long long wait_barrier_cycles = moe::host::kDefaultBarrierWaitCycles;
+  long long wait_flag_cycles = moe::host::kDefaultFlagWaitCycles;
+  uint32_t *probe_flag = nullptr;  // device word that nothing sets (moe_debug_wait_flag)
   moe::host::EpState ep;
 };
 

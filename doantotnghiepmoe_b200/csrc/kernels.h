@@ -141,6 +141,7 @@ struct FusedArgs {
   int int4;                  // every layer of the launch has INT4 experts
   int tiles;                 // every layer has weight-tile maps; 16-byte aligned inputs
   unsigned long long *phase_ts;  // optional [5] phase timestamps (profiling)
+  long long wait_cycles;     // bound of each grid-barrier wait (SM clock cycles)
 };
 bool fused_decode_supported(int T, int H, int I, int E, int K);
 cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint32_t *bar,
@@ -176,6 +177,7 @@ struct EpP2P {
   size_t off_xq, plane;        // int8 [2][RR][H] digit planes (plane = RR * H)
   size_t off_s1, off_s2, off_gate, off_rank, off_tok, off_slot, off_amax;  // [RR]
   size_t off_contrib;          // f32 [T, K, H] outputs of this rank's routes
+  long long wait_cycles;       // bound of every flag wait (SM clock cycles)
 };
 // epoch: this rank's call counter in device memory; the publish kernel
 // advances it, every later kernel of the call reads it.
@@ -193,6 +195,11 @@ cudaError_t launch_ep_recv_prep(const int32_t *owner, int E, const EpP2P &p,
                                 int32_t *n_active_l, int32_t *n_recv, uint32_t *status,
                                 cudaStream_t s);
 cudaError_t launch_ep_signal(const EpP2P &p, const uint32_t *epoch, cudaStream_t s);
+// One thread waits, with the flag waits' bound, until flags[0..n) all reach
+// `target`; on expiry kStatusTimeout goes into *status.  Used by the
+// failure-path test (moe_debug_wait_flag) on a flag that nobody sets.
+cudaError_t launch_wait_probe(const uint32_t *flags, int n, uint32_t target,
+                              long long wait_cycles, uint32_t *status, cudaStream_t s);
 cudaError_t launch_ep_wait_combine(const EpP2P &p, const uint32_t *epoch, const float *resid,
                                    float *out, int T, int K, int H, uint32_t *status,
                                    cudaStream_t s);

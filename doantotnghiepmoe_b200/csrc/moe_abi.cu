@@ -347,7 +347,7 @@ void free_handle(moe_handle *h) {
                   h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
                   h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles, h->d_flayers,
                   h->dtile_expert, h->dtile_row0, h->dtile_rows, h->n_dtiles,
-                  h->tok_cnt, h->fbar, h->phase_ts, h->perm_scratch};
+                  h->tok_cnt, h->fbar, h->phase_ts, h->perm_scratch, h->probe_flag};
   for (void *p : ptrs) cudaFree(p);
   cudaFreeHost(h->h_pin_in);
   cudaFreeHost(h->h_pin_out);
@@ -414,6 +414,7 @@ FusedArgs fused_args(moe_handle *h, int T) {
   f.contrib = h->contrib;
   f.tok_cnt = h->tok_cnt;
   f.status = h->status;
+  f.wait_cycles = h->wait_barrier_cycles;
   if (h->prof.on) {
     f.phase_ts = h->phase_ts;
     h->phase_pending = true;
@@ -634,6 +635,8 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && dalloc(&h->tok_cnt, T) == cudaSuccess && dalloc(&h->fbar, 1) == cudaSuccess;
   ok = ok && cudaMemset(h->tok_cnt, 0, T * sizeof(uint32_t)) == cudaSuccess;
   ok = ok && dalloc(&h->phase_ts, 16) == cudaSuccess;
+  ok = ok && dalloc(&h->probe_flag, 1) == cudaSuccess &&
+       cudaMemset(h->probe_flag, 0, sizeof(uint32_t)) == cudaSuccess;
   h->perm_scratch_words = permute_scratch_words((int)(T * K), (int)E);
   ok = ok && dalloc(&h->perm_scratch, h->perm_scratch_words) == cudaSuccess;
   h->flayers.assign(d.num_layers, FusedLayer{});
@@ -696,6 +699,38 @@ extern "C" moe_status moe_set_path(moe_handle *h, int path) {
   std::lock_guard<std::mutex> lock(h->mu);
   h->path = path;
   return MOE_OK;
+}
+
+extern "C" moe_status moe_set_wait_limit(moe_handle *h, uint64_t ns) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (ns == 0) {
+    h->wait_barrier_cycles = kDefaultBarrierWaitCycles;
+    h->wait_flag_cycles = kDefaultFlagWaitCycles;
+  } else {
+    // clock64() counts SM cycles: a bound in time becomes cycles at the
+    // maximum SM clock (at a lower clock the wait lasts longer, never less)
+    int khz = 0;
+    if (cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, h->device) != cudaSuccess || khz <= 0)
+      khz = 2000000;
+    const double cyc = (double)ns * (double)khz * 1e-6;
+    const long long c = cyc > 9e18 ? (long long)9e18 : std::max(1000LL, (long long)cyc);
+    h->wait_barrier_cycles = c;
+    h->wait_flag_cycles = c;
+  }
+  h->ep.P.wait_cycles = h->wait_flag_cycles;
+  drop_graphs(h);  // captured launches carry the old bound
+  return MOE_OK;
+}
+
+extern "C" moe_status moe_debug_wait_flag(moe_handle *h, void *stream) {
+  if (!h) return MOE_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(h->mu);
+  DeviceGuard g(h->device);
+  cudaStream_t s = pick(h, stream);
+  const cudaError_t e =
+      launch_wait_probe(h->probe_flag, 1, 1u, h->wait_flag_cycles, h->status, s);
+  return e == cudaSuccess ? MOE_OK : cuda_fail(h, e, "wait probe launch");
 }
 
 extern "C" moe_status moe_set_layer_q(moe_handle *h, int layer, const void *const *d_weights,

@@ -12,9 +12,13 @@
 // activations, contributions, the status word) lives in one file-scope
 // device array of kNoAllocScratchBytes.  The array is part of the loaded
 // module, so each GPU that loads this library holds it from load until the
-// process exits.  Its address is fetched once per device with
-// cudaGetSymbolAddress on the first call on that device (with that device
-// current); make that first call before any stream capture.  All calls share
+// process exits.  The call runs on the device that owns `stream` (the
+// current device for the legacy default stream), made current for the
+// duration of the call.  The array's address on that device is fetched once,
+// with cudaGetSymbolAddress on the first call there; make that first call
+// before any stream capture.  The address is cached for the life of the
+// process, so the entry point must not be used again on a device after
+// cudaDeviceReset() on it.  All calls share
 // the one array: calls whose work overlaps on the GPU (two streams, two host
 // threads) race on it and must be serialised by the caller.  The array keeps
 // the previous call's contents; the only state that must start from zero
@@ -35,6 +39,10 @@
 #include "kernels.h"
 
 namespace {
+
+// the GEMV kernels stage this many input rows of H (gate/up) or I (down)
+// floats in shared memory
+constexpr int kGemvStagedRows = 4;
 
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per GPU
 constexpr int kMaxDevices = 64;
@@ -78,7 +86,8 @@ extern "C" moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8
     return MOE_ERR_INVALID;
   }
   const moe_dims &d = *dims;
-  if (d.hidden <= 0 || d.intermediate <= 0 || d.num_experts <= 0 || d.num_experts > kMaxExperts ||
+  if (d.hidden <= 0 || d.intermediate <= 0 || d.hidden > (1 << 16) ||
+      d.intermediate > (1 << 16) || d.num_experts <= 0 || d.num_experts > kMaxExperts ||
       d.top_k <= 0 || d.top_k > kMaxTopK || d.top_k > d.num_experts || T < 0 ||
       (router_dtype != MOE_ROUTER_F32 && router_dtype != MOE_ROUTER_BF16) ||
       ((uintptr_t)d_scales & 3)) {
@@ -108,10 +117,43 @@ extern "C" moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8
            T, off, kNoAllocScratchBytes);
     return MOE_ERR_INVALID;
   }
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int prev = -1, dev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) {
     report(err_msg, err_len, "no usable current CUDA device");
     return MOE_ERR_CUDA;
+  }
+  dev = prev;
+  // a stream of another device: run there (its copy of the array)
+  if (s && cudaStreamGetDevice(s, &dev) != cudaSuccess) {
+    cudaGetLastError();
+    report(err_msg, err_len, "stream does not belong to a usable CUDA device");
+    return MOE_ERR_INVALID;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    report(err_msg, err_len, "device %d outside the supported range [0, %d)", dev, kMaxDevices);
+    return MOE_ERR_INVALID;
+  }
+  struct Restore {
+    int prev, dev;
+    ~Restore() {
+      if (prev != dev) cudaSetDevice(prev);
+    }
+  } restore{prev, dev};
+  if (dev != prev && cudaSetDevice(dev) != cudaSuccess) {
+    report(err_msg, err_len, "cannot make device %d current", dev);
+    return MOE_ERR_CUDA;
+  }
+  // The GEMV kernels stage their input rows in shared memory: a shape that
+  // would not fit is rejected here rather than failing at launch.
+  int smem_max = 0;
+  cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const size_t smem_need = sizeof(float) * kGemvStagedRows * std::max(H, I);
+  if (smem_max > 0 && smem_need > (size_t)smem_max) {
+    report(err_msg, err_len,
+           "hidden %zu / intermediate %zu need %zu bytes of shared memory per block, more "
+           "than the device's %d", H, I, smem_need, smem_max);
+    return MOE_ERR_INVALID;
   }
   unsigned char *base = nullptr;
   {
@@ -130,7 +172,6 @@ extern "C" moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8
     }
     base = static_cast<unsigned char *>(g_scratch_ptr[dev]);
   }
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   uint32_t *status = reinterpret_cast<uint32_t *>(base + o_status);
   auto at = [&](size_t o) { return base + o; };
 
@@ -171,6 +212,9 @@ extern "C" moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8
   pa.r_gate = reinterpret_cast<float *>(at(o_rgate));
   pa.r_pos = reinterpret_cast<int32_t *>(at(o_rpos));
   pa.status = status;
+  // pa.scratch stays null: launch_permute then sorts every route in one CTA,
+  // whatever their count, and never takes its multi-CTA path (which needs
+  // scratch of its own).
   if (e == cudaSuccess) e = launch_permute(pa, s);
   GemvArgs a{};
   a.H = (int)H;

@@ -162,6 +162,16 @@ class MoeLayerEngine:
     def last_launch_count(self) -> int:
         return int(lib().moe_last_launch_count(self._h))
 
+    def set_wait_limit(self, ns: int = 0):
+        """Bound of the device-side waits (grid barriers, expert-parallel flag
+        waits) in nanoseconds; 0 restores the defaults."""
+        self._check(lib().moe_set_wait_limit(self._h, int(ns)))
+
+    def debug_wait_flag(self, stream=None):
+        """Failure-path probe: a bounded wait on a device flag that nothing
+        sets; the next sync_status() raises MoeError(MOE_ERR_TIMEOUT)."""
+        self._check(lib().moe_debug_wait_flag(self._h, _stream(stream)))
+
     # -- expert parallelism (one process per GPU) -------------------------
     def ep_init(self, rank: int, nranks: int, unique_id: bytes, owner):
         owner = np.ascontiguousarray(owner, np.int32)

@@ -210,6 +210,22 @@ moe_status moe_host_free(void *p);
  * status word: MOE_OK, MOE_ERR_NONFINITE or MOE_ERR_TIMEOUT. */
 moe_status moe_sync_status(moe_handle *h, void *stream);
 
+/* Bound of the device-side waits of this handle's kernels: the grid barriers
+ * of the single-launch decode kernels and the expert-parallel flag waits, in
+ * nanoseconds at the maximum SM clock (0 restores the defaults, about 1 s and
+ * 2 s).  A wait that runs out records a timeout in the handle's status word,
+ * which moe_sync_status() returns as MOE_ERR_TIMEOUT; the kernel stops its
+ * work and returns, so the context stays usable.  The reference's engine
+ * trips its GPU circuit breaker on such an error (src/gpu.rs:534-550).  The
+ * mbarrier waits inside the tensor-core kernels keep their own bound. */
+moe_status moe_set_wait_limit(moe_handle *h, uint64_t ns);
+
+/* Failure-path probe (tests): one thread waits, with the handle's flag-wait
+ * bound, on a device word of the handle that nothing ever sets.  The wait
+ * runs out and the handle's status word records the timeout; nothing faults
+ * or traps.  Asynchronous on `stream` (NULL = the handle's stream). */
+moe_status moe_debug_wait_flag(moe_handle *h, void *stream);
+
 /* Number of kernel launches issued by the last layer/stack call. */
 int moe_last_launch_count(const moe_handle *h);
 
@@ -224,10 +240,14 @@ int moe_last_launch_count(const moe_handle *h);
  * Intermediates live in a fixed 8 MiB device array inside this library that
  * every GPU loading the library holds until the process exits; a call whose
  * T needs more returns MOE_ERR_INVALID with the reason in err_msg (optional
- * buffer).  The first call on each device looks the array up with that
- * device current, so make it before any stream capture.  Calls share the
- * array: calls that overlap on the GPU race on it.  The call synchronises
- * `stream` (NULL = legacy default stream) and returns MOE_ERR_NONFINITE like
+ * buffer).  The call runs on the device that owns `stream` (NULL = the
+ * legacy default stream of the current device).  The first call on each
+ * device looks the array up with that device current, so make it before any
+ * stream capture; the address is kept for the process, so do not call this
+ * again on a device after cudaDeviceReset() on it.  Calls share the array:
+ * calls that overlap on the GPU race on it.  Shapes whose GEMV staging does
+ * not fit in shared memory are rejected with MOE_ERR_INVALID.  The call
+ * synchronises `stream` and returns MOE_ERR_NONFINITE like
  * moe_layer_forward_host() when an input or output is not finite. */
 moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8_t *d_experts,
                                      const float *d_scales, const void *d_router,

@@ -51,3 +51,21 @@ def test_product_never_loads_the_oracle():
             if f.endswith((".py", ".cu", ".cuh", ".h", ".cpp")):
                 text = open(os.path.join(dirpath, f)).read()
                 assert not pat.search(text), f
+
+
+def test_noalloc_rejects_before_touching_a_gpu():
+    """moe_layer_forward_noalloc checks its arguments and the fixed scratch
+    size on the host, before any CUDA call: T = 85 at the OLMoE shape needs
+    more than the 8 MiB array, and H above 65536 is out of range."""
+    fake = ctypes.c_void_p(256)  # never dereferenced: the call returns first
+    err = ctypes.create_string_buffer(256)
+    dims = _lib.MoeDims(2048, 1024, 64, 8, 0, 85, 1)
+    st = M.lib().moe_layer_forward_noalloc(ctypes.byref(dims), fake, fake, fake,
+                                           _lib.MOE_ROUTER_F32, fake, None, fake, 85, None,
+                                           err, len(err))
+    assert st == _lib.MOE_ERR_INVALID and b"scratch" in err.value
+    dims = _lib.MoeDims(65537, 16, 4, 2, 0, 1, 1)
+    st = M.lib().moe_layer_forward_noalloc(ctypes.byref(dims), fake, fake, fake,
+                                           _lib.MOE_ROUTER_F32, fake, None, fake, 1, None,
+                                           err, len(err))
+    assert st == _lib.MOE_ERR_INVALID
