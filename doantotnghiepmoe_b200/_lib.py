@@ -98,6 +98,7 @@ SIGNATURES = {
     "moe_set_graphs": (I32, [P, I32]),
     "moe_set_wait_limit": (I32, [P, U64]),
     "moe_debug_wait_flag": (I32, [P, P]),
+    "moe_debug_stream_read": (I32, [P, SZ, P, P]),
 }
 
 _lib = None

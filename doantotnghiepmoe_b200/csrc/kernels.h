@@ -213,4 +213,8 @@ cudaError_t launch_synth_expert(uint64_t seed, int layer, int expert, int H, int
 // expected == null).  Used by the parity tests.
 cudaError_t launch_expf_eval(uint32_t bits_lo, uint32_t count, float *out, cudaStream_t s);
 
+// Read `bytes` (a multiple of 16, 16-byte aligned) once with 16-byte loads.
+cudaError_t launch_stream_read(const void *buf, size_t bytes, uint32_t *sink, int sm_count,
+                               cudaStream_t s);
+
 }  // namespace moe

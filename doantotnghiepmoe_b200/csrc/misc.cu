@@ -1,5 +1,7 @@
 // Small kernels around the expert GEMV/GEMM: slot-ordered combine, RMSNorm,
 // the seeded synthetic-weight generator and the expf evaluation hook.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -146,6 +148,28 @@ __global__ void expf_eval_kernel(uint32_t lo, uint32_t count, float *out) {
     out[i] = expf_ref(__uint_as_float(lo + i));
 }
 
+// A plain read of a buffer with 16-byte non-temporal loads, eight in flight
+// per thread: the bandwidth ceiling of one launch over the same byte count
+// as a decode layer, timed by the benchmark beside the layer.
+__global__ void __launch_bounds__(256) stream_read_kernel(const uint4 *__restrict__ p, size_t n,
+                                                          uint32_t *sink) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  uint32_t acc = 0;
+  for (; i + 7 * stride < n; i += 8 * stride) {
+    uint4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = __ldcs(p + i + k * stride);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc ^= v[k].x ^ v[k].y ^ v[k].z ^ v[k].w;
+  }
+  for (; i < n; i += stride) {
+    const uint4 v = __ldcs(p + i);
+    acc ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (acc == 0x9e3779b9u) *sink = acc;  // keeps the loads; practically never written
+}
+
 }  // namespace
 
 cudaError_t launch_combine(const float *contrib, const float *resid, float *out, int T, int K,
@@ -179,6 +203,14 @@ cudaError_t launch_synth_expert(uint64_t seed, int layer, int expert, int H, int
 
 cudaError_t launch_expf_eval(uint32_t bits_lo, uint32_t count, float *out, cudaStream_t s) {
   expf_eval_kernel<<<148 * 8, 256, 0, s>>>(bits_lo, count, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_stream_read(const void *buf, size_t bytes, uint32_t *sink, int sm_count,
+                               cudaStream_t s) {
+  const size_t n = bytes / 16;
+  const int grid = std::max(1, std::min<int>(sm_count * 8, (int)((n + 255) / 256)));
+  stream_read_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const uint4 *>(buf), n, sink);
   return cudaGetLastError();
 }
 

@@ -1351,6 +1351,16 @@ extern "C" moe_status moe_debug_expf(uint32_t bits_lo, uint32_t count, float *d_
   return e == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
+extern "C" moe_status moe_debug_stream_read(const void *d_buf, size_t bytes, uint32_t *d_sink,
+                                            void *stream) {
+  if (!d_buf || !d_sink || bytes % 16 || ((uintptr_t)d_buf & 15)) return MOE_ERR_INVALID;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MOE_ERR_CUDA;
+  const cudaError_t e = launch_stream_read(d_buf, bytes, d_sink, sm_count_of(dev),
+                                           reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
 extern "C" moe_status moe_profile_enable(moe_handle *h, int enable) {
   if (!h) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);

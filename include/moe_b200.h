@@ -348,6 +348,14 @@ moe_status moe_synth_expert(uint64_t seed, int layer, int expert, int hidden, in
  * bit patterns starting at bits_lo (device output). */
 moe_status moe_debug_expf(uint32_t bits_lo, uint32_t count, float *d_out, void *stream);
 
+/* Read `bytes` of device memory once (16-byte loads, eight in flight per
+ * thread, a few CTAs per SM): the bandwidth ceiling of a single launch over
+ * a given byte count, which the benchmark times beside the decode layer.
+ * d_buf 16-byte aligned, bytes a multiple of 16; d_sink is one device word
+ * the kernel almost never writes.  Asynchronous on `stream`. */
+moe_status moe_debug_stream_read(const void *d_buf, size_t bytes, uint32_t *d_sink,
+                                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif
