@@ -409,7 +409,7 @@ def measure_decode_c0(M, args, local) -> dict:
     # the ceiling: the same byte count read by one plain launch, rotating over
     # buffers that together exceed L2 (back to back, like the layer steps)
     nbuf = 8
-    nb = (alg + 15) // 16 * 16
+    nb = (int(alg) + 15) // 16 * 16
     bufs = [torch.empty(nb, dtype=torch.uint8, device="cuda") for _ in range(nbuf)]
     sink = torch.zeros(1, dtype=torch.int32, device="cuda")
     L = M.lib()

@@ -12,6 +12,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "digits.cuh"
 #include "kernels.h"
 
 namespace moe {
@@ -49,21 +50,13 @@ __global__ void pack_kernel(const float *__restrict__ x, const int32_t *__restri
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+  const float s = digits::row_scale(amax);
   const float inv = 1.0f / s;
   uint8_t *row = send + (size_t)warp * ep_row_bytes(H);
   for (int c = lane * 4; c < H; c += 128) {
     const float4 v = *reinterpret_cast<const float4 *>(xr + c);
-    const float in[4] = {v.x, v.y, v.z, v.w};
-    uint32_t p1 = 0, p2 = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float q = in[k] * inv;
-      const float a1 = fminf(fmaxf(rintf(q), -127.0f), 127.0f);
-      const float a2 = fminf(fmaxf(rintf((q - a1) * 254.0f), -127.0f), 127.0f);
-      p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
-      p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
-    }
+    uint32_t p2;
+    const uint32_t p1 = digits::split4(v.x, v.y, v.z, v.w, inv, p2);
     *reinterpret_cast<uint32_t *>(row + c) = p1;
     *reinterpret_cast<uint32_t *>(row + H + c) = p2;
   }
@@ -349,7 +342,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+      const float s = digits::row_scale(amax);
       const float inv = 1.0f / s;
       // 16 elements per lane per pass: 16-byte stores, 512 bytes per warp
       // instruction on the link (H is a multiple of 16)
@@ -358,18 +351,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
 #pragma unroll
         for (int w4 = 0; w4 < 4; ++w4) {
           const float4 v = *reinterpret_cast<const float4 *>(xr + c + 4 * w4);
-          const float in[4] = {v.x, v.y, v.z, v.w};
-          uint32_t b1 = 0, b2 = 0;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float qv = in[k] * inv;
-            const float a1 = fminf(fmaxf(rintf(qv), -127.0f), 127.0f);
-            const float a2 = fminf(fmaxf(rintf((qv - a1) * 254.0f), -127.0f), 127.0f);
-            b1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
-            b2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
-          }
-          p1[w4] = b1;
-          p2[w4] = b2;
+          p1[w4] = digits::split4(v.x, v.y, v.z, v.w, inv, p2[w4]);
         }
         const uint4 v1 = make_uint4(p1[0], p1[1], p1[2], p1[3]);
         const uint4 v2 = make_uint4(p2[0], p2[1], p2[2], p2[3]);

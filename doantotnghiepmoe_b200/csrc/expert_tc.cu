@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "expert_tc.h"
+#include "digits.cuh"
 #include "tma_ptx.cuh"
 
 namespace moe {
@@ -317,11 +318,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
           if (c < nr) {
             const int r = r0 + c;
             const float s1 = tab.s1[c], s2 = tab.s2[c];
-            const float gd = fmaf(s1, (float)v[0][j], s2 * (float)v[1][j]);
-            const float ud = fmaf(s1, (float)v[2][j], s2 * (float)v[3][j]);
-            const float gg = gd * sg, uu = ud * su;
             // tolerance path: the hardware exp (the GEMV path keeps libm's)
-            act = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
+            act = digits::swiglu(v[0][j], v[1][j], v[2][j], v[3][j], s1, s2, sg, su);
             if (i < a.I) a.act[(size_t)r * a.I + i] = act;
           }
           mx[j] = fabsf(act);
@@ -390,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
         for (int jj = 0; jj < 16; ++jj) {
           const int c = c0 + jj;
           if (c < nr && j < a.H) {
-            const float y = fmaf(tab.s1[c], (float)v[0][jj], tab.s2[c] * (float)v[1][jj]) * sd;
+            const float y = digits::down(v[0][jj], v[1][jj], tab.s1[c], tab.s2[c], sd);
             bad |= !is_finite_f(y);
             // expert parallelism: the row goes straight to the source rank's
             // contribution buffer (peer memory over NVLink)
@@ -611,11 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c < nr) {
             const int r = r0 + c;
             const float s1 = tab.s1[c], s2 = tab.s2[c];
-            const float gd = fmaf(s1, (float)v[0][jj], s2 * (float)v[1][jj]);
-            const float ud = fmaf(s1, (float)v[2][jj], s2 * (float)v[3][jj]);
-            const float gg = gd * sg, uu = ud * su;
-            // tolerance path: the hardware exp (the GEMV path keeps libm's)
-            act = __fdividef(gg, 1.0f + __expf(-gg)) * uu;
+act = digits::swiglu(v[0][jj], v[1][jj], v[2][jj], v[3][jj], s1, s2, sg, su);
             if (i < I) a.act[(size_t)r * I + i] = act;
           }
           mx[jj] = fabsf(act);
@@ -685,7 +679,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int jj = 0; jj < 16; ++jj) {
           const int c = c0 + jj;
           if (c < nr && jr < a.H) {
-            const float y = fmaf(tab.s1[c], (float)v[0][jj], tab.s2[c] * (float)v[1][jj]) * sd;
+            const float y = digits::down(v[0][jj], v[1][jj], tab.s1[c], tab.s2[c], sd);
             bad |= !is_finite_f(y);
             float *dst = a.r_rank ? a.peer_contrib[tab.rank[c]] : a.contrib;
             dst[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + jr] = __fmul_rn(tab.gate[c], y);
@@ -765,23 +759,15 @@ __global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   }
-  const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+  const float s = digits::row_scale(amax);
   const float inv = 1.0f / s;
   int8_t *q1 = q + (size_t)warp * n;
   int8_t *q2 = q + plane + (size_t)warp * n;
 #pragma unroll 4
   for (int c = lane * 4; c < n; c += 128) {
     const float4 v = *reinterpret_cast<const float4 *>(x + c);
-    const float in[4] = {v.x, v.y, v.z, v.w};
-    uint32_t p1 = 0, p2 = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float t = in[k] * inv;
-      const float a1 = fminf(fmaxf(rintf(t), -127.0f), 127.0f);
-      const float a2 = fminf(fmaxf(rintf((t - a1) * 254.0f), -127.0f), 127.0f);
-      p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
-      p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
-    }
+    uint32_t p2;
+    const uint32_t p1 = digits::split4(v.x, v.y, v.z, v.w, inv, p2);
     *reinterpret_cast<uint32_t *>(q1 + c) = p1;
     *reinterpret_cast<uint32_t *>(q2 + c) = p2;
   }
@@ -801,18 +787,7 @@ __global__ void quantize_rows_kernel(const float *__restrict__ src, const int32_
 // digit store is 16 bytes.
 constexpr int kQtThreads = 128;
 __device__ __forceinline__ uint32_t digits4(const float4 v, float inv, uint32_t &hi) {
-  const float in[4] = {v.x, v.y, v.z, v.w};
-  uint32_t p1 = 0, p2 = 0;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float u = in[k] * inv;
-    const float a1 = fminf(fmaxf(rintf(u), -127.0f), 127.0f);
-    const float a2 = fminf(fmaxf(rintf((u - a1) * 254.0f), -127.0f), 127.0f);
-    p1 |= (uint32_t)(uint8_t)(int8_t)(int)a1 << (8 * k);
-    p2 |= (uint32_t)(uint8_t)(int8_t)(int)a2 << (8 * k);
-  }
-  hi = p2;
-  return p1;
+  return digits::split4(v.x, v.y, v.z, v.w, inv, hi);
 }
 
 __global__ void __launch_bounds__(kQtThreads, 4) quantize_tokens_kernel(
@@ -839,7 +814,7 @@ __global__ void __launch_bounds__(kQtThreads, 4) quantize_tokens_kernel(
   __syncthreads();
 #pragma unroll
   for (int w = 0; w < kQtThreads / 32; ++w) amax = fmaxf(amax, wmax[w]);
-  const float s = amax > 0.0f ? amax / 127.0f : 1.0f;
+  const float s = digits::row_scale(amax);
   const float inv = 1.0f / s;
   int pos[kMaxTopK];
 #pragma unroll
