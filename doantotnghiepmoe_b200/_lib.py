@@ -27,6 +27,7 @@ MOE_ROUTER_F32, MOE_ROUTER_BF16 = 0, 1
 MOE_ROUTE_SOFTMAX_TOPK, MOE_ROUTE_TOPK_SOFTMAX = 0, 1
 MOE_PATH_AUTO, MOE_PATH_GEMV, MOE_PATH_TENSOR, MOE_PATH_GEMV_PHASED = 0, 1, 2, 3
 MOE_PATH_GEMV_FUSED = 4
+MOE_PATH_DIGITS = 5
 MOE_QUANT_INT8, MOE_QUANT_INT4 = 0, 1
 
 # Every symbol the header declares, with (restype, argtypes).

@@ -147,6 +147,40 @@ bool fused_decode_supported(int T, int H, int I, int E, int K);
 cudaError_t launch_fused_decode(const FusedArgs &a, int vec, int sm_count, uint32_t *bar,
                                 cudaStream_t s);
 
+// Digit decode (decode_digits.cu): a whole layer, or a stack of layers with
+// RMSNorm + residual, in one cooperative launch for decode batches, on the
+// tolerance path (two-digit int8 activations, dp4a; results bit-identical to
+// the tensor-core path, routing bit-identical to the CPU reference).  Every
+// layer INT8 with 16-byte aligned expert rows (FusedLayer::prefetch_ok);
+// 16-byte aligned f32 inputs.
+struct DigitArgs {
+  int T, H, I, E, K, norm, route_mode;
+  int n_layers;              // layers in this launch
+  int stacked;               // 1: x <- x + MoE(RMSNorm(x)) per layer, x in `out`
+  const FusedLayer *layers;  // device array [n_layers]
+  const float *h_in;         // single layer: MoE input [T, H]
+  const float *resid;        // single layer: residual [T, H] or null
+  float *out;                // single layer: output; stacked: x, updated in place
+  float eps;
+  float *logits;             // [T, E]
+  uint32_t *ids;             // [T, K] routing of the latest layer
+  float *gates;              // [T, K]
+  uint32_t *ids_out;         // optional copies of the routing (single layer)
+  float *gates_out;
+  int8_t *xq;                // [T][2][H] token digit planes
+  float *xs1, *xs2;          // [T] token scales s, s / 254
+  float *act;                // [T*K, I] activations (token-major route order)
+  float *contrib;            // [T, K, H] gate * y (T > 1)
+  uint32_t *bar;             // grid barrier counter (zeroed by the launcher)
+  uint32_t *status;
+  long long wait_cycles;     // bound of each grid-barrier wait (SM clock cycles)
+  int router_async;          // routers of every layer are 16-byte aligned f32 rows
+  int prefetch_down;         // prefetch the down rows into L2 during gate/up
+  unsigned long long *phase_ts;  // optional [5] phase timestamps (profiling)
+};
+bool digit_decode_supported(int T, int H, int I, int E, int K);
+cudaError_t launch_digit_decode(const DigitArgs &a, int sm_count, cudaStream_t s);
+
 // Expert parallelism (ep.cu): one route on the wire = two int8 digit planes
 // of its token row + {s1, s2, gate, destination-local expert id}.
 __host__ __device__ inline size_t ep_row_bytes(int H) { return (size_t)2 * H + 16; }

@@ -378,9 +378,58 @@ bool use_tensor_path(const moe_handle *h, const LayerSlot &L, int T, const float
   const bool avail = h->tc_ok && L.tc_ok && ((uintptr_t)d_h & 15) == 0;
   if (h->path == MOE_PATH_TENSOR) return avail;
   if (h->path == MOE_PATH_GEMV || h->path == MOE_PATH_GEMV_PHASED ||
-      h->path == MOE_PATH_GEMV_FUSED)
+      h->path == MOE_PATH_GEMV_FUSED || h->path == MOE_PATH_DIGITS)
     return false;
   return avail && T >= kTcMinTokens;
+}
+
+// The digit decode launch can run layers [first, first + n) at T tokens:
+// INT8 layers with 16-byte aligned rows, 16-byte aligned f32 activations.
+bool digits_available(const moe_handle *h, int T, int first, int n, const void *d_x,
+                      const void *d_resid) {
+  if (((uintptr_t)d_x & 15) || ((uintptr_t)d_resid & 15)) return false;
+  if (!digit_decode_supported(T, h->d.hidden, h->d.intermediate, h->d.num_experts, h->d.top_k))
+    return false;
+  for (int l = first; l < first + n; ++l)
+    if (h->flayers[l].int4 || !h->flayers[l].prefetch_ok) return false;
+  return true;
+}
+
+bool use_digits(const moe_handle *h, int T, int first, int n, const void *d_x,
+                const void *d_resid) {
+  if (h->path == MOE_PATH_DIGITS) return true;  // availability is checked by the caller
+  return h->path == MOE_PATH_AUTO && T < kTcMinTokens &&
+         digits_available(h, T, first, n, d_x, d_resid);
+}
+
+DigitArgs digit_args(moe_handle *h, int T) {
+  DigitArgs a{};
+  a.T = T;
+  a.H = h->d.hidden;
+  a.I = h->d.intermediate;
+  a.E = h->d.num_experts;
+  a.K = h->d.top_k;
+  a.norm = h->d.norm_topk_prob;
+  a.route_mode = h->route_mode;
+  a.logits = h->logits;
+  a.ids = h->ids;
+  a.gates = h->gates;
+  a.xq = h->xq;
+  a.xs1 = h->xs1;
+  a.xs2 = h->xs2;
+  a.act = h->act;
+  a.contrib = h->contrib;
+  a.bar = h->fbar;
+  a.status = h->status;
+  a.wait_cycles = h->wait_barrier_cycles;
+  // the down rows of a single-token launch (<= K experts) fit in L2 beside
+  // the gate/up stream
+  a.prefetch_down = T == 1 && (size_t)h->d.top_k * h->d.hidden * h->d.intermediate <= (48u << 20);
+  if (h->prof.on) {
+    a.phase_ts = h->phase_ts;
+    h->phase_pending = true;
+  }
+  return a;
 }
 
 bool use_fused(const moe_handle *h, int T) {
@@ -502,6 +551,35 @@ moe_status layer_forward_locked(moe_handle *h, int layer, const float *d_h, cons
     set_err(h->err, "tensor-core path unavailable for layer %d (needs the packed expert layout, "
             "H and I multiples of 16, 16-byte aligned inputs)", layer);
     return MOE_ERR_STATE;
+  }
+  if (use_digits(h, T, layer, 1, d_h, d_resid)) {
+    if (!digits_available(h, T, layer, 1, d_h, d_resid)) {
+      set_err(h->err, "digit decode path unavailable for layer %d at T=%d (needs INT8 experts "
+              "with 16-byte aligned rows, H and I multiples of 16 up to 2048, T*K <= %d, "
+              "16-byte aligned inputs)", layer, T, kFusedMaxRoutes);
+      return MOE_ERR_STATE;
+    }
+    DigitArgs a = digit_args(h, T);
+    a.n_layers = 1;
+    a.stacked = 0;
+    a.layers = h->d_flayers + layer;
+    a.h_in = d_h;
+    a.resid = d_resid;
+    a.out = d_out;
+    a.ids_out = d_ids;
+    a.gates_out = d_gates;
+    if (!d_ids || !d_gates) a.ids_out = nullptr;
+    a.router_async = h->layer_async[layer];
+    cudaEvent_t p0 = h->prof.begin(s);
+    cudaError_t e = launch_digit_decode(a, h->sm_count, s);
+    h->prof.end("digit_decode", p0, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "digit decode launch");
+    h->last_launches += 1;
+    if (d_ids && !d_gates) cudaMemcpyAsync(d_ids, h->ids, (size_t)T * h->d.top_k * 4,
+                                           cudaMemcpyDeviceToDevice, s);
+    if (d_gates && !d_ids) cudaMemcpyAsync(d_gates, h->gates, (size_t)T * h->d.top_k * 4,
+                                           cudaMemcpyDeviceToDevice, s);
+    return MOE_OK;
   }
   if (!use_tensor_path(h, L, T, d_h) && use_fused(h, T)) {
     FusedArgs f = fused_args(h, T);
@@ -695,7 +773,7 @@ extern "C" moe_status moe_set_route_mode(moe_handle *h, int mode) {
 }
 
 extern "C" moe_status moe_set_path(moe_handle *h, int path) {
-  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_GEMV_FUSED) return MOE_ERR_INVALID;
+  if (!h || path < MOE_PATH_AUTO || path > MOE_PATH_DIGITS) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
   h->path = path;
   return MOE_OK;
@@ -1154,6 +1232,30 @@ moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, fl
   bool vec_all = ((uintptr_t)d_x & 15) == 0;
   for (int l = first_layer; l < first_layer + n_layers; ++l) vec_all = vec_all && h->layer_vec[l];
   const int quant = layers_quant(h, first_layer, n_layers);
+  if (use_digits(h, T, first_layer, n_layers, d_x, nullptr)) {
+    if (!digits_available(h, T, first_layer, n_layers, d_x, nullptr)) {
+      set_err(h->err, "digit decode path unavailable for layers [%d, %d) at T=%d (needs INT8 "
+              "experts with 16-byte aligned rows, H and I multiples of 16 up to 2048, "
+              "T*K <= %d, a 16-byte aligned x)", first_layer, first_layer + n_layers, T,
+              kFusedMaxRoutes);
+      return MOE_ERR_STATE;
+    }
+    DigitArgs a = digit_args(h, T);
+    a.n_layers = n_layers;
+    a.stacked = 1;
+    a.layers = h->d_flayers + first_layer;
+    a.out = d_x;
+    a.eps = rms_eps;
+    a.router_async = 1;
+    for (int l = first_layer; l < first_layer + n_layers; ++l)
+      a.router_async = a.router_async && h->layer_async[l];
+    cudaEvent_t p0 = h->prof.begin(s);
+    cudaError_t e = launch_digit_decode(a, h->sm_count, s);
+    h->prof.end("digit_decode", p0, s);
+    if (e != cudaSuccess) return cuda_fail(h, e, "digit decode launch");
+    h->last_launches += 1;
+    return MOE_OK;
+  }
   if (h->path != MOE_PATH_TENSOR && use_fused(h, T) && quant >= 0) {
     FusedArgs f = fused_args(h, T);
     f.n_layers = n_layers;

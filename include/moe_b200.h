@@ -107,12 +107,20 @@ enum {
 
 /* Expert GEMM back-end for a layer call. */
 enum {
-  MOE_PATH_AUTO = 0,        /* GEMV for small T, tensor cores for large T */
+  MOE_PATH_AUTO = 0,        /* the digit decode launch for T < 128 when the layers allow it
+                               (INT8, 16-byte aligned rows), else the exact GEMV; tensor
+                               cores from T = 128 */
   MOE_PATH_GEMV = 1,        /* exact-order INT8 GEMV (bit-identical to the CPU path); for
                                small T the whole layer runs as one cooperative launch */
   MOE_PATH_TENSOR = 2,      /* tcgen05 grouped GEMM (within the 1e-3 tolerance) */
   MOE_PATH_GEMV_PHASED = 3, /* exact-order GEMV, one launch per phase (no fusion) */
-  MOE_PATH_GEMV_FUSED = 4   /* same as MOE_PATH_GEMV: the register-prefetch single launch */
+  MOE_PATH_GEMV_FUSED = 4,  /* same as MOE_PATH_GEMV: the register-prefetch single launch */
+  MOE_PATH_DIGITS = 5       /* decode batches (T*K <= 1024) in one cooperative launch per
+                               layer or stack: routing bit-identical to the CPU path, experts
+                               on two-digit int8 activations with exact int32 dot products
+                               (dp4a), outputs bit-identical to MOE_PATH_TENSOR and within
+                               the 1e-3 tolerance; INT8 layers with 16-byte aligned experts,
+                               H and I multiples of 16 (<= 2048) */
 };
 
 moe_status moe_create(int device, const moe_dims *dims, moe_handle **out);

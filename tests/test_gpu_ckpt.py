@@ -63,6 +63,7 @@ def test_loaded_layers_bit_exact(tmp_path):
     write_safetensors(tmp_path / "model-00001.safetensors", layer_tensors(1, lw1, "BF16"))
     ck = M.Checkpoint(str(tmp_path))
     eng = M.MoeLayerEngine(M.MoeConfig(H, I, E, K, False, 6, 3))
+    eng.set_path(_lib.MOE_PATH_GEMV)
     eng.load_layer(ck, 0)
     eng.load_layer(ck, 1)                      # router kept as BF16
     eng.load_layer(ck, 1, layer=2, keep_bf16=False)  # widened to f32: the same values

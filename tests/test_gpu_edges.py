@@ -23,7 +23,7 @@ H, I, E, K = 256, 128, 16, 4
 
 
 @pytest.mark.parametrize("path", [_lib.MOE_PATH_AUTO, _lib.MOE_PATH_GEMV,
-                                  _lib.MOE_PATH_GEMV_PHASED,
+                                  _lib.MOE_PATH_GEMV_PHASED, _lib.MOE_PATH_DIGITS,
                                   _lib.MOE_PATH_TENSOR])
 def test_empty_batch_is_a_no_op(path):
     lw = O.synth_layer(231, 0, H, I, E, K, False)

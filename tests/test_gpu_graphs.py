@@ -20,7 +20,8 @@ def bits(a):
 
 
 @pytest.mark.parametrize("path,T", [(_lib.MOE_PATH_TENSOR, 256), (_lib.MOE_PATH_GEMV, 3),
-                                    (_lib.MOE_PATH_GEMV_PHASED, 40)])
+                                    (_lib.MOE_PATH_GEMV_PHASED, 40), (_lib.MOE_PATH_DIGITS, 3),
+                                    (_lib.MOE_PATH_DIGITS, 1)])
 def test_replay_equals_direct(path, T):
     H, I, E, K = 512, 256, 32, 4
     lw = O.synth_layer(501, 0, H, I, E, K, True)
@@ -43,7 +44,7 @@ def test_replay_equals_direct(path, T):
         d = out.cpu().numpy()
         assert np.array_equal(bits(g), bits(d)), rep
         ref = O.layer_forward(lw, h)
-        if path == _lib.MOE_PATH_TENSOR:
+        if path in (_lib.MOE_PATH_TENSOR, _lib.MOE_PATH_DIGITS):
             assert helpers.rel_err(g, ref.out) < 1e-3
         else:
             assert np.array_equal(bits(g), bits(ref.out))
@@ -53,6 +54,7 @@ def test_replay_follows_new_weights_and_stacks():
     H, I, E, K, T = 512, 256, 16, 4, 2
     layers = [O.synth_layer(520 + l, 0, H, I, E, K, False) for l in range(2)]
     eng = M.MoeLayerEngine(M.MoeConfig(H, I, E, K, False, T, 1))
+    eng.set_path(_lib.MOE_PATH_GEMV)
     x0 = O.synth_hidden(530, T, H)
     hd = torch.from_numpy(x0).cuda()
     out = torch.empty_like(hd)
@@ -67,6 +69,7 @@ def test_replay_follows_new_weights_and_stacks():
         assert np.array_equal(bits(out.cpu().numpy()), bits(O.layer_forward(lw, x0).out))
     # a two-layer stack replayed twice from the same input
     eng2 = M.MoeLayerEngine(M.MoeConfig(H, I, E, K, False, T, 2))
+    eng2.set_path(_lib.MOE_PATH_GEMV)
     for l, t in enumerate(keep):
         eng2.set_layer_packed(l, *t)
     ref_x, _, _ = O.stack_forward(layers, x0)

@@ -21,9 +21,12 @@ from doantotnghiepmoe_b200 import _lib  # noqa: E402
 TOL = 1e-3
 
 
-def engine_for(lw, max_tokens, num_layers=1):
+def engine_for(lw, max_tokens, num_layers=1, path=_lib.MOE_PATH_GEMV):
+    """An engine on the exact path by default: these tests compare bits."""
     cfg = M.MoeConfig(lw.H, lw.I, lw.E, lw.K, lw.norm_topk_prob, max_tokens, num_layers)
-    return M.MoeLayerEngine(cfg)
+    eng = M.MoeLayerEngine(cfg)
+    eng.set_path(path)
+    return eng
 
 
 def bits(a):
@@ -217,6 +220,7 @@ def test_stacked_decode_bit_exact():
     ref_x, ref_ids, _ = O.stack_forward(layers, x0)
     cfg = M.MoeConfig(2048, 1024, 64, 8, False, 8, 4)
     eng = M.MoeLayerEngine(cfg)
+    eng.set_path(_lib.MOE_PATH_GEMV)
     keep = []
     for l, lw in enumerate(layers):
         ex, sc, rt = helpers.to_device(lw)
@@ -251,7 +255,7 @@ def test_host_buffers_pinned_and_staged():
     T = 300
     h = O.synth_hidden(43, T, 2048)
     resid = O.synth_hidden(44, T, 2048)
-    eng = engine_for(lw, T)
+    eng = engine_for(lw, T, path=_lib.MOE_PATH_AUTO)
     ex, sc, rt = helpers.to_device(lw)
     eng.set_layer_packed(0, ex, sc, rt)
     hd, rd = torch.from_numpy(h).cuda(), torch.from_numpy(resid).cuda()
