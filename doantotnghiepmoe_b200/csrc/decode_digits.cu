@@ -36,8 +36,9 @@
 //      CTA digitises the activation rows of its experts' routes and writes
 //      gate * y; a barrier, then the slot-ordered combine.
 //   -- grid barrier before the next stacked layer --
-// Every barrier wait is bounded (FusedArgs-style wait_cycles); on expiry the
-// CTA records kStatusTimeout and returns.
+// Every barrier wait is bounded (DigitArgs::wait_cycles); on expiry the CTA
+// records kStatusTimeout and stops.  The barrier counters reset themselves at
+// the end of each launch.
 #include <algorithm>
 
 #include "common.cuh"
@@ -55,25 +56,39 @@ constexpr int kRTE = 4;          // router task: experts
 constexpr int kGR = 16;          // routes whose digit planes are staged at once
 constexpr int kMaxChunks = 4;    // 16-byte chunks per lane of a row (rows <= 2048 bytes)
 
+constexpr int kGateW = 4;        // gate/up split: cost of a row pair = routes + kGateW
+constexpr int kDownW = 3;        // down split: cost of an output row = routes + kDownW
+
 struct DTables {
-  int32_t seg_off[kMaxExperts + 1];
-  int32_t active[kMaxExperts];
-  int32_t run[kMaxExperts];
+  int32_t run[kMaxExperts];               // counting-sort scratch
+  int32_t act_e[kMaxExperts];             // active experts, ascending id
+  int32_t act_r0[kMaxExperts + 1];        // routes of active a: [act_r0[a], act_r0[a + 1])
+  int32_t cost_g[kMaxExperts + 1];        // gate/up cost prefix over the active experts
+  int32_t cost_d[kMaxExperts + 1];        // down cost prefix
   int32_t n_active;
-  int32_t r_token[kFusedMaxRoutes];
+  int32_t r_token[kFusedMaxRoutes];       // sorted route -> token, slot, gate
   int32_t r_slot[kFusedMaxRoutes];
   float r_gate[kFusedMaxRoutes];
-  uint32_t ids[kFusedMaxRoutes];   // token-major routing of the current layer
+  uint32_t ids[kFusedMaxRoutes];          // token-major routing of the current layer
   float gates[kFusedMaxRoutes];
-  int32_t wcnt[kDW][kMaxExperts];
+  const int8_t *wp[kMaxExperts];          // the layer's expert pointers
+  const float *sp[kMaxExperts];
+  union {
+    int32_t wcnt[kDW][kMaxExperts];       // tables: per-warp counts
+    struct {
+      uint32_t key[kDW][kMaxExperts];     // top-k: total-order keys of a warp's token
+      float ex[kDW][kMaxExperts];         // softmax numerators
+    } s;
+  } u;
+  float sel_v[kDW][kMaxTopK];
+  uint32_t sel_i[kDW][kMaxTopK];
   float s1[kMaxTopK > kGR ? kMaxTopK : kGR];  // scales of the staged digit rows
   float s2[kMaxTopK > kGR ? kMaxTopK : kGR];
   float inv[kRTT];                            // RMSNorm factors of the staged tokens
 };
 
 constexpr size_t align128(size_t n) { return (n + 127) & ~size_t(127); }
-constexpr size_t kSelOff = align128(sizeof(DTables));
-constexpr size_t kStageOff = align128(kSelOff + kDW * sizeof(SelectScratch));
+constexpr size_t kStageOff = align128(sizeof(DTables));
 
 __device__ __forceinline__ bool grid_sync(uint32_t *bar, uint32_t target, uint32_t *status,
                                           long long limit) {
@@ -84,13 +99,15 @@ __device__ __forceinline__ bool grid_sync(uint32_t *bar, uint32_t target, uint32
     atomicAdd(bar, 1u);
     const long long t0 = clock64();
     int good = 1;
-    while (*(volatile uint32_t *)bar < target) {
+    // poll without sleeping for the first few microseconds (the usual wait
+    // is one phase's tail), then back off
+    for (int it = 0; *(volatile uint32_t *)bar < target; ++it) {
       if (clock64() - t0 > limit) {
         good = 0;
         set_status(status, kStatusTimeout);
         break;
       }
-      __nanosleep(32);
+      if (it > 4096) __nanosleep(64);
     }
     __threadfence();
     ok = good;
@@ -249,9 +266,11 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
         if (!is_finite_f(logit)) set_status(a.status, kStatusNonFinite);
       }
     }
-    // the token rows' digit planes, once per token (expert group 0)
-    if (e0 == 0 && warp < nt) {
-      const float *x = stage + (size_t)warp * H;
+    // the token rows' digit planes, once per token (expert group 0), on the
+    // warps above the ones running the dot (token r on warp kDW - 1 - r)
+    if (e0 == 0 && kDW - 1 - warp < nt) {
+      const int r = kDW - 1 - warp;
+      const float *x = stage + (size_t)r * H;
       float amax = 0.0f;
       for (int c = lane * 4; c < H; c += 128) {
         const float4 v = *reinterpret_cast<const float4 *>(x + c);
@@ -261,7 +280,7 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
       const float s = digits::row_scale(amax);
       const float inv = 1.0f / s;
-      const int t = t0 + warp;
+      const int t = t0 + r;
       int8_t *q1 = a.xq + (size_t)t * 2 * H, *q2 = q1 + H;
       for (int c = lane * 4; c < H; c += 128) {
         const float4 v = *reinterpret_cast<const float4 *>(x + c);
@@ -279,120 +298,366 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
   }
 }
 
-// P: stable counting sort of the R routes (tb.ids, token-major) by expert:
-// experts ascending, routes ascending inside (src/olmoe.rs:3474-3480).
-__device__ void build_tables(int R, int K, int E, DTables &tb) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int e = tid; e < E; e += kDT) tb.run[e] = 0;
-  for (int i = tid; i < kDW * kMaxExperts; i += kDT) (&tb.wcnt[0][0])[i] = 0;
-  __syncthreads();
-  for (int r = tid; r < R; r += kDT) {
-    const uint32_t e = tb.ids[r];
-    if (e < (uint32_t)E) atomicAdd(&tb.run[e], 1);
+// S: softmax and top-k of one token, by one warp (src/backend.rs:375-389,
+// src/olmoe.rs:2595-2621; the Router::select_top_k variant, src/router.rs:
+// 84-103, on raw scores).  Same arithmetic as select_token in route_core.cuh;
+// the K winners are found by rank instead of K argmax rounds: a candidate's
+// slot is the number of candidates before it in the reference's order
+// (f32::total_cmp descending, ties to the lower expert id).
+template <int kPer>
+__device__ void select_rank(const float *lg, int E, int K, int norm_topk_prob, int mode,
+                            uint32_t *ids, float *gates, uint32_t *key, float *sel_v,
+                            uint32_t *sel_i, float *ex, uint32_t *status) {
+  const int lane = threadIdx.x & 31;
+  float v[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < E ? __ldcg(lg + e) : __int_as_float(0xff800000);  // -inf pad
+  }
+  if (mode == kRouteSoftmaxTopk) {
+    float mx = __int_as_float(0xff800000);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) mx = fmaxf(mx, v[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E) {
+        v[j] = expf_ref(__fsub_rn(v[j], mx));
+        ex[e] = v[j];
+      }
+    }
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0) {
+      // sequential in index order, loads batched ahead of the dependent adds
+      sum = -0.0f;
+      int e = 0;
+      for (; e + 8 <= E; e += 8) {
+        float v8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v8[j] = ex[e + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sum = __fadd_rn(sum, v8[j]);
+      }
+      for (; e < E; ++e) sum = __fadd_rn(sum, ex[e]);
+    }
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (lane + 32 * j < E) v[j] = __fdiv_rn(v[j], sum);
+  } else {
+    // partial_cmp treats -0.0 == +0.0: canonical zero, so ties go by index
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (v[j] == 0.0f) v[j] = 0.0f;
+  }
+  uint32_t k[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    k[j] = total_order_u32(v[j]);
+    if (lane + 32 * j < E) key[lane + 32 * j] = k[j];
+  }
+  __syncwarp();
+  int rank[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) rank[j] = 0;
+  for (int f = 0; f < E; ++f) {
+    const uint32_t kf = key[f];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane + 32 * j;
+      rank[j] += (kf > k[j]) || (kf == k[j] && f < e);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane + 32 * j;
+    if (e < E && rank[j] < K) {
+      sel_v[rank[j]] = v[j];
+      sel_i[rank[j]] = (uint32_t)e;
+    }
+  }
+  __syncwarp();
+  if (mode == kRouteSoftmaxTopk) {
+    float norm = 1.0f;
+    if (norm_topk_prob) {
+      if (lane == 0) {
+        norm = -0.0f;
+        for (int q = 0; q < K; ++q) norm = __fadd_rn(norm, sel_v[q]);
+      }
+      norm = __shfl_sync(0xffffffffu, norm, 0);
+    }
+    if (lane < K) {
+      ids[lane] = sel_i[lane];
+      gates[lane] = __fdiv_rn(sel_v[lane], norm);
+      if (sel_i[lane] >= (uint32_t)E) set_status(status, kStatusBadRoute);
+    }
+  } else {
+    float total = 0.0f;
+    if (lane == 0) {
+      const float mx = sel_v[0];
+      total = -0.0f;
+      for (int q = 0; q < K; ++q) {
+        ex[q] = expf_ref(__fsub_rn(sel_v[q], mx));
+        total = __fadd_rn(total, ex[q]);
+      }
+    }
+    total = __shfl_sync(0xffffffffu, total, 0);
+    __syncwarp();
+    if (lane < K) {
+      ids[lane] = sel_i[lane];
+      gates[lane] = __fdiv_rn(ex[lane], total);
+    }
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void select_one(const DigitArgs &a, int t, uint32_t *ids,
+                                           float *gates, DTables &tb) {
+  const int w = threadIdx.x >> 5;
+  const float *lg = a.logits + (size_t)t * a.E;
+  uint32_t *key = tb.u.s.key[w];
+  float *ex = tb.u.s.ex[w];
+  if (a.E <= 64)
+    select_rank<2>(lg, a.E, a.K, a.norm, a.route_mode, ids, gates, key, tb.sel_v[w],
+                   tb.sel_i[w], ex, a.status);
+  else if (a.E <= 128)
+    select_rank<4>(lg, a.E, a.K, a.norm, a.route_mode, ids, gates, key, tb.sel_v[w],
+                   tb.sel_i[w], ex, a.status);
+  else
+    select_rank<kMaxExperts / 32>(lg, a.E, a.K, a.norm, a.route_mode, ids, gates, key,
+                                  tb.sel_v[w], tb.sel_i[w], ex, a.status);
+}
+
+// P: the R routes (tb.ids, token-major) sorted by expert, stable
+// (src/olmoe.rs:3474-3480: experts ascending, routes ascending inside), as
+// active-expert ranges, plus the cost prefixes of the gate/up and down splits.
+__device__ void build_tables(const DigitArgs &a, int R, DTables &tb) {
+  const int K = a.K, E = a.E, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (R <= 32) {
+    // one warp: a route's position counts the routes ordered before it
+    if (warp == 0) {
+      const uint32_t e = lane < R ? tb.ids[lane] : 0xFFFFFFFFu;
+      const bool valid = e < (uint32_t)E;
+      const unsigned same = __match_any_sync(0xffffffffu, valid ? e : 0xFFFFFFFFu);
+      const bool first = valid && (__ffs(same) - 1) == lane;
+      int pos = 0, act = 0;
+      for (int l = 0; l < 32; ++l) {
+        const uint32_t el = __shfl_sync(0xffffffffu, e, l);
+        const bool fl = __shfl_sync(0xffffffffu, first, l);
+        pos += el < (uint32_t)E && (el < e || (el == e && l < lane));
+        act += fl && el < e;
+      }
+      if (valid) {
+        tb.r_token[pos] = lane / K;
+        tb.r_slot[pos] = lane % K;
+        tb.r_gate[pos] = tb.gates[lane];
+      }
+      if (first) {
+        tb.act_e[act] = (int)e;
+        tb.act_r0[act] = pos;
+      }
+      const int na = __popc(__ballot_sync(0xffffffffu, first));
+      const int nv = __popc(__ballot_sync(0xffffffffu, valid));
+      if (lane == 0) {
+        tb.n_active = na;
+        tb.act_r0[na] = nv;
+      }
+    }
+  } else {
+    for (int e = tid; e < E; e += kDT) tb.run[e] = 0;
+    for (int i = tid; i < kDW * E; i += kDT) tb.u.wcnt[i / E][i % E] = 0;
+    __syncthreads();
+    for (int r = tid; r < R; r += kDT) {
+      const uint32_t e = tb.ids[r];
+      if (e < (uint32_t)E) atomicAdd(&tb.run[e], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int acc = 0, na = 0;
+      for (int base = 0; base < E; base += 32) {
+        const int e = base + lane;
+        const int c = e < E ? tb.run[e] : 0;
+        int inc = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += v;
+        }
+        const unsigned act = __ballot_sync(0xffffffffu, c > 0);
+        if (e < E) {
+          tb.run[e] = acc + inc - c;
+          if (c > 0) {
+            const int ai = na + __popc(act & ((1u << lane) - 1u));
+            tb.act_e[ai] = e;
+            tb.act_r0[ai] = acc + inc - c;
+          }
+        }
+        acc += __shfl_sync(0xffffffffu, inc, 31);
+        na += __popc(act);
+      }
+      if (lane == 0) {
+        tb.n_active = na;
+        tb.act_r0[na] = acc;
+      }
+    }
+    __syncthreads();
+    for (int base = 0; base < R; base += kDT) {
+      const int r = base + tid;
+      const bool valid = r < R;
+      const uint32_t e = valid ? tb.ids[r] : 0xFFFFFFFFu;
+      const bool ok = valid && e < (uint32_t)E;
+      const unsigned mask = __match_any_sync(0xffffffffu, ok ? e : 0xFFFFFFFFu);
+      const int intra = __popc(mask & ((1u << lane) - 1u));
+      if (ok && intra == 0) tb.u.wcnt[warp][e] = __popc(mask);
+      __syncthreads();
+      if (ok) {
+        int pos = tb.run[e] + intra;
+        for (int w = 0; w < warp; ++w) pos += tb.u.wcnt[w][e];
+        tb.r_token[pos] = r / K;
+        tb.r_slot[pos] = r % K;
+        tb.r_gate[pos] = tb.gates[r];
+      }
+      __syncthreads();
+      for (int ee = tid; ee < E; ee += kDT) {
+        int tot = 0;
+        for (int w = 0; w < kDW; ++w) {
+          tot += tb.u.wcnt[w][ee];
+          tb.u.wcnt[w][ee] = 0;
+        }
+        tb.run[ee] += tot;
+      }
+      __syncthreads();
+    }
   }
   __syncthreads();
+  // cost prefixes: a gate/up row pair costs (routes + kGateW), a down row
+  // (routes + kDownW), in units of one route's dot products
   if (warp == 0) {
-    int acc = 0, na = 0;
-    for (int base = 0; base < E; base += 32) {
-      const int e = base + lane;
-      const int c = e < E ? tb.run[e] : 0;
-      int inc = c;
+    const int na = tb.n_active;
+    int cg = 0, cd = 0;
+    for (int base = 0; base < na; base += 32) {
+      const int ai = base + lane;
+      const int r = ai < na ? tb.act_r0[ai + 1] - tb.act_r0[ai] : 0;
+      int g = ai < na ? a.I * (r + kGateW) : 0, d = ai < na ? a.H * (r + kDownW) : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += v;
+        const int vg = __shfl_up_sync(0xffffffffu, g, o), vd = __shfl_up_sync(0xffffffffu, d, o);
+        if (lane >= o) {
+          g += vg;
+          d += vd;
+        }
       }
-      const unsigned act = __ballot_sync(0xffffffffu, c > 0);
-      if (e < E) {
-        tb.seg_off[e] = acc + inc - c;
-        tb.run[e] = acc + inc - c;
-        if (c > 0) tb.active[na + __popc(act & ((1u << lane) - 1u))] = e;
+      if (ai < na) {
+        tb.cost_g[ai + 1] = cg + g;
+        tb.cost_d[ai + 1] = cd + d;
       }
-      acc += __shfl_sync(0xffffffffu, inc, 31);
-      na += __popc(act);
+      cg += __shfl_sync(0xffffffffu, g, 31);
+      cd += __shfl_sync(0xffffffffu, d, 31);
     }
     if (lane == 0) {
-      tb.seg_off[E] = acc;
-      tb.n_active = na;
+      tb.cost_g[0] = 0;
+      tb.cost_d[0] = 0;
     }
   }
   __syncthreads();
-  for (int base = 0; base < R; base += kDT) {
-    const int r = base + tid;
-    const bool valid = r < R;
-    const uint32_t e = valid ? tb.ids[r] : 0xFFFFFFFFu;
-    const bool ok = valid && e < (uint32_t)E;
-    const unsigned mask = __match_any_sync(0xffffffffu, ok ? e : 0xFFFFFFFFu);
-    const int intra = __popc(mask & ((1u << lane) - 1u));
-    if (ok && intra == 0) tb.wcnt[warp][e] = __popc(mask);
-    __syncthreads();
-    if (ok) {
-      int pos = tb.run[e] + intra;
-      for (int w = 0; w < warp; ++w) pos += tb.wcnt[w][e];
-      tb.r_token[pos] = r / K;
-      tb.r_slot[pos] = r % K;
-      tb.r_gate[pos] = tb.gates[r];
-    }
-    __syncthreads();
-    for (int ee = tid; ee < E; ee += kDT) {
-      int tot = 0;
-      for (int w = 0; w < kDW; ++w) {
-        tot += tb.wcnt[w][ee];
-        tb.wcnt[w][ee] = 0;
-      }
-      tb.run[ee] += tot;
-    }
-    __syncthreads();
+}
+
+// P for one token, by the warp that selected it: the K routes' experts are
+// distinct, so a route's sorted position is the number of smaller expert ids.
+__device__ void tables_single(const DigitArgs &a, DTables &tb) {
+  const int K = a.K, lane = threadIdx.x & 31;
+  __syncwarp();
+  const uint32_t e = lane < K ? tb.ids[lane] : 0xFFFFFFFFu;
+  const bool valid = e < (uint32_t)a.E;
+  int pos = 0;
+  for (int l = 0; l < K; ++l) {
+    const uint32_t el = __shfl_sync(0xffffffffu, e, l);
+    pos += el < (uint32_t)a.E && el < e;
+  }
+  if (valid) {
+    tb.r_token[pos] = 0;
+    tb.r_slot[pos] = lane;
+    tb.r_gate[pos] = tb.gates[lane];
+    tb.act_e[pos] = (int)e;
+    tb.act_r0[pos] = pos;
+  }
+  const int na = __popc(__ballot_sync(0xffffffffu, valid));
+  if (lane <= na) {
+    tb.cost_g[lane] = lane * a.I * (1 + kGateW);
+    tb.cost_d[lane] = lane * a.H * (1 + kDownW);
+  }
+  if (lane == 0) {
+    tb.n_active = na;
+    tb.act_r0[na] = na;
+  }
+  __syncwarp();
+}
+
+// This CTA's part of a cost-weighted split: the active experts a with rows
+// [rows_lo, rows_hi) of n rows each, unit cost w_a = routes + w0.  CTA c owns
+// cost [C c / G, C (c + 1) / G); a boundary inside expert a falls on row
+// ceil((x - cost[a]) / w_a), so neighbouring CTAs meet exactly.
+template <typename F>
+__device__ __forceinline__ void for_each_share(const DTables &tb, const int32_t *cost, int n,
+                                               int w0, F &&fn) {
+  const int na = tb.n_active;
+  const long long C = cost[na];
+  const long long c0 = C * blockIdx.x / gridDim.x, c1 = C * (blockIdx.x + 1) / gridDim.x;
+  for (int ai = 0; ai < na; ++ai) {
+    if (cost[ai + 1] <= c0) continue;
+    if (cost[ai] >= c1) break;
+    const int r0 = tb.act_r0[ai], r1 = tb.act_r0[ai + 1];
+    const long long w = r1 - r0 + w0;
+    const long long lo = std::max<long long>(0, c0 - cost[ai]);
+    const long long hi = std::min<long long>((long long)n * w, c1 - cost[ai]);
+    const int row0 = (int)((lo + w - 1) / w), row1 = (int)std::min<long long>(n, (hi + w - 1) / w);
+    if (row1 > row0) fn(ai, row0, row1, r0, r1);
   }
 }
 
-// The CTA's share [u0, u1) of n units.
+// The CTA's share [u0, u1) of n equal units.
 __device__ __forceinline__ void share(long long n, long long &u0, long long &u1) {
   u0 = n * blockIdx.x / gridDim.x;
   u1 = n * (blockIdx.x + 1) / gridDim.x;
 }
 
 // Bulk L2 prefetch of the down rows this CTA reads in D (same partition).
-__device__ void prefetch_down(const DigitArgs &a, const FusedLayer &L, const DTables &tb) {
+__device__ void prefetch_down(const DigitArgs &a, const DTables &tb) {
   if (threadIdx.x != 0) return;
   const int H = a.H, I = a.I;
-  long long u0, u1;
   if (a.T == 1) {
+    long long u0, u1;
     share(H, u0, u1);
     if (u1 <= u0) return;
     for (int k = 0; k < a.K; ++k) {
       const uint32_t e = tb.ids[k];
       if (e >= (uint32_t)a.E) continue;
-      prefetch_l2(L.w_ptr[e] + (size_t)2 * I * H + (size_t)u0 * I, (uint32_t)((u1 - u0) * I));
+      prefetch_l2(tb.wp[e] + (size_t)2 * I * H + (size_t)u0 * I, (uint32_t)((u1 - u0) * I));
     }
     return;
   }
-  share((long long)tb.n_active * H, u0, u1);
-  for (long long u = u0; u < u1;) {
-    const int ai = (int)(u / H), j0 = (int)(u - (long long)ai * H);
-    const int j1 = (int)std::min<long long>(H, j0 + (u1 - u));
-    prefetch_l2(L.w_ptr[tb.active[ai]] + (size_t)2 * I * H + (size_t)j0 * I,
+  for_each_share(tb, tb.cost_d, H, kDownW, [&](int ai, int j0, int j1, int, int) {
+    prefetch_l2(tb.wp[tb.act_e[ai]] + (size_t)2 * I * H + (size_t)j0 * I,
                 (uint32_t)((j1 - j0) * I));
-    u += j1 - j0;
-  }
+  });
 }
 
-// G: gate/up over the CTA's share of the (active expert, row) pairs.  A warp
-// takes two row pairs at a time, so 4 * NCH 16-byte loads per lane are in
-// flight before the first dot (NCH = 16-byte chunks per lane of an H row).
+// G: gate/up over the CTA's cost share of the (active expert, row pair)
+// units.  A warp takes two row pairs at a time, so 4 * NCH 16-byte loads per
+// lane are in flight before the first dot (NCH = 16-byte chunks per lane of
+// an H row); the rows' scales are loaded with them.
 template <int NCH>
-__device__ void gate_up_phase(const DigitArgs &a, const FusedLayer &L, uint8_t *xd, DTables &tb) {
+__device__ void gate_up_phase(const DigitArgs &a, uint8_t *xd, DTables &tb) {
   constexpr int kRows = 2;
   const int H = a.H, I = a.I, K = a.K, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  long long u0, u1;
-  share((long long)tb.n_active * I, u0, u1);
-  for (long long u = u0; u < u1;) {
-    const int ai = (int)(u / I), i0 = (int)(u - (long long)ai * I);
-    const int i1 = (int)std::min<long long>(I, i0 + (u1 - u));
-    u += i1 - i0;
-    const int e = tb.active[ai], r0 = tb.seg_off[e], r1 = tb.seg_off[e + 1];
-    const int8_t *W = L.w_ptr[e];
-    const float *S = L.s_ptr[e];
+  for_each_share(tb, tb.cost_g, I, kGateW, [&](int ai, int i0, int i1, int r0, int r1) {
+    const int e = tb.act_e[ai];
+    const int8_t *W = tb.wp[e];
+    const float *S = tb.sp[e];
     for (int rb = r0; rb < r1; rb += kGR) {
       const int nr = min(kGR, r1 - rb);
       // the digit planes of routes rb .. rb + nr (2H bytes each) and scales
@@ -423,6 +688,13 @@ __device__ void gate_up_phase(const DigitArgs &a, const FusedLayer &L, uint8_t *
               wg[q][m] = wu[q][m] = make_uint4(0, 0, 0, 0);
             }
           }
+        float sg[kRows], su[kRows];
+#pragma unroll
+        for (int q = 0; q < kRows; ++q) {
+          const int i = min(ib + q, i1 - 1);
+          sg[q] = S[i];
+          su[q] = S[I + i];
+        }
         int mg1[kRows] = {}, mg2[kRows] = {}, mu1[kRows] = {}, mu2[kRows] = {};  // route `lane`
         for (int j = 0; j < nr; ++j) {
           const uint8_t *x1 = xd + (size_t)j * 2 * H, *x2 = x1 + H;
@@ -464,37 +736,53 @@ __device__ void gate_up_phase(const DigitArgs &a, const FusedLayer &L, uint8_t *
             const int i = ib + q;
             if (i < i1)
               act[i] = digits::swiglu(mg1[q], mg2[q], mu1[q], mu2[q], tb.s1[lane], tb.s2[lane],
-                                      S[i], S[I + i]);
+                                      sg[q], su[q]);
           }
         }
       }
     }
-  }
+  });
 }
 
 // Digit planes of activation rows (I floats each, read through L2) into xd,
-// one warp per row; scales into tb.s1 / tb.s2.  rows[j] = act row index.
+// one warp per row; scales into tb.s1 / tb.s2.  act_row[j] = act row index.
+// Lane l owns the 16-element chunks l + 32 m (m < NCI) of the row, the same
+// chunks its dot products read later; all of its loads go out before the
+// row maximum is formed.
+template <int NCI>
 __device__ void digitise_act(const DigitArgs &a, const int32_t *act_row, int nr, uint8_t *xd,
                              DTables &tb) {
   const int I = a.I, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int j = warp; j < nr; j += kDW) {
-    const float *x = a.act + (size_t)act_row[j] * I;
+    const float4 *x = reinterpret_cast<const float4 *>(a.act + (size_t)act_row[j] * I);
+    float4 v[NCI][4];
     float amax = 0.0f;
-    for (int c = lane * 4; c < I; c += 128) {
-      const float4 v = __ldcg(reinterpret_cast<const float4 *>(x + c));
-      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+#pragma unroll
+    for (int m = 0; m < NCI; ++m) {
+      const int c = 16 * (lane + 32 * m);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[m][q] = c < I ? __ldcg(x + c / 4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[m][q].x), fabsf(v[m][q].y)),
+                                 fmaxf(fabsf(v[m][q].z), fabsf(v[m][q].w))));
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float s = digits::row_scale(amax);
     const float inv = 1.0f / s;
     uint8_t *q1 = xd + (size_t)j * 2 * I, *q2 = q1 + I;
-    for (int c = lane * 4; c < I; c += 128) {
-      const float4 v = __ldcg(reinterpret_cast<const float4 *>(x + c));
-      uint32_t p2;
-      const uint32_t p1 = digits::split4(v.x, v.y, v.z, v.w, inv, p2);
-      *reinterpret_cast<uint32_t *>(q1 + c) = p1;
-      *reinterpret_cast<uint32_t *>(q2 + c) = p2;
+#pragma unroll
+    for (int m = 0; m < NCI; ++m) {
+      const int c = 16 * (lane + 32 * m);
+      if (c < I) {
+        uint32_t p1[4], p2[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          p1[q] = digits::split4(v[m][q].x, v[m][q].y, v[m][q].z, v[m][q].w, inv, p2[q]);
+        *reinterpret_cast<uint4 *>(q1 + c) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+        *reinterpret_cast<uint4 *>(q2 + c) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+      }
     }
     if (lane == 0) {
       tb.s1[j] = s;
@@ -503,104 +791,110 @@ __device__ void digitise_act(const DigitArgs &a, const int32_t *act_row, int nr,
   }
 }
 
-// D for one token: the CTA's block of output rows over all K routes, combined
-// in slot order in registers: out = base + g_0 y_0 + ... + g_{K-1} y_{K-1}.
-// The rows of up to 8 experts are loaded before the first dot.
+// D for one token: the CTA's block of output rows [u0, u1) over all K
+// routes.  Warp w streams slot w's expert (and w + 8, ...): its rows of the
+// block are contiguous, and all of them are loaded before the first dot.  The
+// gate-weighted outputs meet in shared memory and each row is combined in slot
+// order: out = base + g_0 y_0 + ... + g_{K-1} y_{K-1}.
 template <int NCI>
-__device__ void down_single(const DigitArgs &a, const FusedLayer &L, const float *resid,
-                            float *out, uint8_t *xd, DTables &tb) {
-  constexpr int kE = 8;
+__device__ void down_single(const DigitArgs &a, const float *resid, float *out, uint8_t *xd,
+                            DTables &tb) {
+  constexpr int kMaxRows = 8;  // rows of the block handled per pass
   const int H = a.H, I = a.I, K = a.K, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   long long u0, u1;
   share(H, u0, u1);
+  const int nrows = (int)(u1 - u0);
   __shared__ int32_t rows[kMaxTopK];
+  __shared__ float cs[kMaxRows][kMaxTopK];
   if (threadIdx.x < K) rows[threadIdx.x] = threadIdx.x;  // act row of slot k (token 0)
   __syncthreads();
-  digitise_act(a, rows, K, xd, tb);
+  digitise_act<NCI>(a, rows, K, xd, tb);
   __syncthreads();
   bool bad = false;
-  for (int j = (int)u0 + warp; j < (int)u1; j += kDW) {
-    int my1 = 0, my2 = 0;  // sums of slot `lane`
-    for (int k0 = 0; k0 < K; k0 += kE) {
-      uint4 w[kE][NCI];
+  for (int r0 = 0; r0 < nrows; r0 += kMaxRows) {
+    const int nr = min(kMaxRows, nrows - r0);
+    for (int k = warp; k < K; k += kDW) {
+      const uint32_t e = tb.ids[k];
+      if (e >= (uint32_t)a.E) {
+        if (lane < nr) cs[lane][k] = 0.0f;
+        continue;
+      }
+      const int j0 = (int)u0 + r0;
+      const int8_t *Wr = tb.wp[e] + (size_t)2 * I * H + (size_t)j0 * I;
+      const float sd = lane < nr ? tb.sp[e][2 * I + j0 + lane] : 0.0f;
+      uint4 w[kMaxRows][NCI];
 #pragma unroll
-      for (int kk = 0; kk < kE; ++kk) {
-        const int k = k0 + kk;
-        const uint32_t e = k < K ? tb.ids[k] : 0xFFFFFFFFu;
-        const int8_t *Wr = e < (uint32_t)a.E
-                               ? L.w_ptr[e] + (size_t)2 * I * H + (size_t)j * I
-                               : nullptr;
+      for (int q = 0; q < kMaxRows; ++q)
 #pragma unroll
         for (int m = 0; m < NCI; ++m) {
           const int off = 16 * (lane + 32 * m);
-          w[kk][m] = (Wr && off < I) ? ldg_stream16(Wr + off) : make_uint4(0, 0, 0, 0);
+          w[q][m] = (q < nr && off < I) ? ldg_stream16(Wr + (size_t)q * I + off)
+                                        : make_uint4(0, 0, 0, 0);
         }
-      }
+      const uint8_t *x1 = xd + (size_t)k * 2 * I, *x2 = x1 + I;
+      uint4 c1[NCI], c2[NCI];
 #pragma unroll
-      for (int kk = 0; kk < kE; ++kk) {
-        const int k = k0 + kk;
-        if (k >= K) break;
-        const uint8_t *x1 = xd + (size_t)k * 2 * I, *x2 = x1 + I;
+      for (int m = 0; m < NCI; ++m) {
+        const int off = 16 * (lane + 32 * m);
+        c1[m] = off < I ? *reinterpret_cast<const uint4 *>(x1 + off) : make_uint4(0, 0, 0, 0);
+        c2[m] = off < I ? *reinterpret_cast<const uint4 *>(x2 + off) : make_uint4(0, 0, 0, 0);
+      }
+      int my1 = 0, my2 = 0;  // sums of row `lane`
+#pragma unroll
+      for (int q = 0; q < kMaxRows; ++q) {
+        if (q >= nr) break;
         int d1 = 0, d2 = 0;
 #pragma unroll
         for (int m = 0; m < NCI; ++m) {
-          const int off = 16 * (lane + 32 * m);
-          if (off < I) {
-            dp4(w[kk][m], *reinterpret_cast<const uint4 *>(x1 + off), d1);
-            dp4(w[kk][m], *reinterpret_cast<const uint4 *>(x2 + off), d2);
-          }
+          dp4(w[q][m], c1[m], d1);
+          dp4(w[q][m], c2[m], d2);
         }
         d1 = warp_sum(d1);
         d2 = warp_sum(d2);
-        if (lane == k) {
+        if (lane == q) {
           my1 = d1;
           my2 = d2;
         }
       }
-    }
-    float c = 0.0f;
-    if (lane < K) {
-      const uint32_t e = tb.ids[lane];
-      if (e < (uint32_t)a.E) {
-        const float y = digits::down(my1, my2, tb.s1[lane], tb.s2[lane], L.s_ptr[e][2 * I + j]);
+      if (lane < nr) {
+        const float y = digits::down(my1, my2, tb.s1[k], tb.s2[k], sd);
         bad |= !is_finite_f(y);
-        c = __fmul_rn(tb.gates[lane], y);
+        cs[lane][k] = __fmul_rn(tb.gates[k], y);
       }
     }
-    float acc = resid ? __ldcg(resid + j) : 0.0f;
-    for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, c, k));
-    if (lane == 0) {
+    __syncthreads();
+    if (threadIdx.x < nr) {
+      const int j = (int)u0 + r0 + threadIdx.x;
+      float acc = resid ? __ldcg(resid + j) : 0.0f;
+      for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, cs[threadIdx.x][k]);
       bad |= !is_finite_f(acc);
       out[j] = acc;
     }
+    __syncthreads();
   }
   if (bad) set_status(a.status, kStatusNonFinite);
 }
 
-// D for T > 1: the CTA's share of (active expert, output row) pairs; gate * y
-// into contrib[token, slot, row].  A warp takes four rows at a time.
+// D for T > 1: the CTA's cost share of (active expert, output row) units;
+// gate * y into contrib[token, slot, row].  A warp takes six rows at a time,
+// with their scales.
 template <int NCI>
-__device__ void down_items(const DigitArgs &a, const FusedLayer &L, uint8_t *xd, DTables &tb) {
-  constexpr int kRows = 4;
+__device__ void down_items(const DigitArgs &a, uint8_t *xd, DTables &tb) {
+  constexpr int kRows = 6;
   const int H = a.H, I = a.I, K = a.K, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ int32_t rows[kGR];
-  long long u0, u1;
-  share((long long)tb.n_active * H, u0, u1);
   bool bad = false;
-  for (long long u = u0; u < u1;) {
-    const int ai = (int)(u / H), j0 = (int)(u - (long long)ai * H);
-    const int j1 = (int)std::min<long long>(H, j0 + (u1 - u));
-    u += j1 - j0;
-    const int e = tb.active[ai], r0 = tb.seg_off[e], r1 = tb.seg_off[e + 1];
-    const int8_t *Wd = L.w_ptr[e] + (size_t)2 * I * H;
-    const float *Sd = L.s_ptr[e] + 2 * I;
+  for_each_share(tb, tb.cost_d, H, kDownW, [&](int ai, int j0, int j1, int r0, int r1) {
+    const int e = tb.act_e[ai];
+    const int8_t *Wd = tb.wp[e] + (size_t)2 * I * H;
+    const float *Sd = tb.sp[e] + 2 * I;
     for (int rb = r0; rb < r1; rb += kGR) {
       const int nr = min(kGR, r1 - rb);
       __syncthreads();
       if (threadIdx.x < nr)
         rows[threadIdx.x] = tb.r_token[rb + threadIdx.x] * K + tb.r_slot[rb + threadIdx.x];
       __syncthreads();
-      digitise_act(a, rows, nr, xd, tb);
+      digitise_act<NCI>(a, rows, nr, xd, tb);
       __syncthreads();
       for (int jb = j0 + warp * kRows; jb < j1; jb += kDW * kRows) {
         uint4 w[kRows][NCI];
@@ -612,6 +906,9 @@ __device__ void down_items(const DigitArgs &a, const FusedLayer &L, uint8_t *xd,
             w[q][m] = (j < j1 && off < I) ? ldg_stream16(Wd + (size_t)j * I + off)
                                           : make_uint4(0, 0, 0, 0);
           }
+        float sd[kRows];
+#pragma unroll
+        for (int q = 0; q < kRows; ++q) sd[q] = Sd[min(jb + q, j1 - 1)];
         int my1[kRows] = {}, my2[kRows] = {};
         for (int r = 0; r < nr; ++r) {
           const uint8_t *x1 = xd + (size_t)r * 2 * I, *x2 = x1 + I;
@@ -644,7 +941,7 @@ __device__ void down_items(const DigitArgs &a, const FusedLayer &L, uint8_t *xd,
           for (int q = 0; q < kRows; ++q) {
             const int j = jb + q;
             if (j < j1) {
-              const float y = digits::down(my1[q], my2[q], tb.s1[lane], tb.s2[lane], Sd[j]);
+              const float y = digits::down(my1[q], my2[q], tb.s1[lane], tb.s2[lane], sd[q]);
               bad |= !is_finite_f(y);
               a.contrib[(size_t)rows[lane] * H + j] = __fmul_rn(tb.r_gate[rb + lane], y);
             }
@@ -652,7 +949,7 @@ __device__ void down_items(const DigitArgs &a, const FusedLayer &L, uint8_t *xd,
         }
       }
     }
-  }
+  });
   if (bad) set_status(a.status, kStatusNonFinite);
 }
 
@@ -672,12 +969,9 @@ __device__ void combine_phase(const DigitArgs &a, const float *resid, float *out
   if (bad) set_status(a.status, kStatusNonFinite);
 }
 
+// The layers of one launch; false when a barrier wait gave up.
 template <int NCH, int NCI>
-__global__ void __launch_bounds__(kDT, 2) digit_decode_kernel(DigitArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  DTables &tb = *reinterpret_cast<DTables *>(smem);
-  SelectScratch *sel = reinterpret_cast<SelectScratch *>(smem + kSelOff);
-  uint8_t *stage = smem + kStageOff;
+__device__ bool run_layers(const DigitArgs &a, DTables &tb, uint8_t *stage) {
   const int G = gridDim.x, T = a.T, K = a.K, R = T * K;
   const int warp = threadIdx.x >> 5;
   uint32_t nbar = 0;
@@ -685,19 +979,25 @@ __global__ void __launch_bounds__(kDT, 2) digit_decode_kernel(DigitArgs a) {
     ++nbar;
     return grid_sync(a.bar, nbar * G, a.status, a.wait_cycles);
   };
-  stamp(a, 0);
   for (int l = 0; l < a.n_layers; ++l) {
     const FusedLayer L = a.layers[l];
+    const bool first = l == 0;
+    // the layer's expert pointers, read while the router runs
+    for (int e = threadIdx.x; e < a.E; e += kDT) {
+      tb.wp[e] = L.w_ptr[e];
+      tb.sp[e] = L.s_ptr[e];
+    }
     // stacked: x is the residual stream (in `out`), normalised while staged
     const float *xin = a.stacked ? a.out : a.h_in;
     const float *resid = a.stacked ? a.out : a.resid;
     router_phase(a, L, xin, a.stacked != 0, reinterpret_cast<float *>(stage), tb);
-    if (!sync()) return;
+    if (first) stamp(a, 1);
+    if (!sync()) return false;
+    if (first) stamp(a, 2);
     // S: selection
     if (T <= kDW) {
-      if (warp < T)
-        select_token(a.logits + (size_t)warp * a.E, a.E, K, a.norm, a.route_mode,
-                     tb.ids + warp * K, tb.gates + warp * K, nullptr, sel[warp], a.status);
+      if (warp < T) select_one(a, warp, tb.ids + warp * K, tb.gates + warp * K, tb);
+      if (T == 1 && warp == 0) tables_single(a, tb);
       __syncthreads();
       if (blockIdx.x == 0)
         for (int r = threadIdx.x; r < R; r += kDT) {
@@ -706,38 +1006,69 @@ __global__ void __launch_bounds__(kDT, 2) digit_decode_kernel(DigitArgs a) {
         }
     } else {
       for (int t = blockIdx.x * kDW + warp; t < T; t += G * kDW)
-        select_token(a.logits + (size_t)t * a.E, a.E, K, a.norm, a.route_mode, a.ids + t * K,
-                     a.gates + t * K, nullptr, sel[warp], a.status);
-      if (!sync()) return;
+        select_one(a, t, a.ids + t * K, a.gates + t * K, tb);
+      if (!sync()) return false;
       for (int r = threadIdx.x; r < R; r += kDT) {
         tb.ids[r] = __ldcg(a.ids + r);
         tb.gates[r] = __ldcg(a.gates + r);
       }
       __syncthreads();
     }
-    build_tables(R, K, a.E, tb);
-    if (l == 0) stamp(a, 1);
-    if (a.prefetch_down) prefetch_down(a, L, tb);
-    gate_up_phase<NCH>(a, L, stage, tb);
-    if (!sync()) return;
-    if (l == 0) stamp(a, 2);
+    if (first) stamp(a, 3);
+    if (T > 1) build_tables(a, R, tb);
+    if (first) stamp(a, 4);
+    if (a.prefetch_down) prefetch_down(a, tb);
+    gate_up_phase<NCH>(a, stage, tb);
+    if (first) stamp(a, 5);
+    if (!sync()) return false;
+    if (first) stamp(a, 6);
     if (T == 1) {
-      down_single<NCI>(a, L, resid, a.out, stage, tb);
+      down_single<NCI>(a, resid, a.out, stage, tb);
     } else {
-      down_items<NCI>(a, L, stage, tb);
-      if (!sync()) return;
+      down_items<NCI>(a, stage, tb);
+      if (!sync()) return false;
       combine_phase(a, resid, a.out);
     }
-    if (l == 0) stamp(a, 3);
-    if (a.stacked && l + 1 < a.n_layers && !sync()) return;
+    if (first) stamp(a, 7);
+    if (a.stacked && l + 1 < a.n_layers && !sync()) return false;
   }
   if (blockIdx.x == 0 && a.ids_out)
     for (int r = threadIdx.x; r < R; r += kDT) {
       a.ids_out[r] = __ldcg(a.ids + r);
       a.gates_out[r] = __ldcg(a.gates + r);
     }
+  return true;
+}
+
+// bar[0] counts barrier arrivals, bar[1] exits: the last CTA to leave --
+// after every other CTA has passed all of its barriers, or given up --
+// zeroes both, so the next launch needs no reset of its own.
+template <int NCH, int NCI>
+__global__ void __launch_bounds__(kDT, 2) digit_decode_kernel(DigitArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  DTables &tb = *reinterpret_cast<DTables *>(smem);
+  uint8_t *stage = smem + kStageOff;
+  stamp(a, 0);
+  unsigned long long t_start = 0;
+  if (a.phase_ts && threadIdx.x == 0) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
+  run_layers<NCH, NCI>(a, tb, stage);
   __syncthreads();
-  stamp(a, 4);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
+      atomicExch(a.bar, 0u);
+      atomicExch(a.bar + 1, 0u);
+      __threadfence();
+    }
+    if (a.phase_ts) {
+      // per-CTA start and end (profiling): [16 + 2 c], [16 + 2 c + 1]
+      unsigned long long t_end;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_end));
+      a.phase_ts[16 + 2 * blockIdx.x] = t_start;
+      a.phase_ts[16 + 2 * blockIdx.x + 1] = t_end;
+    }
+  }
+  stamp(a, 8);
 }
 
 size_t digit_smem_bytes(int H, int I) {
@@ -780,8 +1111,6 @@ cudaError_t launch_digit_decode(const DigitArgs &a_in, int sm_count, cudaStream_
     cached_fn = fn;
     cached_grid = std::min(per_sm, 2) * sm_count;
   }
-  cudaError_t e = cudaMemsetAsync(a_in.bar, 0, sizeof(uint32_t), s);
-  if (e != cudaSuccess) return e;
   DigitArgs a = a_in;
   a.router_async = a_in.router_async && a_in.H % 4 == 0;
   void *params[] = {&a};

@@ -212,6 +212,8 @@ struct moe_handle {
   std::vector<moe::FusedLayer> flayers;
   std::vector<int> layer_vec;
   uint32_t *tok_cnt = nullptr, *fbar = nullptr;
+  uint32_t *dbar = nullptr;                // digit decode barrier: arrivals, exits
+  int phase_kind = 0;                      // stamps of: 0 the exact kernel, 1 the digit kernel
   int32_t *perm_scratch = nullptr;         // multi-CTA permutation
   size_t perm_scratch_words = 0;
   std::vector<int> layer_async;            // router rows are 16-byte aligned f32

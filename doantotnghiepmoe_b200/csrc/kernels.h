@@ -171,12 +171,13 @@ struct DigitArgs {
   float *xs1, *xs2;          // [T] token scales s, s / 254
   float *act;                // [T*K, I] activations (token-major route order)
   float *contrib;            // [T, K, H] gate * y (T > 1)
-  uint32_t *bar;             // grid barrier counter (zeroed by the launcher)
+  uint32_t *bar;             // [2] barrier arrivals, exits: zero before the first launch;
+                             // every launch leaves them zero
   uint32_t *status;
   long long wait_cycles;     // bound of each grid-barrier wait (SM clock cycles)
   int router_async;          // routers of every layer are 16-byte aligned f32 rows
   int prefetch_down;         // prefetch the down rows into L2 during gate/up
-  unsigned long long *phase_ts;  // optional [5] phase timestamps (profiling)
+  unsigned long long *phase_ts;  // optional [9] phase timestamps (profiling)
 };
 bool digit_decode_supported(int T, int H, int I, int E, int K);
 cudaError_t launch_digit_decode(const DigitArgs &a, int sm_count, cudaStream_t s);

@@ -347,7 +347,7 @@ void free_handle(moe_handle *h) {
                   h->aq,      h->xs1,       h->xs2,       h->as1,       h->as2,     h->act_amax,
                   h->tile_expert, h->tile_row0, h->tile_rows, h->n_tiles, h->d_flayers,
                   h->dtile_expert, h->dtile_row0, h->dtile_rows, h->n_dtiles,
-                  h->tok_cnt, h->fbar, h->phase_ts, h->perm_scratch, h->probe_flag};
+                  h->tok_cnt, h->fbar, h->phase_ts, h->perm_scratch, h->probe_flag, h->dbar};
   for (void *p : ptrs) cudaFree(p);
   cudaFreeHost(h->h_pin_in);
   cudaFreeHost(h->h_pin_out);
@@ -419,7 +419,7 @@ DigitArgs digit_args(moe_handle *h, int T) {
   a.xs2 = h->xs2;
   a.act = h->act;
   a.contrib = h->contrib;
-  a.bar = h->fbar;
+  a.bar = h->dbar;
   a.status = h->status;
   a.wait_cycles = h->wait_barrier_cycles;
   // the down rows of a single-token launch (<= K experts) fit in L2 beside
@@ -428,6 +428,7 @@ DigitArgs digit_args(moe_handle *h, int T) {
   if (h->prof.on) {
     a.phase_ts = h->phase_ts;
     h->phase_pending = true;
+    h->phase_kind = 1;
   }
   return a;
 }
@@ -467,6 +468,7 @@ FusedArgs fused_args(moe_handle *h, int T) {
   if (h->prof.on) {
     f.phase_ts = h->phase_ts;
     h->phase_pending = true;
+    h->phase_kind = 0;
   }
   return f;
 }
@@ -712,7 +714,9 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && dalloc(&h->d_flayers, d.num_layers) == cudaSuccess;
   ok = ok && dalloc(&h->tok_cnt, T) == cudaSuccess && dalloc(&h->fbar, 1) == cudaSuccess;
   ok = ok && cudaMemset(h->tok_cnt, 0, T * sizeof(uint32_t)) == cudaSuccess;
-  ok = ok && dalloc(&h->phase_ts, 16) == cudaSuccess;
+  ok = ok && dalloc(&h->phase_ts, 16 + 2 * 1024) == cudaSuccess;  // + per-CTA start, end
+  ok = ok && dalloc(&h->dbar, 2) == cudaSuccess &&
+       cudaMemset(h->dbar, 0, 2 * sizeof(uint32_t)) == cudaSuccess;
   ok = ok && dalloc(&h->probe_flag, 1) == cudaSuccess &&
        cudaMemset(h->probe_flag, 0, sizeof(uint32_t)) == cudaSuccess;
   h->perm_scratch_words = permute_scratch_words((int)(T * K), (int)E);
@@ -1496,16 +1500,44 @@ extern "C" moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int 
   if (h->phase_pending) {
     // phases of the most recent profiled fused launch (first layer; the
     // last entry runs to the end of the launch)
-    unsigned long long ts[16] = {};
-    if (cudaMemcpy(ts, h->phase_ts, sizeof ts, cudaMemcpyDeviceToHost) == cudaSuccess) {
-      static const char *names[4] = {"fused:router", "fused:gate_up", "fused:down",
-                                     "fused:rest"};
-      for (int i = 0; i < 4; ++i) {
+    std::vector<unsigned long long> all(16 + 2 * 1024, 0);
+    unsigned long long *ts = all.data();
+    if (cudaMemcpy(ts, h->phase_ts, all.size() * sizeof(unsigned long long),
+                   cudaMemcpyDeviceToHost) == cudaSuccess) {
+      static const char *names_f[4] = {"fused:router", "fused:gate_up", "fused:down",
+                                       "fused:rest"};
+      static const char *names_d[8] = {"digit:router", "digit:barrier", "digit:select",
+                                       "digit:tables", "digit:gate_up", "digit:barrier2",
+                                       "digit:down", "digit:rest"};
+      const char *const *names = h->phase_kind ? names_d : names_f;
+      const int nph = h->phase_kind ? 8 : 4;
+      for (int i = 0; i < nph; ++i) {
         moe_kernel_time k{};
         snprintf(k.name, sizeof k.name, "%s", names[i]);
         k.launches = 1;
         k.total_ms = ts[i + 1] > ts[i] ? (float)((ts[i + 1] - ts[i]) * 1e-6) : 0.0f;
         acc.push_back(k);
+      }
+      if (h->phase_kind) {
+        // spread of the CTAs' start and end times around CTA 0's start
+        unsigned long long s0 = ~0ull, s1 = 0, e0 = ~0ull, e1 = 0;
+        for (int c = 0; c < 1024; ++c) {
+          const unsigned long long a0 = ts[16 + 2 * c], a1 = ts[16 + 2 * c + 1];
+          if (!a0 || !a1 || a0 + 100000 < ts[0]) continue;  // older launches
+          s0 = std::min(s0, a0), s1 = std::max(s1, a0), e0 = std::min(e0, a1), e1 = std::max(e1, a1);
+        }
+        if (s1 >= s0 && e1 >= e0 && s0 != ~0ull) {
+          const char *nm[3] = {"digit:cta_start_spread", "digit:cta_end_spread",
+                               "digit:first_to_last"};
+          const unsigned long long v[3] = {s1 - s0, e1 - e0, e1 - s0};
+          for (int i = 0; i < 3; ++i) {
+            moe_kernel_time k{};
+            snprintf(k.name, sizeof k.name, "%s", nm[i]);
+            k.launches = 1;
+            k.total_ms = (float)(v[i] * 1e-6);
+            acc.push_back(k);
+          }
+        }
       }
     }
     h->phase_pending = false;

@@ -157,3 +157,39 @@ def test_olmoe_stack_16_layers(T):
         assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ref.ids), l
         assert helpers.rel_err(od.cpu().numpy(), ref.out) < TOL, l
         xl = ref.out
+
+
+def test_topk_ties_and_router_kat_on_the_digit_path():
+    """The reference's top-k tie cases (src/olmoe.rs:6496-6543) and the
+    learned-router KAT (src/router.rs:118-140) through the digit launch's own
+    router and rank-based top-k.  Rows are padded to 16 with zeros: the
+    hidden state is e_0 (plus the KAT's second component), so the logits are
+    the cases' values exactly."""
+    H, I = 16, 16
+    cases = helpers.unit_cases()
+    for case in cases["topk_ties"]:
+        vals = np.array(case["values"], np.float32)
+        router = np.zeros((64, H), np.float32)
+        router[:, 0] = vals
+        lw = O.LayerWeights(H, I, 64, 8, False, router, np.zeros((64, 3 * H * I), np.int8),
+                            np.ones((64, 2 * I + H), np.float32))
+        eng = M.MoeLayerEngine(M.MoeConfig(H, I, 64, 8, False, 1, 1))
+        eng.set_layer_packed(0, *helpers.to_device(lw))
+        h = np.zeros((1, H), np.float32)
+        h[0, 0] = 1.0
+        _, ids, _, prof = run(eng, h, _lib.MOE_PATH_DIGITS)
+        assert "digit_decode" in prof
+        assert list(ids[0]) == case["expected"]
+    kat = cases["router_kat"]
+    router = np.zeros((3, H), np.float32)
+    router[:, :2] = np.array(kat["weights"], np.float32).reshape(3, 2)
+    lw = O.LayerWeights(H, I, 3, 2, False, router, np.zeros((3, 3 * H * I), np.int8),
+                        np.ones((3, 2 * I + H), np.float32))
+    eng = M.MoeLayerEngine(M.MoeConfig(H, I, 3, 2, False, 1, 1))
+    eng.set_layer_packed(0, *helpers.to_device(lw))
+    eng.set_route_mode(_lib.MOE_ROUTE_TOPK_SOFTMAX)
+    h = np.zeros((1, H), np.float32)
+    h[0, :2] = kat["hidden"]
+    _, ids, gates, _ = run(eng, h, _lib.MOE_PATH_DIGITS)
+    assert list(ids[0]) == kat["ids"]
+    assert np.array_equal(bits(gates[0]), bits(np.array(kat["gates"], np.float32)))
