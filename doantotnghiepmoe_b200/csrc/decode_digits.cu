@@ -637,6 +637,11 @@ __device__ void prefetch_down(const DigitArgs &a, const DTables &tb) {
       const uint32_t e = tb.ids[k];
       if (e >= (uint32_t)a.E) continue;
       prefetch_l2(tb.wp[e] + (size_t)2 * I * H + (size_t)u0 * I, (uint32_t)((u1 - u0) * I));
+      // the rows' scales, widened to whole 16-byte blocks
+      const uintptr_t s0 = reinterpret_cast<uintptr_t>(tb.sp[e] + 2 * I + u0) & ~uintptr_t(15);
+      const uintptr_t s1 =
+          (reinterpret_cast<uintptr_t>(tb.sp[e] + 2 * I + u1) + 15) & ~uintptr_t(15);
+      prefetch_l2(reinterpret_cast<const void *>(s0), (uint32_t)(s1 - s0));
     }
     return;
   }

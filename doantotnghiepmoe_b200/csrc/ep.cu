@@ -310,29 +310,19 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
         reinterpret_cast<const int32_t *>(p.base[p.rank] + p.off_counts) + (size_t)par * p.nranks * E;
     ep_dest_bases(cm, owner, E, p.rank, p.nranks, tot, base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // one warp per token: the row is quantized once and stored at each of
-    // its K routes' rows in their owners' expert-sorted buffers
-    for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
-      int q = 0, pos = 0, slot_ok = 0;
-      float g = 0.0f;
-      if (lane < K) {
-        const uint32_t e = ids[(size_t)t * K + lane];
-        const int r = r_pos[(size_t)t * K + lane];
-        if (e < (uint32_t)E && r >= 0) {
-          q = owner[e];
-          pos = base[e] + (r - segs[e]);
-          g = gates[(size_t)t * K + lane];
-          slot_ok = 1;
-        }
-      }
-      const unsigned vmask = __ballot_sync(0xffffffffu, slot_ok);
-      uint8_t *dst[kMaxTopK];
-#pragma unroll
-      for (int k = 0; k < kMaxTopK; ++k) {
-        const int qk = __shfl_sync(0xffffffffu, q, k);
-        const int pk = __shfl_sync(0xffffffffu, pos, k);
-        dst[k] = peer_at(p, qk, p.off_xq) + (size_t)pk * H;
-      }
+    // one warp per route: it digitises its token's row (every route of a
+    // token gets the same digits) and stores them at the route's row in its
+    // owner's expert-sorted buffer.  With a warp per route rather than per
+    // token, every SM issues peer stores.
+    const int R = T * K;
+    for (int r = blockIdx.x * 8 + warp; r < R; r += gridDim.x * 8) {
+      const uint32_t e = ids[r];
+      const int rp = r_pos[r];
+      if (!(e < (uint32_t)E && rp >= 0)) continue;  // warp-uniform
+      const int t = r / K, slot = r - t * K;
+      const int q = owner[e];
+      const int pos = base[e] + (rp - segs[e]);
+      uint8_t *dst = peer_at(p, q, p.off_xq) + (size_t)pos * H;
       const float *xr = x + (size_t)t * H;
       // the single-GPU tensor path's two-digit quantization of the row
       float amax = 0.0f;
@@ -353,22 +343,16 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
           const float4 v = *reinterpret_cast<const float4 *>(xr + c + 4 * w4);
           p1[w4] = digits::split4(v.x, v.y, v.z, v.w, inv, p2[w4]);
         }
-        const uint4 v1 = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-        const uint4 v2 = make_uint4(p2[0], p2[1], p2[2], p2[3]);
-#pragma unroll
-        for (int k = 0; k < kMaxTopK; ++k)
-          if ((vmask >> k) & 1u) {
-            *reinterpret_cast<uint4 *>(dst[k] + c) = v1;
-            *reinterpret_cast<uint4 *>(dst[k] + p.plane + c) = v2;
-          }
+        *reinterpret_cast<uint4 *>(dst + c) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+        *reinterpret_cast<uint4 *>(dst + p.plane + c) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
       }
-      if (slot_ok) {
+      if (lane == 0) {
         reinterpret_cast<float *>(peer_at(p, q, p.off_s1))[pos] = s;
         reinterpret_cast<float *>(peer_at(p, q, p.off_s2))[pos] = s / 254.0f;
-        reinterpret_cast<float *>(peer_at(p, q, p.off_gate))[pos] = g;
+        reinterpret_cast<float *>(peer_at(p, q, p.off_gate))[pos] = gates[r];
         reinterpret_cast<int32_t *>(peer_at(p, q, p.off_rank))[pos] = p.rank;
         reinterpret_cast<int32_t *>(peer_at(p, q, p.off_tok))[pos] = t;
-        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_slot))[pos] = lane;
+        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_slot))[pos] = slot;
         reinterpret_cast<uint32_t *>(peer_at(p, q, p.off_amax))[pos] = 0u;
       }
     }
@@ -453,32 +437,39 @@ __global__ void ep_wait_combine_kernel(EpP2P p, const uint32_t *epoch_p,
   }
   __syncthreads();
   if (!ok) return;
-  const float *contrib = reinterpret_cast<const float *>(p.base[p.rank] + p.off_contrib);
+  // the owners' int16 rows and their per-(route, 32-row block) scales
+  const int16_t *q16 = reinterpret_cast<const int16_t *>(p.base[p.rank] + p.off_contrib);
+  const float *sc = reinterpret_cast<const float *>(p.base[p.rank] + p.off_cscale);
+  const int hb = (H + 31) / 32;
   bool bad = false;
-  // slot order as the single-GPU combine; 4 columns per thread, all K slot
-  // loads issued before the first add (the peers' stores reached this
-  // buffer before their flags C, so the loads bypass L1)
+  // slot order as the single-GPU combine; 4 columns per thread (one scale
+  // block), all K slot loads issued before the first add (the peers' stores
+  // reached these buffers before their flags C, so the loads bypass L1)
   const bool vec = (H & 3) == 0 && K <= kMaxTopK &&
-                   (((uintptr_t)out | (uintptr_t)resid | (uintptr_t)contrib) & 15) == 0 &&
+                   (((uintptr_t)out | (uintptr_t)resid) & 15) == 0 &&
                    (size_t)T * H / 4 < (1u << 31);
   if (vec) {
     const uint32_t H4 = H / 4, n4 = (uint32_t)((size_t)T * H / 4);
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4;
          i += gridDim.x * blockDim.x) {
-      const uint32_t t = i / H4, j4 = i - t * H4;
+      const uint32_t t = i / H4, j4 = i - t * H4, j = 4 * j4;
       float4 acc = resid ? reinterpret_cast<const float4 *>(resid)[i] : make_float4(0, 0, 0, 0);
-      const float4 *c = reinterpret_cast<const float4 *>(contrib) + (size_t)t * K * H4 + j4;
-      float4 v[kMaxTopK];
-#pragma unroll
-      for (int k = 0; k < kMaxTopK; ++k)
-        if (k < K) v[k] = __ldcg(c + (size_t)k * H4);
+      uint2 v[kMaxTopK];
+      float f[kMaxTopK];
 #pragma unroll
       for (int k = 0; k < kMaxTopK; ++k)
         if (k < K) {
-          acc.x = __fadd_rn(acc.x, v[k].x);
-          acc.y = __fadd_rn(acc.y, v[k].y);
-          acc.z = __fadd_rn(acc.z, v[k].z);
-          acc.w = __fadd_rn(acc.w, v[k].w);
+          const size_t row = (size_t)t * K + k;
+          v[k] = __ldcg(reinterpret_cast<const uint2 *>(q16 + row * H + j));
+          f[k] = __ldcg(sc + row * hb + j / 32);
+        }
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K) {
+          acc.x = __fmaf_rn((float)(int16_t)(v[k].x & 0xFFFFu), f[k], acc.x);
+          acc.y = __fmaf_rn((float)(int16_t)(v[k].x >> 16), f[k], acc.y);
+          acc.z = __fmaf_rn((float)(int16_t)(v[k].y & 0xFFFFu), f[k], acc.z);
+          acc.w = __fmaf_rn((float)(int16_t)(v[k].y >> 16), f[k], acc.w);
         }
       bad |= !(is_finite_f(acc.x) && is_finite_f(acc.y) && is_finite_f(acc.z) &&
                is_finite_f(acc.w));
@@ -490,7 +481,10 @@ __global__ void ep_wait_combine_kernel(EpP2P p, const uint32_t *epoch_p,
          i += (size_t)gridDim.x * blockDim.x) {
       const size_t t = i / H, j = i % H;
       float acc = resid ? resid[i] : 0.0f;
-      for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __ldcg(contrib + (t * K + k) * H + j));
+      for (int k = 0; k < K; ++k) {
+        const size_t row = t * K + k;
+        acc = __fmaf_rn((float)__ldcg(q16 + row * H + j), __ldcg(sc + row * hb + j / 32), acc);
+      }
       bad |= !is_finite_f(acc);
       out[i] = acc;
     }

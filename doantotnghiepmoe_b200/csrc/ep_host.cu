@@ -81,7 +81,8 @@ void ep_setup_p2p(moe_handle *h, size_t Tm) {
   P.off_tok = off;     off = align_up(off + RR * 4, 1024);
   P.off_slot = off;    off = align_up(off + RR * 4, 1024);
   P.off_amax = off;    off = align_up(off + RR * 4, 1024);
-  P.off_contrib = off; off = align_up(off + Tm * K * H * 4, 1024);
+  P.off_contrib = off; off = align_up(off + Tm * K * H * 2, 1024);
+  P.off_cscale = off;  off = align_up(off + Tm * K * ((H + 31) / 32) * 4, 1024);
   P.rank = ep.rank;
   P.nranks = N;
   P.wait_cycles = h->wait_flag_cycles;
@@ -399,8 +400,11 @@ moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const floa
     a.r_slot = (const int32_t *)(me + P.off_slot);
     a.r_gate = (const float *)(me + P.off_gate);
     a.r_rank = (const int32_t *)(me + P.off_rank);
-    for (int q = 0; q < P.nranks; ++q) a.peer_contrib[q] = (float *)(P.base[q] + P.off_contrib);
-    a.contrib = a.peer_contrib[P.rank];
+    for (int q = 0; q < P.nranks; ++q) {
+      a.peer_c16[q] = (int16_t *)(P.base[q] + P.off_contrib);
+      a.peer_cscale[q] = (float *)(P.base[q] + P.off_cscale);
+    }
+    a.contrib = nullptr;
     a.status = h->status;
     cudaEvent_t p3 = h->prof.begin(s);
     e = tc::launch_gate_up_tc(EL.map_gu, bn == 64 ? ep.map_x64 : ep.map_x128, a, bn,

@@ -264,6 +264,35 @@ __device__ __forceinline__ float warp_colmax16(float (&m)[16]) {
   return fmaxf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 1));
 }
 
+// Expert-parallel return of a warp's 32 output rows (this lane: row j) for
+// 16 route columns c0 .. c0 + 15 of the tile: int16 values with one scale per
+// (route, 32-row block), q = rint(v * 32767 / m), m = max |v| over the block;
+// the source rank multiplies back by m / 32767 (per-element error <= m /
+// 65534).  No cross-warp synchronisation: each warp owns its block.
+__device__ __forceinline__ void ep_store16(const TcArgs &a, const RouteTab &tab, int c0, int nr,
+                                           int j, int jblk, float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+  float mx[16];
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) mx[jj] = fabsf(v[jj]);
+  const float m = warp_colmax16(mx);  // lane l: column (l >> 1) & 15
+  const int hb = (a.H + 31) / 32;
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    const int c = c0 + jj;
+    const float mc = __shfl_sync(0xffffffffu, m, 2 * jj);
+    if (c < nr) {
+      const size_t row = (size_t)tab.tok[c] * a.K + tab.slot[c];
+      if (j < a.H) {
+        const float f = mc > 0.0f ? 32767.0f / mc : 0.0f;
+        const float q = fminf(fmaxf(rintf(v[jj] * f), -32767.0f), 32767.0f);
+        a.peer_c16[tab.rank[c]][row * a.H + j] = (int16_t)q;
+      }
+      if (lane == 2 * jj) a.peer_cscale[tab.rank[c]][row * hb + jblk] = mc / 32767.0f;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // GEMM 1: gate/up.  A = gate rows [m0, m0+128) and up rows [I+m0, ...) of
 // expert e; B = the two digit planes of the tile's routes.  BN routes per
@@ -384,18 +413,21 @@ __global__ void __launch_bounds__(kThreads, MINB)
         tmem_ld16(trow + c0, v[0]);
         tmem_ld16(trow + BN + c0, v[1]);
         tmem_wait_ld();
+        float gy[16];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const int c = c0 + jj;
+          gy[jj] = 0.0f;
           if (c < nr && j < a.H) {
             const float y = digits::down(v[0][jj], v[1][jj], tab.s1[c], tab.s2[c], sd);
             bad |= !is_finite_f(y);
-            // expert parallelism: the row goes straight to the source rank's
-            // contribution buffer (peer memory over NVLink)
-            float *dst = a.r_rank ? a.peer_contrib[tab.rank[c]] : a.contrib;
-            dst[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + j] = __fmul_rn(tab.gate[c], y);
+            gy[jj] = __fmul_rn(tab.gate[c], y);
+            if (!a.r_rank) a.contrib[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + j] = gy[jj];
           }
         }
+        // expert parallelism: the rows go straight to the source ranks'
+        // buffers (peer memory over NVLink)
+        if (a.r_rank) ep_store16(a, tab, c0, nr, j, (m0 + 32 * q) / 32, gy);
       }
       if (bad) set_status(a.status, kStatusNonFinite);
     }
@@ -675,16 +707,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(trow + c0, v[0]);
         tmem_ld16(trow + PBN + c0, v[1]);
         tmem_wait_ld();
+        float gy[16];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const int c = c0 + jj;
+          gy[jj] = 0.0f;
           if (c < nr && jr < a.H) {
             const float y = digits::down(v[0][jj], v[1][jj], tab.s1[c], tab.s2[c], sd);
             bad |= !is_finite_f(y);
-            float *dst = a.r_rank ? a.peer_contrib[tab.rank[c]] : a.contrib;
-            dst[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + jr] = __fmul_rn(tab.gate[c], y);
+            gy[jj] = __fmul_rn(tab.gate[c], y);
+            if (!a.r_rank)
+              a.contrib[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + jr] = gy[jj];
           }
         }
+        if (a.r_rank) ep_store16(a, tab, c0, nr, jr, (m * BM + 32 * qd) / 32, gy);
       }
       fence_before_sync();
       __syncwarp();

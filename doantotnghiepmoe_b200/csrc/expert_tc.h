@@ -54,9 +54,12 @@ struct TcArgs {
   const float *r_gate;
   float *contrib;              // [T, K, H]
   // expert parallelism over peer memory: when r_rank is set, route r's row
-  // goes to peer_contrib[r_rank[r]] (the source rank's [T, K, H] buffer)
+  // goes to the source rank r_rank[r] as int16 values peer_c16[rank] [T, K, H]
+  // with one scale per (route, 32-row block) in peer_cscale[rank]
+  // [T, K, ceil(H / 32)]: value = q * scale (see ep_store16)
   const int32_t *r_rank;
-  float *peer_contrib[8];
+  int16_t *peer_c16[8];
+  float *peer_cscale[8];
   uint32_t *status;
 };
 

@@ -425,6 +425,12 @@ DigitArgs digit_args(moe_handle *h, int T) {
   // the down rows of a single-token launch (<= K experts) fit in L2 beside
   // the gate/up stream
   a.prefetch_down = T == 1 && (size_t)h->d.top_k * h->d.hidden * h->d.intermediate <= (48u << 20);
+  // MOE_DIGIT_PREFETCH=0 in the environment turns the down-row prefetch off
+  static const bool prefetch_env = [] {
+    const char *v = getenv("MOE_DIGIT_PREFETCH");
+    return !(v && v[0] == '0');
+  }();
+  a.prefetch_down = a.prefetch_down && prefetch_env;
   if (h->prof.on) {
     a.phase_ts = h->phase_ts;
     h->phase_pending = true;

@@ -1,8 +1,11 @@
 """Expert parallelism on 2 GPUs (skipped with fewer): experts split over two
 processes, tokens split over two processes, dispatch/combine inside the
-library over both transports (kernels writing into peer memory, and NCCL).  Each rank's output rows must equal, bit for bit, the single-GPU
-tensor-core path run on the same rank with all experts resident; routing must
-equal the CPU oracle's."""
+library over both transports (kernels writing into peer memory, and NCCL).
+Routing must equal the CPU oracle's and outputs stay within 1e-3 of it.
+Against the single-GPU tensor-core path on the same rank with all experts
+resident: the NCCL transport returns fp32 rows and is bit-identical; the
+peer-memory transport returns int16 rows with a scale per (route, 32-row
+block), within 1e-4 of it."""
 import os
 import socket
 import tempfile
@@ -94,6 +97,9 @@ def test_expert_parallel_two_gpus_bit_exact(transport):
             ep = np.load(os.path.join(d, f"ep{r}.npy"))
             tc = np.load(os.path.join(d, f"tc{r}.npy"))
             ids = np.load(os.path.join(d, f"ids{r}.npy")).astype(np.uint32)
-            assert np.array_equal(ep.view(np.uint32), tc.view(np.uint32)), r
+            if transport == "nccl":
+                assert np.array_equal(ep.view(np.uint32), tc.view(np.uint32)), r
+            else:
+                assert helpers.rel_err(ep, tc) < 1e-4, r
             assert np.array_equal(ids, ref.ids[r * 96:(r + 1) * 96])
             assert helpers.rel_err(ep, ref.out[r * 96:(r + 1) * 96]) < 1e-3
