@@ -663,6 +663,11 @@ __device__ void gate_up_phase(const DigitArgs &a, uint8_t *xd, DTables &tb) {
     const int e = tb.act_e[ai];
     const int8_t *W = tb.wp[e];
     const float *S = tb.sp[e];
+    // this share's gate and up rows head for L2 while the digits are staged
+    if (tid == 0) {
+      prefetch_l2(W + (size_t)i0 * H, (uint32_t)((i1 - i0) * H));
+      prefetch_l2(W + (size_t)(I + i0) * H, (uint32_t)((i1 - i0) * H));
+    }
     for (int rb = r0; rb < r1; rb += kGR) {
       const int nr = min(kGR, r1 - rb);
       // the digit planes of routes rb .. rb + nr (2H bytes each) and scales
