@@ -10,6 +10,8 @@
 // owner of the token in slot order; results are bit-identical to the
 // single-GPU tensor-core path.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "digits.cuh"
@@ -292,7 +294,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const float *__restrict__ x, const int32_t *__restrict__ seg_off,
     const uint32_t *__restrict__ ids, const float *__restrict__ gates,
     const int32_t *__restrict__ r_pos, const int32_t *__restrict__ owner, int E, int T, int K,
-    int H, EpP2P p, const uint32_t *epoch_p, uint32_t *done, uint32_t *status) {
+    int H, EpP2P p, const uint32_t *epoch_p, uint32_t *done, uint32_t *status, int per_token) {
   __shared__ int32_t tot[kMaxExperts], base[kMaxExperts], segs[kMaxExperts + 1];
   __shared__ int ok;
   const uint32_t epoch = *epoch_p;
@@ -310,50 +312,115 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
         reinterpret_cast<const int32_t *>(p.base[p.rank] + p.off_counts) + (size_t)par * p.nranks * E;
     ep_dest_bases(cm, owner, E, p.rank, p.nranks, tot, base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // one warp per route: it digitises its token's row (every route of a
-    // token gets the same digits) and stores them at the route's row in its
-    // owner's expert-sorted buffer.  With a warp per route rather than per
-    // token, every SM issues peer stores.
-    const int R = T * K;
-    for (int r = blockIdx.x * 8 + warp; r < R; r += gridDim.x * 8) {
-      const uint32_t e = ids[r];
-      const int rp = r_pos[r];
-      if (!(e < (uint32_t)E && rp >= 0)) continue;  // warp-uniform
-      const int t = r / K, slot = r - t * K;
-      const int q = owner[e];
-      const int pos = base[e] + (rp - segs[e]);
-      uint8_t *dst = peer_at(p, q, p.off_xq) + (size_t)pos * H;
-      const float *xr = x + (size_t)t * H;
-      // the single-GPU tensor path's two-digit quantization of the row
-      float amax = 0.0f;
-      for (int c = lane * 4; c < H; c += 128) {
-        const float4 v = *reinterpret_cast<const float4 *>(xr + c);
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float s = digits::row_scale(amax);
-      const float inv = 1.0f / s;
-      // 16 elements per lane per pass: 16-byte stores, 512 bytes per warp
-      // instruction on the link (H is a multiple of 16)
-      for (int c = lane * 16; c < H; c += 512) {
-        uint32_t p1[4], p2[4];
-#pragma unroll
-        for (int w4 = 0; w4 < 4; ++w4) {
-          const float4 v = *reinterpret_cast<const float4 *>(xr + c + 4 * w4);
-          p1[w4] = digits::split4(v.x, v.y, v.z, v.w, inv, p2[w4]);
+    if (per_token) {
+      // one warp per token: the row is quantized once and stored at each of
+      // its K routes' rows in their owners' expert-sorted buffers
+      for (int t = blockIdx.x * 8 + warp; t < T; t += gridDim.x * 8) {
+        int q = 0, pos = 0, slot_ok = 0;
+        float g = 0.0f;
+        if (lane < K) {
+          const uint32_t e = ids[(size_t)t * K + lane];
+          const int r = r_pos[(size_t)t * K + lane];
+          if (e < (uint32_t)E && r >= 0) {
+            q = owner[e];
+            pos = base[e] + (r - segs[e]);
+            g = gates[(size_t)t * K + lane];
+            slot_ok = 1;
+          }
         }
-        *reinterpret_cast<uint4 *>(dst + c) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
-        *reinterpret_cast<uint4 *>(dst + p.plane + c) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+        const unsigned vmask = __ballot_sync(0xffffffffu, slot_ok);
+        uint8_t *dst[kMaxTopK];
+  #pragma unroll
+        for (int k = 0; k < kMaxTopK; ++k) {
+          const int qk = __shfl_sync(0xffffffffu, q, k);
+          const int pk = __shfl_sync(0xffffffffu, pos, k);
+          dst[k] = peer_at(p, qk, p.off_xq) + (size_t)pk * H;
+        }
+        const float *xr = x + (size_t)t * H;
+        // the single-GPU tensor path's two-digit quantization of the row
+        float amax = 0.0f;
+        for (int c = lane * 4; c < H; c += 128) {
+          const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+          amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+  #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float s = digits::row_scale(amax);
+        const float inv = 1.0f / s;
+        // 16 elements per lane per pass: 16-byte stores, 512 bytes per warp
+        // instruction on the link (H is a multiple of 16)
+        for (int c = lane * 16; c < H; c += 512) {
+          uint32_t p1[4], p2[4];
+  #pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + c + 4 * w4);
+            p1[w4] = digits::split4(v.x, v.y, v.z, v.w, inv, p2[w4]);
+          }
+          const uint4 v1 = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+          const uint4 v2 = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+  #pragma unroll
+          for (int k = 0; k < kMaxTopK; ++k)
+            if ((vmask >> k) & 1u) {
+              *reinterpret_cast<uint4 *>(dst[k] + c) = v1;
+              *reinterpret_cast<uint4 *>(dst[k] + p.plane + c) = v2;
+            }
+        }
+        if (slot_ok) {
+          reinterpret_cast<float *>(peer_at(p, q, p.off_s1))[pos] = s;
+          reinterpret_cast<float *>(peer_at(p, q, p.off_s2))[pos] = s / 254.0f;
+          reinterpret_cast<float *>(peer_at(p, q, p.off_gate))[pos] = g;
+          reinterpret_cast<int32_t *>(peer_at(p, q, p.off_rank))[pos] = p.rank;
+          reinterpret_cast<int32_t *>(peer_at(p, q, p.off_tok))[pos] = t;
+          reinterpret_cast<int32_t *>(peer_at(p, q, p.off_slot))[pos] = lane;
+          reinterpret_cast<uint32_t *>(peer_at(p, q, p.off_amax))[pos] = 0u;
+        }
       }
-      if (lane == 0) {
-        reinterpret_cast<float *>(peer_at(p, q, p.off_s1))[pos] = s;
-        reinterpret_cast<float *>(peer_at(p, q, p.off_s2))[pos] = s / 254.0f;
-        reinterpret_cast<float *>(peer_at(p, q, p.off_gate))[pos] = gates[r];
-        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_rank))[pos] = p.rank;
-        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_tok))[pos] = t;
-        reinterpret_cast<int32_t *>(peer_at(p, q, p.off_slot))[pos] = slot;
-        reinterpret_cast<uint32_t *>(peer_at(p, q, p.off_amax))[pos] = 0u;
+    } else {
+      // one warp per route: it digitises its token's row (every route of a
+      // token gets the same digits) and stores them at the route's row in its
+      // owner's expert-sorted buffer.  With a warp per route rather than per
+      // token, every SM issues peer stores.
+      const int R = T * K;
+      for (int r = blockIdx.x * 8 + warp; r < R; r += gridDim.x * 8) {
+        const uint32_t e = ids[r];
+        const int rp = r_pos[r];
+        if (!(e < (uint32_t)E && rp >= 0)) continue;  // warp-uniform
+        const int t = r / K, slot = r - t * K;
+        const int q = owner[e];
+        const int pos = base[e] + (rp - segs[e]);
+        uint8_t *dst = peer_at(p, q, p.off_xq) + (size_t)pos * H;
+        const float *xr = x + (size_t)t * H;
+        // the single-GPU tensor path's two-digit quantization of the row
+        float amax = 0.0f;
+        for (int c = lane * 4; c < H; c += 128) {
+          const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+          amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+  #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float s = digits::row_scale(amax);
+        const float inv = 1.0f / s;
+        // 16 elements per lane per pass: 16-byte stores, 512 bytes per warp
+        // instruction on the link (H is a multiple of 16)
+        for (int c = lane * 16; c < H; c += 512) {
+          uint32_t p1[4], p2[4];
+  #pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + c + 4 * w4);
+            p1[w4] = digits::split4(v.x, v.y, v.z, v.w, inv, p2[w4]);
+          }
+          *reinterpret_cast<uint4 *>(dst + c) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+          *reinterpret_cast<uint4 *>(dst + p.plane + c) = make_uint4(p2[0], p2[1], p2[2], p2[3]);
+        }
+        if (lane == 0) {
+          reinterpret_cast<float *>(peer_at(p, q, p.off_s1))[pos] = s;
+          reinterpret_cast<float *>(peer_at(p, q, p.off_s2))[pos] = s / 254.0f;
+          reinterpret_cast<float *>(peer_at(p, q, p.off_gate))[pos] = gates[r];
+          reinterpret_cast<int32_t *>(peer_at(p, q, p.off_rank))[pos] = p.rank;
+          reinterpret_cast<int32_t *>(peer_at(p, q, p.off_tok))[pos] = t;
+          reinterpret_cast<int32_t *>(peer_at(p, q, p.off_slot))[pos] = slot;
+          reinterpret_cast<uint32_t *>(peer_at(p, q, p.off_amax))[pos] = 0u;
+        }
       }
     }
   }
@@ -442,6 +509,27 @@ __global__ void ep_wait_combine_kernel(EpP2P p, const uint32_t *epoch_p,
   const float *sc = reinterpret_cast<const float *>(p.base[p.rank] + p.off_cscale);
   const int hb = (H + 31) / 32;
   bool bad = false;
+  if (!p.ret16) {
+    // fp32 rows: slot order as the single-GPU combine (bit-identical)
+    const float *c32 = reinterpret_cast<const float *>(p.base[p.rank] + p.off_contrib);
+    const size_t n = (size_t)T * H;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+      const size_t t = i / H, j = i % H;
+      float acc = resid ? resid[i] : 0.0f;
+      float v[kMaxTopK];
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K) v[k] = __ldcg(c32 + (t * K + k) * H + j);
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K) acc = __fadd_rn(acc, v[k]);
+      bad |= !is_finite_f(acc);
+      out[i] = acc;
+    }
+    if (bad) set_status(status, kStatusNonFinite);
+    return;
+  }
   // slot order as the single-GPU combine; 4 columns per thread (one scale
   // block), all K slot loads issued before the first add (the peers' stores
   // reached these buffers before their flags C, so the loads bypass L1)
@@ -505,8 +593,14 @@ cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const uin
                                int E, int T, int K, int H, const EpP2P &p, const uint32_t *epoch,
                                uint32_t *done, int grid, uint32_t *status, cudaStream_t s) {
   if (K > kMaxTopK) return cudaErrorInvalidValue;
+  // one warp per token (default) or per route: MOE_EP_DISPATCH=route (the
+  // two measured the same on 2 B200s: 86.5 vs 92.7 us at C4)
+  static const int per_token = [] {
+    const char *v = getenv("MOE_EP_DISPATCH");
+    return v && strcmp(v, "route") == 0 ? 0 : 1;
+  }();
   ep_dispatch_kernel<<<grid, 256, 0, s>>>(x, seg_off, ids, gates, r_pos, owner, E, T, K, H, p,
-                                          epoch, done, status);
+                                          epoch, done, status, per_token);
   return cudaGetLastError();
 }
 

@@ -81,10 +81,15 @@ void ep_setup_p2p(moe_handle *h, size_t Tm) {
   P.off_tok = off;     off = align_up(off + RR * 4, 1024);
   P.off_slot = off;    off = align_up(off + RR * 4, 1024);
   P.off_amax = off;    off = align_up(off + RR * 4, 1024);
-  P.off_contrib = off; off = align_up(off + Tm * K * H * 2, 1024);
+  P.off_contrib = off; off = align_up(off + Tm * K * H * 4, 1024);  // room for f32 rows
   P.off_cscale = off;  off = align_up(off + Tm * K * ((H + 31) / 32) * 4, 1024);
   P.rank = ep.rank;
   P.nranks = N;
+  // return rows as fp32 (default) or as int16 with a scale per 32 rows:
+  // MOE_EP_RETURN=i16.  On 2 B200s the int16 epilogue cost more than the
+  // halved traffic saved (down GEMM 331 vs 203 us at C4), so fp32 stays.
+  const char *ret = getenv("MOE_EP_RETURN");
+  P.ret16 = ret && strcmp(ret, "i16") == 0;
   P.wait_cycles = h->wait_flag_cycles;
   void *region = nullptr;
   if (cudaMalloc(&region, off) != cudaSuccess || cudaMemset(region, 0, off) != cudaSuccess) {
@@ -403,8 +408,10 @@ moe_status ep_forward_p2p(moe_handle *h, int layer, const float *d_h, const floa
     for (int q = 0; q < P.nranks; ++q) {
       a.peer_c16[q] = (int16_t *)(P.base[q] + P.off_contrib);
       a.peer_cscale[q] = (float *)(P.base[q] + P.off_cscale);
+      a.peer_c32[q] = (float *)(P.base[q] + P.off_contrib);
     }
     a.contrib = nullptr;
+    a.ret16 = P.ret16;
     a.status = h->status;
     cudaEvent_t p3 = h->prof.begin(s);
     e = tc::launch_gate_up_tc(EL.map_gu, bn == 64 ? ep.map_x64 : ep.map_x128, a, bn,

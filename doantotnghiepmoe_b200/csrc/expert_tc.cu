@@ -293,6 +293,21 @@ __device__ __forceinline__ void ep_store16(const TcArgs &a, const RouteTab &tab,
   }
 }
 
+// The same columns as fp32 rows (ret16 == 0), or as int16 rows with scales.
+__device__ __forceinline__ void ep_store(const TcArgs &a, const RouteTab &tab, int c0, int nr,
+                                         int j, int jblk, float (&v)[16]) {
+  if (a.ret16) {
+    ep_store16(a, tab, c0, nr, j, jblk, v);
+    return;
+  }
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    const int c = c0 + jj;
+    if (c < nr && j < a.H)
+      a.peer_c32[tab.rank[c]][((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + j] = v[jj];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // GEMM 1: gate/up.  A = gate rows [m0, m0+128) and up rows [I+m0, ...) of
 // expert e; B = the two digit planes of the tile's routes.  BN routes per
@@ -427,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
         }
         // expert parallelism: the rows go straight to the source ranks'
         // buffers (peer memory over NVLink)
-        if (a.r_rank) ep_store16(a, tab, c0, nr, j, (m0 + 32 * q) / 32, gy);
+        if (a.r_rank) ep_store(a, tab, c0, nr, j, (m0 + 32 * q) / 32, gy);
       }
       if (bad) set_status(a.status, kStatusNonFinite);
     }
@@ -720,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               a.contrib[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + jr] = gy[jj];
           }
         }
-        if (a.r_rank) ep_store16(a, tab, c0, nr, jr, (m * BM + 32 * qd) / 32, gy);
+        if (a.r_rank) ep_store(a, tab, c0, nr, jr, (m * BM + 32 * qd) / 32, gy);
       }
       fence_before_sync();
       __syncwarp();

@@ -57,9 +57,12 @@ struct TcArgs {
   // goes to the source rank r_rank[r] as int16 values peer_c16[rank] [T, K, H]
   // with one scale per (route, 32-row block) in peer_cscale[rank]
   // [T, K, ceil(H / 32)]: value = q * scale (see ep_store16)
+  // (ret16), or as fp32 rows peer_c32[rank] [T, K, H] (ret16 == 0)
   const int32_t *r_rank;
+  int ret16;
   int16_t *peer_c16[8];
   float *peer_cscale[8];
+  float *peer_c32[8];
   uint32_t *status;
 };
 

@@ -211,9 +211,10 @@ struct EpP2P {
   size_t off_counts;           // int32 [2][nranks][E] route counts by source rank
   size_t off_xq, plane;        // int8 [2][RR][H] digit planes (plane = RR * H)
   size_t off_s1, off_s2, off_gate, off_rank, off_tok, off_slot, off_amax;  // [RR]
-  size_t off_contrib;          // int16 [T, K, H] outputs of this rank's routes, written by
-                               // their owners (value = q * scale)
-  size_t off_cscale;           // f32 [T, K, ceil(H / 32)] scales of off_contrib
+  size_t off_contrib;          // outputs of this rank's routes, written by their owners:
+                               // int16 [T, K, H] (value = q * scale) when ret16, else f32
+  size_t off_cscale;           // f32 [T, K, ceil(H / 32)] scales of the int16 rows
+  int ret16;                   // return format (MOE_EP_RETURN)
   long long wait_cycles;       // bound of every flag wait (SM clock cycles)
 };
 // epoch: this rank's call counter in device memory; the publish kernel

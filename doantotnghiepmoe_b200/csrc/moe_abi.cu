@@ -1164,7 +1164,16 @@ extern "C" moe_status moe_route(moe_handle *h, int layer, const float *d_h, int 
   if (!h || !d_h || !d_ids || !d_gates) return MOE_ERR_INVALID;
   std::lock_guard<std::mutex> lock(h->mu);
   drop_graphs(h);
+  // routing needs only the router: a layer registered for expert
+  // parallelism (moe_ep_set_layer) routes too
   moe_status st = check_layer(h, layer, T);
+  if (st == MOE_ERR_STATE && h->layers[layer].router) {
+    st = MOE_OK;
+    if (T < 0 || T > h->d.max_tokens) {
+      set_err(h->err, "token count %d outside [0, %d]", T, h->d.max_tokens);
+      st = MOE_ERR_INVALID;
+    }
+  }
   if (st != MOE_OK || T == 0) return st;
   DeviceGuard g(h->device);
   h->last_launches = 0;

@@ -169,7 +169,8 @@ moe_status moe_set_layer_packed_q(moe_handle *h, int layer, const void *d_expert
                                   int quant);
 
 /* Routing only: ids/gates [T,K] (device).  probs (optional, device [T,E])
- * receives the post-softmax probabilities. */
+ * receives the post-softmax probabilities.  Needs only the layer's router,
+ * so it also serves layers registered with moe_ep_set_layer. */
 moe_status moe_route(moe_handle *h, int layer, const float *d_h, int T, uint32_t *d_ids,
                      float *d_gates, float *d_probs, void *stream);
 
@@ -272,10 +273,10 @@ moe_status moe_layer_forward_noalloc(const moe_dims *dims, const int8_t *d_exper
  *     moe_ep_init; no host synchronisation per layer); without peer mappings,
  *     or with MOE_EP_TRANSPORT=nccl in the environment, as NCCL
  *     point-to-point exchanges.  Routing is the single-GPU routing bit for
- *     bit.  The NCCL transport returns fp32 rows and equals the single-GPU
- *     tensor-core path bit for bit; the peer-memory transport returns each
- *     route's output row as int16 with one scale per 32 rows (error <= 1/65534
- *     of the block's largest value), within 1e-4 of it. 
+ *     bit, and with the default fp32 returns the outputs equal the
+ *     single-GPU tensor-core path bit for bit.  MOE_EP_RETURN=i16 sends each
+ *     route's output row as int16 with one scale per 32 rows instead (error
+ *     <= 1/65534 of the block's largest value; within 1e-4). 
  * ---------------------------------------------------------------------- */
 /* 128-byte NCCL unique id; rank 0 creates it and the host shares it. */
 moe_status moe_ep_unique_id(unsigned char id_out[128]);

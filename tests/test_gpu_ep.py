@@ -3,9 +3,9 @@ processes, tokens split over two processes, dispatch/combine inside the
 library over both transports (kernels writing into peer memory, and NCCL).
 Routing must equal the CPU oracle's and outputs stay within 1e-3 of it.
 Against the single-GPU tensor-core path on the same rank with all experts
-resident: the NCCL transport returns fp32 rows and is bit-identical; the
-peer-memory transport returns int16 rows with a scale per (route, 32-row
-block), within 1e-4 of it."""
+resident: fp32 returns (both transports' default) are bit-identical; the
+peer-memory transport's int16 returns (MOE_EP_RETURN=i16, a scale per
+(route, 32-row block)) are within 1e-4 of it."""
 import os
 import socket
 import tempfile
@@ -37,6 +37,8 @@ def _worker(rank, world, port, outdir, transport):
     torch.cuda.set_device(rank)
     if transport == "nccl":
         os.environ["MOE_EP_TRANSPORT"] = "nccl"
+    if transport == "p2p-i16":
+        os.environ["MOE_EP_RETURN"] = "i16"
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world, timeout=datetime.timedelta(seconds=120))
     H, I, E, K, T = 2048, 768, 16, 4, 96
@@ -50,7 +52,7 @@ def _worker(rank, world, port, outdir, transport):
     dist.broadcast(uid, 0)
     eng = M.MoeLayerEngine(M.MoeConfig(H, I, E, K, True, T, 1), device=rank)
     eng.ep_init(rank, world, bytes(uid.tolist()), owner)
-    assert eng.ep_transport() == transport, eng.ep_transport()
+    assert eng.ep_transport() == transport.split("-")[0], eng.ep_transport()
     loc = placement.local_experts(owner, rank)
     ex = torch.from_numpy(np.ascontiguousarray(lw.experts[loc])).cuda()
     sc = torch.from_numpy(np.ascontiguousarray(lw.scales[loc])).cuda()
@@ -79,7 +81,7 @@ def _worker(rank, world, port, outdir, transport):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["p2p", "nccl"])
+@pytest.mark.parametrize("transport", ["p2p", "nccl", "p2p-i16"])
 def test_expert_parallel_two_gpus_bit_exact(transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -97,7 +99,7 @@ def test_expert_parallel_two_gpus_bit_exact(transport):
             ep = np.load(os.path.join(d, f"ep{r}.npy"))
             tc = np.load(os.path.join(d, f"tc{r}.npy"))
             ids = np.load(os.path.join(d, f"ids{r}.npy")).astype(np.uint32)
-            if transport == "nccl":
+            if transport != "p2p-i16":
                 assert np.array_equal(ep.view(np.uint32), tc.view(np.uint32)), r
             else:
                 assert helpers.rel_err(ep, tc) < 1e-4, r
