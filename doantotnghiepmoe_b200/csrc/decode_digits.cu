@@ -55,9 +55,8 @@ constexpr int kRTT = 4;          // router task: tokens
 constexpr int kRTE = 4;          // router task: experts
 constexpr int kGR = 16;          // routes whose digit planes are staged at once
 constexpr int kMaxChunks = 4;    // 16-byte chunks per lane of a row (rows <= 2048 bytes)
+constexpr int kRowPad = 8;       // floats of padding per staged router-phase row
 
-constexpr int kGateW = 4;        // gate/up split: cost of a row pair = routes + kGateW
-constexpr int kDownW = 3;        // down split: cost of an output row = routes + kDownW
 
 struct DTables {
   int32_t run[kMaxExperts];               // counting-sort scratch
@@ -162,6 +161,9 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
   const int nte = (E + RE - 1) / RE;
   const int tasks = ntt * nte;
   const int full = H / 8;
+  // staged rows are kRowPad floats longer than H, so the 4 expert rows a
+  // warp reads at the same column fall in different banks
+  const int RS = H + kRowPad;
   const bool seq = a.route_mode == kRouteTopkSoftmax && L.router_dtype == kRouterF32;
   for (int task = blockIdx.x; task < tasks; task += gridDim.x) {
     const int t0 = (task / nte) * TT, e0 = (task % nte) * RE;
@@ -172,7 +174,7 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
       const int q = H / 4;
       for (int i = tid; i < (TT + RE) * q; i += kDT) {
         const int r = i / q, c = (i % q) * 4;
-        float *dst = stage + (size_t)r * H + c;
+        float *dst = stage + (size_t)r * RS + c;
         const float *src = nullptr;
         if (r < TT) {
           if (r < nt) src = xin + (size_t)(t0 + r) * H + c;
@@ -198,17 +200,17 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
         } else if (e0 + r - TT < E) {
           v = load_w(L.router, L.router_dtype, (size_t)(e0 + r - TT) * H + c);
         }
-        stage[i] = v;
+        stage[(size_t)r * RS + c] = v;
       }
     }
     __syncthreads();
     for (int i = tid; i < nt * H; i += kDT)
-      if (!is_finite_f(stage[i])) bad = true;
+      if (!is_finite_f(stage[(size_t)(i / H) * RS + i % H])) bad = true;
     if (stacked) {
       // RMSNorm of each staged token row (src/backend.rs:341-359): lanes 0..7
       // of warp r run the 8-lane sum of squares, then every thread scales.
       if (warp < nt) {
-        const float *x = stage + (size_t)warp * H;
+        const float *x = stage + (size_t)warp * RS;
         float acc = 0.0f;
         if (lane < 8)
           for (int c = 0; c < full; ++c) {
@@ -227,9 +229,10 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
       __syncthreads();
       for (int i = tid; i < nt * H; i += kDT) {
         const int r = i / H, j = i % H;
-        const float o = __fmul_rn(__fmul_rn(stage[i], tb.inv[r]), L.norm_w ? L.norm_w[j] : 1.0f);
+        float &v = stage[(size_t)r * RS + j];
+        const float o = __fmul_rn(__fmul_rn(v, tb.inv[r]), L.norm_w ? L.norm_w[j] : 1.0f);
         if (!is_finite_f(o)) bad = true;
-        stage[i] = o;
+        v = o;
       }
       __syncthreads();
     }
@@ -240,8 +243,8 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
       const int l8 = tid & 7, pair = tid >> 3;
       const bool live = pair < npairs;
       const int ti = live ? pair / RE : 0, ei = live ? pair % RE : 0;
-      const float *hs = stage + (size_t)ti * H;
-      const float *w = stage + (size_t)(TT + ei) * H;
+      const float *hs = stage + (size_t)ti * RS;
+      const float *w = stage + (size_t)(TT + ei) * RS;
       float logit;
       if (seq) {
         float acc = -0.0f;  // src/router.rs:59-62, Rust's f32 Sum folds from -0.0
@@ -270,7 +273,7 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
     // warps above the ones running the dot (token r on warp kDW - 1 - r)
     if (e0 == 0 && kDW - 1 - warp < nt) {
       const int r = kDW - 1 - warp;
-      const float *x = stage + (size_t)r * H;
+      const float *x = stage + (size_t)r * RS;
       float amax = 0.0f;
       for (int c = lane * 4; c < H; c += 128) {
         const float4 v = *reinterpret_cast<const float4 *>(x + c);
@@ -534,15 +537,15 @@ __device__ void build_tables(const DigitArgs &a, int R, DTables &tb) {
     }
   }
   __syncthreads();
-  // cost prefixes: a gate/up row pair costs (routes + kGateW), a down row
-  // (routes + kDownW), in units of one route's dot products
+  // cost prefixes: a gate/up row pair costs (routes + gate_w), a down row
+  // (routes + down_w), in units of one route's dot products
   if (warp == 0) {
     const int na = tb.n_active;
     int cg = 0, cd = 0;
     for (int base = 0; base < na; base += 32) {
       const int ai = base + lane;
       const int r = ai < na ? tb.act_r0[ai + 1] - tb.act_r0[ai] : 0;
-      int g = ai < na ? a.I * (r + kGateW) : 0, d = ai < na ? a.H * (r + kDownW) : 0;
+      int g = ai < na ? a.I * (r + a.gate_w) : 0, d = ai < na ? a.H * (r + a.down_w) : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int vg = __shfl_up_sync(0xffffffffu, g, o), vd = __shfl_up_sync(0xffffffffu, d, o);
@@ -587,8 +590,8 @@ __device__ void tables_single(const DigitArgs &a, DTables &tb) {
   }
   const int na = __popc(__ballot_sync(0xffffffffu, valid));
   if (lane <= na) {
-    tb.cost_g[lane] = lane * a.I * (1 + kGateW);
-    tb.cost_d[lane] = lane * a.H * (1 + kDownW);
+    tb.cost_g[lane] = lane * a.I * (1 + a.gate_w);
+    tb.cost_d[lane] = lane * a.H * (1 + a.down_w);
   }
   if (lane == 0) {
     tb.n_active = na;
@@ -645,7 +648,7 @@ __device__ void prefetch_down(const DigitArgs &a, const DTables &tb) {
     }
     return;
   }
-  for_each_share(tb, tb.cost_d, H, kDownW, [&](int ai, int j0, int j1, int, int) {
+  for_each_share(tb, tb.cost_d, H, a.down_w, [&](int ai, int j0, int j1, int, int) {
     prefetch_l2(tb.wp[tb.act_e[ai]] + (size_t)2 * I * H + (size_t)j0 * I,
                 (uint32_t)((j1 - j0) * I));
   });
@@ -659,7 +662,7 @@ template <int NCH>
 __device__ void gate_up_phase(const DigitArgs &a, uint8_t *xd, DTables &tb) {
   constexpr int kRows = 2;
   const int H = a.H, I = a.I, K = a.K, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for_each_share(tb, tb.cost_g, I, kGateW, [&](int ai, int i0, int i1, int r0, int r1) {
+  for_each_share(tb, tb.cost_g, I, a.gate_w, [&](int ai, int i0, int i1, int r0, int r1) {
     const int e = tb.act_e[ai];
     const int8_t *W = tb.wp[e];
     const float *S = tb.sp[e];
@@ -894,7 +897,7 @@ __device__ void down_items(const DigitArgs &a, uint8_t *xd, DTables &tb) {
   const int H = a.H, I = a.I, K = a.K, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ int32_t rows[kGR];
   bool bad = false;
-  for_each_share(tb, tb.cost_d, H, kDownW, [&](int ai, int j0, int j1, int r0, int r1) {
+  for_each_share(tb, tb.cost_d, H, a.down_w, [&](int ai, int j0, int j1, int r0, int r1) {
     const int e = tb.act_e[ai];
     const int8_t *Wd = tb.wp[e] + (size_t)2 * I * H;
     const float *Sd = tb.sp[e] + 2 * I;
@@ -1030,8 +1033,25 @@ __device__ bool run_layers(const DigitArgs &a, DTables &tb, uint8_t *stage) {
     if (a.prefetch_down) prefetch_down(a, tb);
     gate_up_phase<NCH>(a, stage, tb);
     if (first) stamp(a, 5);
+    if (first && a.phase_ts && threadIdx.x == 0) {
+      // per-CTA end of gate/up (profiling): [16 + 2048 + c]
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      a.phase_ts[16 + 2048 + blockIdx.x] = t;
+    }
     if (!sync()) return false;
     if (first) stamp(a, 6);
+    if (a.stacked && l + 1 < a.n_layers && threadIdx.x == 0) {
+      // the next layer's router rows head for L2 while this layer's down
+      // phase runs: each CTA prefetches one 16-byte-aligned slice
+      const FusedLayer &N = a.layers[l + 1];
+      const size_t rb = (size_t)a.E * a.H * (N.router_dtype == kRouterBF16 ? 2 : 4);
+      const size_t per = ((rb + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
+      const size_t o = per * blockIdx.x;
+      if (o < rb && (reinterpret_cast<uintptr_t>(N.router) & 15) == 0)
+        prefetch_l2(static_cast<const uint8_t *>(N.router) + o,
+                    (uint32_t)(std::min(per, (rb - o + 15) & ~size_t(15))));
+    }
     if (T == 1) {
       down_single<NCI>(a, resid, a.out, stage, tb);
     } else {
@@ -1082,7 +1102,7 @@ __global__ void __launch_bounds__(kDT, 2) digit_decode_kernel(DigitArgs a) {
 }
 
 size_t digit_smem_bytes(int H, int I) {
-  const size_t router = (size_t)(kRTT + kRTE) * H * sizeof(float);
+  const size_t router = (size_t)(kRTT + kRTE) * (H + kRowPad) * sizeof(float);
   const size_t digits = (size_t)kGR * 2 * std::max(H, I);
   return kStageOff + std::max(router, digits);
 }

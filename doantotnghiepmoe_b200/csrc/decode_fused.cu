@@ -42,6 +42,7 @@ using namespace gemv;
 constexpr int kFT = 256;          // threads per CTA (8 warps)
 constexpr int kRTT = 4;           // router task: tokens
 constexpr int kRTE = 4;           // router task: experts
+constexpr int kRowPad = 8;        // floats of padding per staged router row
 
 struct Tables {
   uint64_t tile_full[kTileStages];  // weight-tile ring mbarriers
@@ -109,6 +110,9 @@ __device__ void router_phase(const FusedArgs &a, const FusedLayer &L, const floa
   const int nte = (E + RE - 1) / RE;
   const int tasks = ntt * nte;
   const int full = H / 8;
+  // staged rows are kRowPad floats longer than H, so the 4 expert rows a
+  // warp reads at the same column fall in different banks
+  const int RS = H + kRowPad;
   // Router::select_top_k (src/router.rs:59-62) uses a plain sequential dot
   const bool seq = a.route_mode == kRouteTopkSoftmax && L.router_dtype == kRouterF32;
   for (int task = blockIdx.x; task < tasks; task += gridDim.x) {
@@ -123,7 +127,7 @@ __device__ void router_phase(const FusedArgs &a, const FusedLayer &L, const floa
       const int q = H / 4;
       for (int i = tid; i < (TT + RE) * q; i += kFT) {
         const int r = i / q, c = (i % q) * 4;
-        float *dst = stage + (size_t)r * H + c;
+        float *dst = stage + (size_t)r * RS + c;
         const float *src = nullptr;
         if (r < TT) {
           if (r < nt) src = hin + (size_t)(t0 + r) * H + c;
@@ -142,7 +146,7 @@ __device__ void router_phase(const FusedArgs &a, const FusedLayer &L, const floa
       asm volatile("cp.async.wait_all;" ::: "memory");
       __syncthreads();
       for (int i = tid; i < nt * H; i += kFT)
-        if (!is_finite_f(stage[i])) bad = true;
+        if (!is_finite_f(stage[(size_t)(i / H) * RS + i % H])) bad = true;
     } else {
       constexpr int kB = 8;
       for (int base = 0; base < total; base += kFT * kB) {
@@ -164,7 +168,7 @@ __device__ void router_phase(const FusedArgs &a, const FusedLayer &L, const floa
         for (int k = 0; k < kB; ++k) {
           const int i = base + k * kFT + tid;
           if (i < total) {
-            stage[i] = v[k];
+            stage[(size_t)(i / H) * RS + i % H] = v[k];
             if (i < TT * H && !is_finite_f(v[k])) bad = true;
           }
         }
@@ -180,8 +184,8 @@ __device__ void router_phase(const FusedArgs &a, const FusedLayer &L, const floa
       const int lane = tid & 7, pair = tid >> 3;
       const bool live = pair < npairs;
       const int ti = live ? pair / RE : 0, ei = live ? pair % RE : 0;
-      const float *hs = stage + (size_t)ti * H;
-      const float *w = stage + (size_t)(TT + ei) * H;
+      const float *hs = stage + (size_t)ti * RS;
+      const float *w = stage + (size_t)(TT + ei) * RS;
       float logit;
       if (seq) {
         float acc = -0.0f;  // src/router.rs:59-62, Rust's f32 Sum folds from -0.0
@@ -571,7 +575,7 @@ __global__ void __launch_bounds__(kFT, kMulti ? 1 : 2) fused_decode_kernel(Fused
 }
 
 size_t fused_smem_bytes(int H, int I, bool tiles) {
-  const size_t router = (size_t)(kRTT + kRTE) * H * sizeof(float);
+  const size_t router = (size_t)(kRTT + kRTE) * (H + kRowPad) * sizeof(float);
   // token rows, then (tile variants) the weight-tile ring on a 1024-byte
   // boundary
   const size_t gemv = (size_t)kTG * std::max(H, I) * sizeof(float) +

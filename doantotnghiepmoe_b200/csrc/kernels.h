@@ -177,6 +177,7 @@ struct DigitArgs {
   long long wait_cycles;     // bound of each grid-barrier wait (SM clock cycles)
   int router_async;          // routers of every layer are 16-byte aligned f32 rows
   int prefetch_down;         // prefetch the down rows into L2 during gate/up
+  int gate_w, down_w;        // work-split costs: a row costs (its expert's routes + w)
   unsigned long long *phase_ts;  // optional [9] phase timestamps (profiling)
 };
 bool digit_decode_supported(int T, int H, int I, int E, int K);

@@ -431,6 +431,17 @@ DigitArgs digit_args(moe_handle *h, int T) {
     return !(v && v[0] == '0');
   }();
   a.prefetch_down = a.prefetch_down && prefetch_env;
+  // work-split costs (MOE_DIGIT_GW / MOE_DIGIT_DW override them for tuning)
+  static const int gate_w = [] {
+    const char *v = getenv("MOE_DIGIT_GW");
+    return v ? std::max(0, atoi(v)) : 2;
+  }();
+  static const int down_w = [] {
+    const char *v = getenv("MOE_DIGIT_DW");
+    return v ? std::max(0, atoi(v)) : 3;
+  }();
+  a.gate_w = gate_w;
+  a.down_w = down_w;
   if (h->prof.on) {
     a.phase_ts = h->phase_ts;
     h->phase_pending = true;
@@ -720,7 +731,7 @@ extern "C" moe_status moe_create(int device, const moe_dims *dims, moe_handle **
   ok = ok && dalloc(&h->d_flayers, d.num_layers) == cudaSuccess;
   ok = ok && dalloc(&h->tok_cnt, T) == cudaSuccess && dalloc(&h->fbar, 1) == cudaSuccess;
   ok = ok && cudaMemset(h->tok_cnt, 0, T * sizeof(uint32_t)) == cudaSuccess;
-  ok = ok && dalloc(&h->phase_ts, 16 + 2 * 1024) == cudaSuccess;  // + per-CTA start, end
+  ok = ok && dalloc(&h->phase_ts, 16 + 3 * 1024) == cudaSuccess;  // + per-CTA start, end
   ok = ok && dalloc(&h->dbar, 2) == cudaSuccess &&
        cudaMemset(h->dbar, 0, 2 * sizeof(uint32_t)) == cudaSuccess;
   ok = ok && dalloc(&h->probe_flag, 1) == cudaSuccess &&
@@ -1515,7 +1526,7 @@ extern "C" moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int 
   if (h->phase_pending) {
     // phases of the most recent profiled fused launch (first layer; the
     // last entry runs to the end of the launch)
-    std::vector<unsigned long long> all(16 + 2 * 1024, 0);
+    std::vector<unsigned long long> all(16 + 3 * 1024, 0);
     unsigned long long *ts = all.data();
     if (cudaMemcpy(ts, h->phase_ts, all.size() * sizeof(unsigned long long),
                    cudaMemcpyDeviceToHost) == cudaSuccess) {
@@ -1542,10 +1553,17 @@ extern "C" moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int 
           s0 = std::min(s0, a0), s1 = std::max(s1, a0), e0 = std::min(e0, a1), e1 = std::max(e1, a1);
         }
         if (s1 >= s0 && e1 >= e0 && s0 != ~0ull) {
-          const char *nm[3] = {"digit:cta_start_spread", "digit:cta_end_spread",
-                               "digit:first_to_last"};
-          const unsigned long long v[3] = {s1 - s0, e1 - e0, e1 - s0};
-          for (int i = 0; i < 3; ++i) {
+          // spread of the CTAs' gate/up end times (first layer)
+          unsigned long long g0 = ~0ull, g1 = 0;
+          for (int c = 0; c < 1024; ++c) {
+            const unsigned long long g = ts[16 + 2048 + c];
+            if (g < s0 || g > e1) continue;
+            g0 = std::min(g0, g), g1 = std::max(g1, g);
+          }
+          const char *nm[4] = {"digit:cta_start_spread", "digit:cta_end_spread",
+                               "digit:first_to_last", "digit:gate_up_end_spread"};
+          const unsigned long long v[4] = {s1 - s0, e1 - e0, e1 - s0, g1 >= g0 ? g1 - g0 : 0};
+          for (int i = 0; i < 4; ++i) {
             moe_kernel_time k{};
             snprintf(k.name, sizeof k.name, "%s", nm[i]);
             k.launches = 1;
