@@ -172,51 +172,68 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
     // stage rows [0, TT) tokens, [TT, TT + RE) router rows
     if (a.router_async) {
       const int q = H / 4;
-      for (int i = tid; i < (TT + RE) * q; i += kDT) {
-        const int r = i / q, c = (i % q) * 4;
-        float *dst = stage + (size_t)r * RS + c;
-        const float *src = nullptr;
+      for (int r = 0; r < TT + RE; ++r) {
+        const float *row = nullptr;
         if (r < TT) {
-          if (r < nt) src = xin + (size_t)(t0 + r) * H + c;
+          if (r < nt) row = xin + (size_t)(t0 + r) * H;
         } else if (e0 + r - TT < E) {
-          src = reinterpret_cast<const float *>(L.router) + (size_t)(e0 + r - TT) * H + c;
+          row = reinterpret_cast<const float *>(L.router) + (size_t)(e0 + r - TT) * H;
         }
-        if (src) {
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                           (uint32_t)__cvta_generic_to_shared(dst)),
-                       "l"(src)
-                       : "memory");
-        } else {
-          *reinterpret_cast<float4 *>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 4 * tid; c < 4 * q; c += 4 * kDT) {
+          float *dst = stage + (size_t)r * RS + c;
+          if (row) {
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                             (uint32_t)__cvta_generic_to_shared(dst)),
+                         "l"(row + c)
+                         : "memory");
+          } else {
+            *reinterpret_cast<float4 *>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
       }
       asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
-      for (int i = tid; i < (TT + RE) * H; i += kDT) {
-        const int r = i / H, c = i % H;
-        float v = 0.0f;
-        if (r < TT) {
-          if (r < nt) v = __ldcg(xin + (size_t)(t0 + r) * H + c);
-        } else if (e0 + r - TT < E) {
-          v = load_w(L.router, L.router_dtype, (size_t)(e0 + r - TT) * H + c);
+      for (int r = 0; r < TT + RE; ++r)
+        for (int c = tid; c < H; c += kDT) {
+          float v = 0.0f;
+          if (r < TT) {
+            if (r < nt) v = __ldcg(xin + (size_t)(t0 + r) * H + c);
+          } else if (e0 + r - TT < E) {
+            v = load_w(L.router, L.router_dtype, (size_t)(e0 + r - TT) * H + c);
+          }
+          stage[(size_t)r * RS + c] = v;
         }
-        stage[(size_t)r * RS + c] = v;
-      }
     }
     __syncthreads();
-    for (int i = tid; i < nt * H; i += kDT)
-      if (!is_finite_f(stage[(size_t)(i / H) * RS + i % H])) bad = true;
+    const bool sub = task == (int)blockIdx.x && a.sub_stamps;  // first task, profiling
+    if (sub) stamp(a, 9);
+    for (int r = 0; r < nt; ++r)
+      for (int j = tid; j < H; j += kDT)
+        if (!is_finite_f(stage[(size_t)r * RS + j])) bad = true;
     if (stacked) {
       // RMSNorm of each staged token row (src/backend.rs:341-359): lanes 0..7
       // of warp r run the 8-lane sum of squares, then every thread scales.
       if (warp < nt) {
         const float *x = stage + (size_t)warp * RS;
         float acc = 0.0f;
-        if (lane < 8)
-          for (int c = 0; c < full; ++c) {
+        if (lane < 8) {
+          // blocks of 16 squares ahead of the dependent adds (same order)
+          int c = 0;
+          for (; c + 16 <= full; c += 16) {
+            float p[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const float v = x[8 * (c + u) + lane];
+              p[u] = __fmul_rn(v, v);
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, p[u]);
+          }
+          for (; c < full; ++c) {
             const float v = x[8 * c + lane];
             acc = __fadd_rn(acc, __fmul_rn(v, v));
           }
+        }
         float s = -0.0f;
 #pragma unroll
         for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc, l));
@@ -227,16 +244,19 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
         }
       }
       __syncthreads();
-      for (int i = tid; i < nt * H; i += kDT) {
-        const int r = i / H, j = i % H;
-        float &v = stage[(size_t)r * RS + j];
-        const float o = __fmul_rn(__fmul_rn(v, tb.inv[r]), L.norm_w ? L.norm_w[j] : 1.0f);
-        if (!is_finite_f(o)) bad = true;
-        v = o;
+      for (int j = tid; j < H; j += kDT) {
+        const float w = L.norm_w ? L.norm_w[j] : 1.0f;
+        for (int r = 0; r < nt; ++r) {
+          float &v = stage[(size_t)r * RS + j];
+          const float o = __fmul_rn(__fmul_rn(v, tb.inv[r]), w);
+          if (!is_finite_f(o)) bad = true;
+          v = o;
+        }
       }
       __syncthreads();
     }
     if (bad) set_status(a.status, kStatusNonFinite);
+    if (sub) stamp(a, 10);
     // 8 lanes per (token, expert) pair, whole warps (the fold is a shuffle)
     const int npairs = TT * RE;
     if (tid < ((8 * npairs + 31) & ~31)) {
@@ -253,9 +273,16 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
         logit = acc;
       } else {
         float acc = 0.0f;  // `[0.0f32; 8]`, src/backend.rs:107
-#pragma unroll 8
-        for (int c = 0; c < full; ++c)
-          acc = __fadd_rn(acc, __fmul_rn(w[8 * c + l8], hs[8 * c + l8]));
+        // blocks of 16 products ahead of the dependent adds (same order)
+        int c = 0;
+        for (; c + 16 <= full; c += 16) {
+          float p[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) p[u] = __fmul_rn(w[8 * (c + u) + l8], hs[8 * (c + u) + l8]);
+#pragma unroll
+          for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, p[u]);
+        }
+        for (; c < full; ++c) acc = __fadd_rn(acc, __fmul_rn(w[8 * c + l8], hs[8 * c + l8]));
         float s = -0.0f;
         const int base = lane & ~7;
 #pragma unroll
@@ -268,6 +295,10 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
         a.logits[(size_t)t * E + e] = logit;
         if (!is_finite_f(logit)) set_status(a.status, kStatusNonFinite);
       }
+    }
+    if (sub) {
+      __syncthreads();
+      stamp(a, 11);
     }
     // the token rows' digit planes, once per token (expert group 0), on the
     // warps above the ones running the dot (token r on warp kDW - 1 - r)
@@ -676,11 +707,11 @@ __device__ void gate_up_phase(const DigitArgs &a, uint8_t *xd, DTables &tb) {
       // the digit planes of routes rb .. rb + nr (2H bytes each) and scales
       __syncthreads();
       const int q16 = 2 * H / 16;
-      for (int idx = tid; idx < nr * q16; idx += kDT) {
-        const int j = idx / q16, o = idx - j * q16;
-        const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(
-                                   a.xq + (size_t)tb.r_token[rb + j] * 2 * H) + o);
-        reinterpret_cast<uint4 *>(xd + (size_t)j * 2 * H)[o] = v;
+      for (int j = 0; j < nr; ++j) {
+        const uint4 *src =
+            reinterpret_cast<const uint4 *>(a.xq + (size_t)tb.r_token[rb + j] * 2 * H);
+        for (int o = tid; o < q16; o += kDT)
+          reinterpret_cast<uint4 *>(xd + (size_t)j * 2 * H)[o] = __ldcg(src + o);
       }
       if (tid < nr) {
         tb.s1[tid] = __ldcg(a.xs1 + tb.r_token[rb + tid]);
@@ -1003,7 +1034,13 @@ __device__ bool run_layers(const DigitArgs &a, DTables &tb, uint8_t *stage) {
     // stacked: x is the residual stream (in `out`), normalised while staged
     const float *xin = a.stacked ? a.out : a.h_in;
     const float *resid = a.stacked ? a.out : a.resid;
-    router_phase(a, L, xin, a.stacked != 0, reinterpret_cast<float *>(stage), tb);
+    if (first) {
+      DigitArgs a0 = a;
+      a0.sub_stamps = a.phase_ts != nullptr;
+      router_phase(a0, L, xin, a.stacked != 0, reinterpret_cast<float *>(stage), tb);
+    } else {
+      router_phase(a, L, xin, a.stacked != 0, reinterpret_cast<float *>(stage), tb);
+    }
     if (first) stamp(a, 1);
     if (!sync()) return false;
     if (first) stamp(a, 2);
@@ -1018,8 +1055,14 @@ __device__ bool run_layers(const DigitArgs &a, DTables &tb, uint8_t *stage) {
           a.gates[r] = tb.gates[r];
         }
     } else {
-      for (int t = blockIdx.x * kDW + warp; t < T; t += G * kDW)
+      // one token per CTA (warp 0) while T <= G: each selection has an SM's
+      // FP64 units and shared-memory bandwidth to itself
+      for (int t = blockIdx.x + G * warp; t < T; t += G * kDW)
         select_one(a, t, a.ids + t * K, a.gates + t * K, tb);
+      if (first) {
+        __syncthreads();
+        stamp(a, 12);
+      }
       if (!sync()) return false;
       for (int r = threadIdx.x; r < R; r += kDT) {
         tb.ids[r] = __ldcg(a.ids + r);

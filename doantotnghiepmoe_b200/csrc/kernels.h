@@ -178,7 +178,8 @@ struct DigitArgs {
   int router_async;          // routers of every layer are 16-byte aligned f32 rows
   int prefetch_down;         // prefetch the down rows into L2 during gate/up
   int gate_w, down_w;        // work-split costs: a row costs (its expert's routes + w)
-  unsigned long long *phase_ts;  // optional [9] phase timestamps (profiling)
+  unsigned long long *phase_ts;  // optional phase timestamps (profiling)
+  int sub_stamps;            // also stamp inside the router phase (set by the kernel)
 };
 bool digit_decode_supported(int T, int H, int I, int E, int K);
 cudaError_t launch_digit_decode(const DigitArgs &a, int sm_count, cudaStream_t s);

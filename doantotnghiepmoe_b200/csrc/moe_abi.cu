@@ -1560,10 +1560,16 @@ extern "C" moe_status moe_profile_read(moe_handle *h, moe_kernel_time *out, int 
             if (g < s0 || g > e1) continue;
             g0 = std::min(g0, g), g1 = std::max(g1, g);
           }
-          const char *nm[4] = {"digit:cta_start_spread", "digit:cta_end_spread",
-                               "digit:first_to_last", "digit:gate_up_end_spread"};
-          const unsigned long long v[4] = {s1 - s0, e1 - e0, e1 - s0, g1 >= g0 ? g1 - g0 : 0};
-          for (int i = 0; i < 4; ++i) {
+          // router sub-phases of CTA 0's first task, and the distributed
+          // selection (T > 8) before its barrier
+          auto d = [&](int i, int j) { return ts[j] > ts[i] && ts[i] ? ts[j] - ts[i] : 0ull; };
+          const char *nm[8] = {"digit:cta_start_spread", "digit:cta_end_spread",
+                               "digit:first_to_last", "digit:gate_up_end_spread",
+                               "digit:r_stage", "digit:r_norm", "digit:r_dot",
+                               "digit:s_select"};
+          const unsigned long long v[8] = {s1 - s0, e1 - e0, e1 - s0, g1 >= g0 ? g1 - g0 : 0,
+                                           d(0, 9), d(9, 10), d(10, 11), d(2, 12)};
+          for (int i = 0; i < 8; ++i) {
             moe_kernel_time k{};
             snprintf(k.name, sizeof k.name, "%s", nm[i]);
             k.launches = 1;
