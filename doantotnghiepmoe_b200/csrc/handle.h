@@ -193,7 +193,11 @@ struct moe_handle {
   float *h_pin_in = nullptr, *h_pin_out = nullptr;
   uint32_t *h_pin_status = nullptr;
   float *h_pin_meta = nullptr;  // [2][max_tokens * top_k]: ids, gates
-  cudaEvent_t stage_ev[16] = {};  // chunked staging of pageable host outputs
+  cudaEvent_t stage_ev[32] = {};  // chunked staging of pageable host outputs
+  // host-buffer call in token chunks: copy-in and copy-out streams, and per
+  // chunk the events "input arrived" and "layer done"
+  cudaStream_t io_stream[2] = {};
+  cudaEvent_t io_ev[2][8] = {};
   int last_launches = 0;
   moe::host::Profiler prof;
   // tensor-core path scratch

@@ -355,6 +355,11 @@ void free_handle(moe_handle *h) {
   cudaFreeHost(h->h_pin_meta);
   for (auto ev : h->stage_ev)
     if (ev) cudaEventDestroy(ev);
+  for (auto &row : h->io_ev)
+    for (auto ev : row)
+      if (ev) cudaEventDestroy(ev);
+  for (auto st : h->io_stream)
+    if (st) cudaStreamDestroy(st);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
 }
 
@@ -1385,73 +1390,149 @@ static void h2d(void *dst, const void *src, size_t bytes, void *pin, bool pinned
   }
 }
 
+// Token chunks of the host-buffer call.  A layer's result for a token
+// depends on that token's row alone (routing, digitisation and the int32
+// tensor-core sums are per route), so a chunk's outputs, ids and gates are
+// bit-identical to the whole batch's.  Chunk c's layer runs on the handle's
+// stream while chunk c + 1 comes in on one copy stream and chunk c - 1 goes
+// back on another, so the PCIe transfers hide behind the tensor-core work.
+// MOE_HOST_CHUNK sets the chunk in tokens (0: whole batch).
+static constexpr int kHostChunksMax = 8;
+static constexpr int kHostChunkDefault = 1280;
+
+static int host_chunk_tokens(moe_handle *h, int layer, int T) {
+  static int env = -1;
+  if (env < 0) {
+    const char *v = getenv("MOE_HOST_CHUNK");
+    env = v ? std::max(0, atoi(v)) : kHostChunkDefault;
+    if (env > 0) env = std::max(env, 256);
+  }
+  if (env == 0 || T < 2 * env) return T;
+  const int n = std::min(kHostChunksMax, T / env);
+  const int c = ((T + n - 1) / n + 15) & ~15;
+  // every chunk, the last (shortest) one included, must take the tensor-core
+  // path, whose outputs do not depend on the batch composition
+  const LayerSlot &L = h->layers[layer];
+  if (!use_tensor_path(h, L, c, h->io_in) || !use_tensor_path(h, L, T - (n - 1) * c, h->io_in))
+    return T;
+  return c;
+}
+
+static bool host_streams(moe_handle *h) {
+  if (h->io_stream[0]) return true;
+  bool ok = true;
+  for (auto &st : h->io_stream)
+    ok = ok && cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess;
+  for (auto &row : h->io_ev)
+    for (auto &ev : row)
+      ok = ok && cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) cudaGetLastError();
+  return ok;
+}
+
 extern "C" moe_status moe_layer_forward_host(moe_handle *h, int layer, const float *h_in,
                                              const float *h_resid, float *h_out, int T,
                                              uint32_t *h_ids, float *h_gates) {
   if (!h || !h_in || !h_out) return MOE_ERR_INVALID;
-  moe_status st;
-  {
-    std::lock_guard<std::mutex> lock(h->mu);
-    st = check_layer(h, layer, T);
-    if (st != MOE_OK || T == 0) return st;
-    DeviceGuard g(h->device);
-    cudaStream_t s = h->stream;
-    const size_t n = (size_t)T * h->d.hidden;
-    const size_t R = (size_t)T * h->d.top_k;
-    const size_t bytes = n * sizeof(float);
-    h2d(h->io_in, h_in, bytes, h->h_pin_in, host_is_pinned(h_in), s);
-    if (h_resid) h2d(h->io_resid, h_resid, bytes, h->h_pin_in + n, host_is_pinned(h_resid), s);
-    h->last_launches = 0;
-    st = layer_forward_locked(h, layer, h->io_in, h_resid ? h->io_resid : nullptr, h->io_out, T,
-                              h->ids, h->gates, s);
-    if (st != MOE_OK) return st;
-    // ids and gates: straight into pinned buffers, else through the handle's
-    // pinned staging (a copy into pageable memory would block the host)
-    const bool pin_ids = h_ids && host_is_pinned(h_ids);
-    const bool pin_gates = h_gates && host_is_pinned(h_gates);
-    uint32_t *ids_dst = pin_ids ? h_ids : reinterpret_cast<uint32_t *>(h->h_pin_meta);
-    float *gates_dst = pin_gates ? h_gates : h->h_pin_meta + R;
-    // the status word travels back with the outputs and is cleared behind
-    // them, so the call needs one stream synchronisation
-    auto meta_back = [&] {
-      if (h_ids) cudaMemcpyAsync(ids_dst, h->ids, R * 4, cudaMemcpyDeviceToHost, s);
-      if (h_gates) cudaMemcpyAsync(gates_dst, h->gates, R * 4, cudaMemcpyDeviceToHost, s);
-      cudaMemcpyAsync(h->h_pin_status, h->status, 4, cudaMemcpyDeviceToHost, s);
-      cudaMemsetAsync(h->status, 0, 4, s);
-    };
-    cudaError_t e = cudaSuccess;
-    if (host_is_pinned(h_out)) {
-      cudaMemcpyAsync(h_out, h->io_out, bytes, cudaMemcpyDeviceToHost, s);
-      meta_back();
-      e = cudaStreamSynchronize(s);
-    } else {
-      // chunk i is copied out on the host while chunk i + 1 is in flight
-      if (!h->stage_ev[0])
-        for (auto &ev : h->stage_ev) cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-      const size_t c = stage_chunk(bytes);
-      int nc = 0;
-      for (size_t o = 0; o < bytes; o += c, ++nc) {
-        cudaMemcpyAsync(reinterpret_cast<char *>(h->h_pin_out) + o,
-                        reinterpret_cast<char *>(h->io_out) + o, std::min(c, bytes - o),
-                        cudaMemcpyDeviceToHost, s);
-        cudaEventRecord(h->stage_ev[nc], s);
-      }
-      meta_back();
-      for (int i = 0; i < nc && e == cudaSuccess; ++i) {
-        e = cudaEventSynchronize(h->stage_ev[i]);
-        const size_t o = (size_t)i * c;
-        if (e == cudaSuccess)
-          memcpy(reinterpret_cast<char *>(h_out) + o,
-                 reinterpret_cast<char *>(h->h_pin_out) + o, std::min(c, bytes - o));
-      }
-      cudaError_t e2 = cudaStreamSynchronize(s);
-      if (e == cudaSuccess) e = e2;
+  std::lock_guard<std::mutex> lock(h->mu);
+  moe_status st = check_layer(h, layer, T);
+  if (st != MOE_OK || T == 0) return st;
+  DeviceGuard g(h->device);
+  cudaStream_t s = h->stream;
+  const size_t H = h->d.hidden, K = h->d.top_k;
+  const size_t R = (size_t)T * K;
+  const size_t bytes = (size_t)T * H * sizeof(float);
+  int ct = host_chunk_tokens(h, layer, T);
+  if (ct < T && !host_streams(h)) ct = T;
+  const int nch = (T + ct - 1) / ct;
+  // one chunk: everything in order on the handle's stream
+  cudaStream_t si = nch > 1 ? h->io_stream[0] : s, so = nch > 1 ? h->io_stream[1] : s;
+  const bool pin_in = host_is_pinned(h_in);
+  const bool pin_resid = h_resid && host_is_pinned(h_resid);
+  const bool pin_out = host_is_pinned(h_out);
+  if (!pin_out && !h->stage_ev[0])
+    for (auto &ev : h->stage_ev) cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  // pageable outputs come back through the pinned staging in pieces, each
+  // copied out on the host as soon as its event has fired
+  const size_t piece = stage_chunk(bytes);
+  std::vector<std::pair<size_t, size_t>> pieces;
+  auto drain = [&] {
+    cudaStreamSynchronize(si);
+    cudaStreamSynchronize(s);
+    cudaStreamSynchronize(so);
+  };
+  int launches = 0;
+  for (int c = 0; c < nch; ++c) {
+    const size_t t0 = (size_t)c * ct, tc = std::min((size_t)ct, (size_t)T - t0);
+    const size_t o = t0 * H, cb = tc * H * sizeof(float);
+    h2d(h->io_in + o, h_in + o, cb, h->h_pin_in + o, pin_in, si);
+    if (h_resid)
+      h2d(h->io_resid + o, h_resid + o, cb, h->h_pin_in + (size_t)T * H + o, pin_resid, si);
+    if (si != s) {
+      cudaEventRecord(h->io_ev[0][c], si);
+      cudaStreamWaitEvent(s, h->io_ev[0][c], 0);
     }
-    if (e == cudaSuccess && h_ids && !pin_ids) memcpy(h_ids, ids_dst, R * 4);
-    if (e == cudaSuccess && h_gates && !pin_gates) memcpy(h_gates, gates_dst, R * 4);
-    if (e != cudaSuccess) return cuda_fail(h, e, "layer_forward_host");
-    return status_error(h, *h->h_pin_status);
+    const float *d_h = h->io_in + o, *d_resid = h_resid ? h->io_resid + o : nullptr;
+    float *d_out = h->io_out + o;
+    uint32_t *d_ids = h->ids + t0 * K;
+    float *d_gates = h->gates + t0 * K;
+    const uint64_t key[10] = {1, (uint64_t)layer, (uint64_t)tc, (uint64_t)d_h,
+                              (uint64_t)d_resid, (uint64_t)d_out, (uint64_t)d_ids,
+                              (uint64_t)d_gates, (uint64_t)s,
+                              (uint64_t)(h->path * 16 + h->route_mode)};
+    h->last_launches = 0;
+    st = graphed(h, key, s, [&] {
+      h->last_launches = 0;
+      return layer_forward_locked(h, layer, d_h, d_resid, d_out, (int)tc, d_ids, d_gates, s);
+    });
+    if (st != MOE_OK) {
+      drain();
+      return st;
+    }
+    launches += h->last_launches;
+    if (so != s) {
+      cudaEventRecord(h->io_ev[1][c], s);
+      cudaStreamWaitEvent(so, h->io_ev[1][c], 0);
+    }
+    if (pin_out) {
+      cudaMemcpyAsync(h_out + o, d_out, cb, cudaMemcpyDeviceToHost, so);
+    } else {
+      for (size_t p = 0; p < cb; p += piece) {
+        const size_t n = std::min(piece, cb - p);
+        cudaMemcpyAsync(reinterpret_cast<char *>(h->h_pin_out + o) + p,
+                        reinterpret_cast<const char *>(d_out) + p, n, cudaMemcpyDeviceToHost,
+                        so);
+        cudaEventRecord(h->stage_ev[pieces.size()], so);
+        pieces.emplace_back(o * sizeof(float) + p, n);
+      }
+    }
   }
+  h->last_launches = launches;
+  // ids, gates and the status word follow the last chunk's layer; the status
+  // is cleared behind them, so the call needs one synchronisation per stream
+  const bool pin_ids = h_ids && host_is_pinned(h_ids);
+  const bool pin_gates = h_gates && host_is_pinned(h_gates);
+  uint32_t *ids_dst = pin_ids ? h_ids : reinterpret_cast<uint32_t *>(h->h_pin_meta);
+  float *gates_dst = pin_gates ? h_gates : h->h_pin_meta + R;
+  if (h_ids) cudaMemcpyAsync(ids_dst, h->ids, R * 4, cudaMemcpyDeviceToHost, so);
+  if (h_gates) cudaMemcpyAsync(gates_dst, h->gates, R * 4, cudaMemcpyDeviceToHost, so);
+  cudaMemcpyAsync(h->h_pin_status, h->status, 4, cudaMemcpyDeviceToHost, so);
+  cudaMemsetAsync(h->status, 0, 4, so);
+  cudaError_t e = cudaSuccess;
+  for (size_t i = 0; i < pieces.size() && e == cudaSuccess; ++i) {
+    e = cudaEventSynchronize(h->stage_ev[i]);
+    if (e == cudaSuccess)
+      memcpy(reinterpret_cast<char *>(h_out) + pieces[i].first,
+             reinterpret_cast<const char *>(h->h_pin_out) + pieces[i].first, pieces[i].second);
+  }
+  for (cudaStream_t x : {so, s, si}) {
+    const cudaError_t e2 = cudaStreamSynchronize(x);
+    if (e == cudaSuccess) e = e2;
+  }
+  if (e == cudaSuccess && h_ids && !pin_ids) memcpy(h_ids, ids_dst, R * 4);
+  if (e == cudaSuccess && h_gates && !pin_gates) memcpy(h_gates, gates_dst, R * 4);
+  if (e != cudaSuccess) return cuda_fail(h, e, "layer_forward_host");
+  return status_error(h, *h->h_pin_status);
 }
 
 extern "C" moe_status moe_host_alloc(size_t bytes, void **out) {

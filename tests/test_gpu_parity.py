@@ -5,6 +5,8 @@ defined as max|gpu - cpu| / max|cpu| as in src/gpu_expert.rs:566-575) is
 asserted as well so a failure says by how much."""
 import ctypes
 
+import os
+
 import numpy as np
 import pytest
 
@@ -289,6 +291,52 @@ def test_host_buffers_pinned_and_staged():
         assert np.array_equal(bits(got), bits(want)), (pin_in, pin_out)
     with pytest.raises(ValueError):
         eng.forward_host(0, h, out=np.zeros((T, 2047), np.float32))
+
+
+def test_host_call_in_token_chunks_matches_whole_batch():
+    """At T >= 2048 the host-buffer call pipelines token chunks (copy in,
+    layer, copy out on three streams).  Chunks of a token-independent layer
+    give the whole batch's bits: 4000 tokens in three chunks, the last one
+    shorter, pinned and pageable buffers, with a residual."""
+    lw = O.synth_layer(45, 0, 2048, 256, 8, 2, True)
+    T = 4000
+    h = O.synth_hidden(45, T, 2048)
+    resid = O.synth_hidden(46, T, 2048)
+    eng = engine_for(lw, T, path=_lib.MOE_PATH_AUTO)
+    ex, sc, rt = helpers.to_device(lw)
+    eng.set_layer_packed(0, ex, sc, rt)
+    hd, rd = torch.from_numpy(h).cuda(), torch.from_numpy(resid).cuda()
+    od = torch.empty_like(hd)
+    idd = torch.empty((T, 2), dtype=torch.int32, device="cuda")
+    gd = torch.empty((T, 2), dtype=torch.float32, device="cuda")
+    eng.forward(0, hd, od, resid=rd, ids=idd, gates=gd)
+    eng.sync_status()
+    whole_launches = eng.last_launch_count()
+    want = od.cpu().numpy()
+    want_ids = idd.cpu().numpy().astype(np.uint32)
+    want_gates = gd.cpu().numpy()
+    rows = np.arange(0, T, 97)
+    ref = O.layer_forward(lw, h[rows], resid=resid[rows])
+    assert np.array_equal(want_ids[rows], ref.ids)
+    assert helpers.rel_err(want[rows], ref.out) < 1e-3
+    chunked = os.environ.get("MOE_HOST_CHUNK", "1280") != "0"
+    for pin in (True, False):
+        def mk(a):
+            if not pin:
+                return np.copy(a)
+            buf = M.host_empty(a.shape, a.dtype)
+            buf[:] = a
+            return buf
+        out = mk(np.zeros_like(h))
+        for _ in range(2):  # the second call replays the chunks' graphs
+            got, ids, gates = eng.forward_host(0, mk(h), mk(resid), out=out,
+                                               ids=mk(np.zeros((T, 2), np.uint32)),
+                                               gates=mk(np.zeros((T, 2), np.float32)))
+            assert np.array_equal(ids, want_ids)
+            assert np.array_equal(bits(gates), bits(want_gates))
+            assert np.array_equal(bits(got), bits(want)), pin
+            if chunked:  # three layer calls (a chunk's route may take fewer launches)
+                assert eng.last_launch_count() > 2 * whole_launches
 
 
 def test_nonfinite_input_is_reported():
