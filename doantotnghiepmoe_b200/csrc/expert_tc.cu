@@ -149,7 +149,11 @@ __device__ __forceinline__ void mainloop(Pipe &pp, uint8_t *tiles, const CUtenso
                                          int b_row, int nk, uint32_t tmem) {
   constexpr uint32_t kBTile = BN * BK;
   constexpr uint32_t kStageBytes = NA * kTileBytes + NB * kBTile;
-  constexpr uint32_t kIdesc = idesc_i8<BN>();
+  // the NB digit tiles of a stage are adjacent 8-row swizzle atoms, so one
+  // MMA of N = NB * BN covers every plane: the weight tile is read from
+  // shared memory once per K step rather than once per plane
+  static_assert(NB * BN <= 256 && (NB * BN) % 16 == 0, "UMMA N");
+  constexpr uint32_t kIdesc = idesc_i8<NB * BN>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0 && lane == 0) {
     int issued = 0;
@@ -188,15 +192,11 @@ __device__ __forceinline__ void mainloop(Pipe &pp, uint8_t *tiles, const CUtenso
       const uint32_t base = su32(tiles + s * kStageBytes);
 #pragma unroll
       for (int k = 0; k < BK / UK; ++k) {
+        const uint64_t bd = sw128_desc(base + NA * kTileBytes + k * UK);
 #pragma unroll
         for (int a = 0; a < NA; ++a) {
           const uint64_t ad = sw128_desc(base + a * kTileBytes + k * UK);
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const uint64_t bd = sw128_desc(base + NA * kTileBytes + b * kBTile + k * UK);
-            mma_i8(tmem + (uint32_t)((a * NB + b) * BN), ad, bd, kIdesc,
-                   (kb > 0 || k > 0) ? 1u : 0u);
-          }
+          mma_i8(tmem + (uint32_t)(a * NB * BN), ad, bd, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
         }
       }
       mma_commit(&pp.empty[s]);
@@ -471,14 +471,23 @@ struct PPipe {
   int consumed;
 };
 
-// Barrier among the four epilogue warps that ORs a predicate over them, so
-// every epilogue thread leaves the tile loop at the same item on an abort.
+// The persistent kernels run 8 epilogue warps (warps 2..9): warp w reads
+// TMEM lane quarter w % 4 (the hardware's rule) and column half (w - 2) / 4
+// of each 64-route item, so twice the store streams of a 4-warp epilogue
+// drain one item while the MMAs fill the other TMEM buffer.
+constexpr int kPEpiWarps = 8;
+constexpr int kPThreads = 64 + 32 * kPEpiWarps;
+
+__device__ __forceinline__ void pepi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Barrier among the epilogue warps that ORs a predicate over them, so every
+// epilogue thread leaves the tile loop at the same item on an abort.
 __device__ __forceinline__ bool epi_any(bool v) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "bar.red.or.pred q, 1, 256, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
       : "r"((uint32_t)v)
@@ -496,7 +505,7 @@ __device__ __forceinline__ void psetup(PPipe &pp, int stages, uint32_t ncols) {
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&pp.tfull[b], 1);
-      mbar_init(&pp.tempty[b], 4);  // one arrive per epilogue warp
+      mbar_init(&pp.tempty[b], kPEpiWarps);  // one arrive per epilogue warp
     }
     mbar_init(&pp.done, 1);
     pp.abort_flag = 0;
@@ -518,7 +527,8 @@ __device__ __forceinline__ void pmain(PPipe &pp, uint8_t *tiles, const CUtensorM
                                       int nM, int nk, ARow arow) {
   constexpr uint32_t kBTile = PBN * BK;
   constexpr uint32_t kStageBytes = NA * kTileBytes + NB * kBTile;
-  constexpr uint32_t kIdesc = idesc_i8<PBN>();
+  static_assert(NB * PBN <= 256 && (NB * PBN) % 16 == 0, "UMMA N");
+  constexpr uint32_t kIdesc = idesc_i8<NB * PBN>();  // every plane in one MMA
   constexpr uint32_t kBufCols = NA * NB * PBN;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0 && lane == 0) {
@@ -569,15 +579,11 @@ __device__ __forceinline__ void pmain(PPipe &pp, uint8_t *tiles, const CUtensorM
         const uint32_t base = su32(tiles + s * kStageBytes);
 #pragma unroll
         for (int k = 0; k < BK / UK; ++k) {
+          const uint64_t bd = sw128_desc(base + NA * kTileBytes + k * UK);
 #pragma unroll
           for (int x = 0; x < NA; ++x) {
             const uint64_t ad = sw128_desc(base + x * kTileBytes + k * UK);
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-              const uint64_t bd = sw128_desc(base + NA * kTileBytes + b * kBTile + k * UK);
-              mma_i8(tmem + (uint32_t)((x * NB + b) * PBN), ad, bd, kIdesc,
-                     (kb > 0 || k > 0) ? 1u : 0u);
-            }
+            mma_i8(tmem + (uint32_t)(x * NB * PBN), ad, bd, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
         }
         mma_commit(&pp.empty[s]);
@@ -604,7 +610,7 @@ constexpr size_t psmem_bytes(int na, int nb, int stages) {
 }
 
 template <int S>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPThreads, 1)
     gate_up_tc_pkernel(const __grid_constant__ CUtensorMap mapW,
                        const __grid_constant__ CUtensorMap mapX, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -619,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                  [I](int m, int x) { return x * I + m * BM; });
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= 2) {
-    const int qd = warp & 3;
+    const int qd = warp & 3, half = (warp - 2) >> 2;
     int j = 0;
     for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++j) {
       const int buf = j & 1, g = w / nM, m = w % nM;
@@ -628,12 +634,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i = m * BM + 32 * qd + lane;  // weight row of this thread
       const float *Sc = a.s_ptr[e];
       const float sg = i < I ? Sc[i] : 0.0f, su = i < I ? Sc[I + i] : 0.0f;
-      epi_sync();  // every epilogue warp is past the item that last used tab[buf]
-      for (int c = threadIdx.x - 64; c < nr; c += 128) {
+      pepi_sync();  // every epilogue warp is past the item that last used tab[buf]
+      for (int c = threadIdx.x - 64; c < nr; c += 32 * kPEpiWarps) {
         tab.s1[c] = a.xs1[r0 + c];
         tab.s2[c] = a.xs2[r0 + c];
       }
-      epi_sync();
+      pepi_sync();
       const bool ok = mbar_wait(&pp.tfull[buf], (j >> 1) & 1, &pp.abort_flag);
       if (epi_any(!ok)) {  // uniform over the epilogue warps
         pp.abort_flag = 1;
@@ -642,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_after_sync();
       const uint32_t trow =
           pp.tmem_base + (uint32_t)(buf * 4 * PBN) + ((uint32_t)(32 * qd) << 16);
-      for (int c0 = 0; c0 < PBN; c0 += 16) {
+      for (int c0 = half * (PBN / 2); c0 < (half + 1) * (PBN / 2); c0 += 16) {
         if (c0 >= nr) break;  // warp-uniform
         int32_t v[4][16];
 #pragma unroll
@@ -673,32 +679,43 @@ act = digits::swiglu(v[0][jj], v[1][jj], v[2][jj], v[3][jj], s1, s2, sg, su);
   pteardown(pp, kCols, a.status);
 }
 
-template <int S>
-__global__ void __launch_bounds__(kThreads, 1)
+// NA weight row blocks per work item: with NA = 2 the item's digit tile is
+// loaded once for 256 output rows (half the activation traffic of NA = 1),
+// and epilogue warp w takes row block (w - 2) / 4 of the item, all 64
+// columns; with NA = 1 it takes column half (w - 2) / 4 of the one block.
+template <int S, int NA>
+__global__ void __launch_bounds__(kPThreads, 1)
     down_tc_pkernel(const __grid_constant__ CUtensorMap mapW,
                     const __grid_constant__ CUtensorMap mapA, TcArgs a) {
+  static_assert(NA == 1 || NA == 2, "row blocks per item");
   extern __shared__ uint8_t smem_raw[];
   PPipe &pp = *reinterpret_cast<PPipe *>(smem_raw);
   RouteTab *tabs = reinterpret_cast<RouteTab *>(smem_raw + sizeof(PPipe));
   uint8_t *tiles = align1024(smem_raw + sizeof(PPipe) + 2 * sizeof(RouteTab));
-  const int nM = (a.H + BM - 1) / BM, nwork = *a.n_tiles * nM, nk = (a.I + BK - 1) / BK;
-  constexpr uint32_t kCols = 2 * 2 * PBN;
+  const int nM = (a.H + NA * BM - 1) / (NA * BM), nwork = *a.n_tiles * nM;
+  const int nk = (a.I + BK - 1) / BK;
+  constexpr uint32_t kBufCols = NA * 2 * PBN;
+  constexpr uint32_t kCols = 2 * kBufCols;
   psetup(pp, S, kCols);
-  pmain<1, 2, S>(pp, tiles, &mapW, &mapA, a, nwork, nM, nk,
-                 [](int m, int) { return m * BM; });
+  pmain<NA, 2, S>(pp, tiles, &mapW, &mapA, a, nwork, nM, nk,
+                  [](int m, int x) { return (NA * m + x) * BM; });
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= 2) {
-    const int qd = warp & 3;
+    const int qd = warp & 3, sel = (warp - 2) >> 2;
+    const int x = NA == 2 ? sel : 0;                     // row block of the item
+    const int cb = NA == 2 ? 0 : sel * (PBN / 2);        // first column
+    const int ce = NA == 2 ? PBN : (sel + 1) * (PBN / 2);
     bool bad = false;
     int j = 0;
     for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++j) {
       const int buf = j & 1, g = w / nM, m = w % nM;
       const int e = a.tile_expert[g], r0 = a.tile_row0[g], nr = a.tile_rows[g];
       RouteTab &tab = tabs[buf];
-      const int jr = m * BM + 32 * qd + lane;  // output row (hidden index)
+      const int rb = (NA * m + x) * BM + 32 * qd;  // first output row of this warp
+      const int jr = rb + lane;                    // output row (hidden index)
       const float sd = jr < a.H ? a.s_ptr[e][2 * a.I + jr] : 0.0f;
-      epi_sync();
-      for (int c = threadIdx.x - 64; c < nr; c += 128) {
+      pepi_sync();
+      for (int c = threadIdx.x - 64; c < nr; c += 32 * kPEpiWarps) {
         const int r = r0 + c;
         tab.s1[c] = a.as1[r];
         tab.s2[c] = a.as2[r];
@@ -707,35 +724,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         tab.slot[c] = a.r_slot[r];
         tab.rank[c] = a.r_rank ? a.r_rank[r] : 0;
       }
-      epi_sync();
+      pepi_sync();
       const bool ok = mbar_wait(&pp.tfull[buf], (j >> 1) & 1, &pp.abort_flag);
       if (epi_any(!ok)) {  // uniform over the epilogue warps
         pp.abort_flag = 1;
         break;
       }
       fence_after_sync();
-      const uint32_t trow =
-          pp.tmem_base + (uint32_t)(buf * 2 * PBN) + ((uint32_t)(32 * qd) << 16);
-      for (int c0 = 0; c0 < PBN; c0 += 16) {
-        if (c0 >= nr) break;
-        int32_t v[2][16];
-        tmem_ld16(trow + c0, v[0]);
-        tmem_ld16(trow + PBN + c0, v[1]);
-        tmem_wait_ld();
-        float gy[16];
+      const uint32_t trow = pp.tmem_base + (uint32_t)(buf * kBufCols + x * 2 * PBN) +
+                            ((uint32_t)(32 * qd) << 16);
+      if (rb < a.H) {  // warp-uniform: a row block past H has nothing to store
+        for (int c0 = cb; c0 < ce; c0 += 16) {
+          if (c0 >= nr) break;
+          int32_t v[2][16];
+          tmem_ld16(trow + c0, v[0]);
+          tmem_ld16(trow + PBN + c0, v[1]);
+          tmem_wait_ld();
+          float gy[16];
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int c = c0 + jj;
-          gy[jj] = 0.0f;
-          if (c < nr && jr < a.H) {
-            const float y = digits::down(v[0][jj], v[1][jj], tab.s1[c], tab.s2[c], sd);
-            bad |= !is_finite_f(y);
-            gy[jj] = __fmul_rn(tab.gate[c], y);
-            if (!a.r_rank)
-              a.contrib[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + jr] = gy[jj];
+          for (int jj = 0; jj < 16; ++jj) {
+            const int c = c0 + jj;
+            gy[jj] = 0.0f;
+            if (c < nr && jr < a.H) {
+              const float y = digits::down(v[0][jj], v[1][jj], tab.s1[c], tab.s2[c], sd);
+              bad |= !is_finite_f(y);
+              gy[jj] = __fmul_rn(tab.gate[c], y);
+              if (!a.r_rank)
+                a.contrib[((size_t)tab.tok[c] * a.K + tab.slot[c]) * a.H + jr] = gy[jj];
+            }
           }
+          if (a.r_rank) ep_store(a, tab, c0, nr, jr, rb / 32, gy);
         }
-        if (a.r_rank) ep_store(a, tab, c0, nr, jr, (m * BM + 32 * qd) / 32, gy);
       }
       fence_before_sync();
       __syncwarp();
@@ -950,14 +969,17 @@ cudaError_t launch_quantize_tokens(const float *x, const int32_t *r_pos, int T, 
 }
 
 // Persistent tile loop with double-buffered accumulators for 64-route tiles:
-// MOE_TC_PERSISTENT=1 for both GEMMs, =2 for the down GEMM only, =3 for the
-// gate/up GEMM only; by default one CTA per tile.
+// Persistent kernels (one CTA per SM walking 64-route work items, TMEM double
+// buffered, 8 epilogue warps) for both GEMMs by default: measured on B200
+// faster than one CTA per tile at Qwen3 T = 512, 1376 and 4096 and OLMoE
+// T = 512.  MOE_TC_PERSISTENT=0 selects one CTA per tile, =2 persistent down
+// only, =3 persistent gate/up only.
 int persistent_mode() {
   static int v = -1;
   if (v < 0) {
     const char *env = getenv("MOE_TC_PERSISTENT");
-    v = env ? atoi(env) : 0;
-    if (v < 0 || v > 3) v = 0;
+    v = env ? atoi(env) : 1;
+    if (v < 0 || v > 3) v = 1;
   }
   return v;
 }
@@ -1021,7 +1043,18 @@ int sm_count_cached() {
   return n;
 }
 
-constexpr int kPStagesGU = 4, kPStagesDN = 6;
+constexpr int kPStagesGU = 4, kPStagesDN = 6, kPStagesDN2 = 4;
+
+// MOE_TC_DN_ROWS=1: one 128-row weight block per persistent down item
+// (default two).
+int dn_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char *env = getenv("MOE_TC_DN_ROWS");
+    v = env && atoi(env) == 1 ? 1 : 2;
+  }
+  return v;
+}
 
 cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, const TcArgs &a,
                               int bn, int max_tiles, cudaStream_t s) {
@@ -1031,7 +1064,7 @@ cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, 
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const long long work = (long long)max_tiles * ((a.I + BM - 1) / BM);
     const int grid = (int)std::min<long long>(sm_count_cached(), std::max<long long>(work, 1));
-    k<<<grid, kThreads, smem, s>>>(mapW, mapX, a);
+    k<<<grid, kPThreads, smem, s>>>(mapW, mapX, a);
     return cudaGetLastError();
   }
   return bn == 64 ? launch_gu<64, 2, 2>(mapW, mapX, a, max_tiles, s)
@@ -1041,12 +1074,13 @@ cudaError_t launch_gate_up_tc(const CUtensorMap &mapW, const CUtensorMap &mapX, 
 cudaError_t launch_down_tc(const CUtensorMap &mapW, const CUtensorMap &mapA, const TcArgs &a,
                            int bn, int max_tiles, cudaStream_t s) {
   if (bn == PBN && persistent_dn()) {
-    const size_t smem = psmem_bytes(1, 2, kPStagesDN);
-    auto k = down_tc_pkernel<kPStagesDN>;
+    const int na = dn_rows();
+    const size_t smem = na == 2 ? psmem_bytes(2, 2, kPStagesDN2) : psmem_bytes(1, 2, kPStagesDN);
+    auto k = na == 2 ? down_tc_pkernel<kPStagesDN2, 2> : down_tc_pkernel<kPStagesDN, 1>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    const long long work = (long long)max_tiles * ((a.H + BM - 1) / BM);
+    const long long work = (long long)max_tiles * ((a.H + na * BM - 1) / (na * BM));
     const int grid = (int)std::min<long long>(sm_count_cached(), std::max<long long>(work, 1));
-    k<<<grid, kThreads, smem, s>>>(mapW, mapA, a);
+    k<<<grid, kPThreads, smem, s>>>(mapW, mapA, a);
     return cudaGetLastError();
   }
   return bn == 64 ? launch_dn<64, 3, 2>(mapW, mapA, a, max_tiles, s)

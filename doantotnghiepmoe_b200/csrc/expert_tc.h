@@ -10,13 +10,14 @@
 namespace moe {
 namespace tc {
 
-int persistent_mode();  // MOE_TC_PERSISTENT: 0 off, 1 both GEMMs, 2 down, 3 gate/up
+int persistent_mode();  // MOE_TC_PERSISTENT: 0 off, 1 both GEMMs (default), 2 down, 3 gate/up
 int tc_bn_override();  // MOE_TC_BN (64 or 128), 0 when unset
 
-// Routes per GEMM tile: 64.  Measured on B200 (OLMoE T=512, Qwen3 T=4096),
-// 64-route tiles with two CTAs per SM beat 128-route tiles at both sizes:
-// two independent pipelines per SM overlap one CTA's epilogue with the
-// other's mainloop.  MOE_TC_BN=128 restores the wide tile.
+// Routes per GEMM tile: 64, which the persistent kernels require.  With one
+// CTA per tile (MOE_TC_PERSISTENT=0), 64-route tiles with two CTAs per SM
+// also beat 128-route tiles on B200 (OLMoE T=512, Qwen3 T=4096): two
+// pipelines per SM overlap one CTA's epilogue with the other's mainloop.
+// MOE_TC_BN=128 selects the wide tile there.
 inline int tc_block_n(int routes, int experts) {
   (void)routes;
   (void)experts;
