@@ -471,14 +471,20 @@ struct PPipe {
   int consumed;
 };
 
-// The persistent kernels run 8 epilogue warps (warps 2..9): warp w reads
-// TMEM lane quarter w % 4 (the hardware's rule) and column half (w - 2) / 4
-// of each 64-route item, so twice the store streams of a 4-warp epilogue
-// drain one item while the MMAs fill the other TMEM buffer.
-constexpr int kPEpiWarps = 8;
+// The persistent kernels run kPEpiWarps epilogue warps (warps 2 ..): warp w
+// reads TMEM lane quarter w % 4 (the hardware's rule), and the kPEpiGroups
+// warps of a quarter split each item's columns (and, in the two-block down
+// GEMM, its row blocks) between them.  The epilogue is issue-latency bound
+// (dependent per-element chains), so more warps drain an item faster while
+// the MMAs fill the other TMEM buffer.
+constexpr int kPEpiWarps = 16;
+constexpr int kPEpiGroups = kPEpiWarps / 4;
 constexpr int kPThreads = 64 + 32 * kPEpiWarps;
+static_assert(PBN % (16 * kPEpiGroups) == 0, "column split");
 
-__device__ __forceinline__ void pepi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void pepi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kPEpiWarps) : "memory");
+}
 
 // Barrier among the epilogue warps that ORs a predicate over them, so every
 // epilogue thread leaves the tile loop at the same item on an abort.
@@ -487,10 +493,10 @@ __device__ __forceinline__ bool epi_any(bool v) {
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 256, p;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"((uint32_t)v)
+      : "r"((uint32_t)v), "n"(32 * kPEpiWarps)
       : "memory");
   return r != 0;
 }
@@ -625,7 +631,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
                  [I](int m, int x) { return x * I + m * BM; });
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= 2) {
-    const int qd = warp & 3, half = (warp - 2) >> 2;
+    const int qd = warp & 3, grp = (warp - 2) >> 2;
+    constexpr int kNC = PBN / kPEpiGroups;  // columns of this warp's share
     int j = 0;
     for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++j) {
       const int buf = j & 1, g = w / nM, m = w % nM;
@@ -648,7 +655,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
       fence_after_sync();
       const uint32_t trow =
           pp.tmem_base + (uint32_t)(buf * 4 * PBN) + ((uint32_t)(32 * qd) << 16);
-      for (int c0 = half * (PBN / 2); c0 < (half + 1) * (PBN / 2); c0 += 16) {
+      for (int c0 = grp * kNC; c0 < (grp + 1) * kNC; c0 += 16) {
         if (c0 >= nr) break;  // warp-uniform
         int32_t v[4][16];
 #pragma unroll
@@ -680,9 +687,9 @@ act = digits::swiglu(v[0][jj], v[1][jj], v[2][jj], v[3][jj], s1, s2, sg, su);
 }
 
 // NA weight row blocks per work item: with NA = 2 the item's digit tile is
-// loaded once for 256 output rows (half the activation traffic of NA = 1),
-// and epilogue warp w takes row block (w - 2) / 4 of the item, all 64
-// columns; with NA = 1 it takes column half (w - 2) / 4 of the one block.
+// loaded once for 256 output rows (half the activation traffic of NA = 1).
+// The kPEpiGroups epilogue warps of a TMEM lane quarter split the item's
+// NA row blocks x 64 columns evenly.
 template <int S, int NA>
 __global__ void __launch_bounds__(kPThreads, 1)
     down_tc_pkernel(const __grid_constant__ CUtensorMap mapW,
@@ -701,10 +708,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
                   [](int m, int x) { return (NA * m + x) * BM; });
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp >= 2) {
-    const int qd = warp & 3, sel = (warp - 2) >> 2;
-    const int x = NA == 2 ? sel : 0;                     // row block of the item
-    const int cb = NA == 2 ? 0 : sel * (PBN / 2);        // first column
-    const int ce = NA == 2 ? PBN : (sel + 1) * (PBN / 2);
+    static_assert(kPEpiGroups % NA == 0, "row split");
+    constexpr int kNC = PBN * NA / kPEpiGroups;  // columns of this warp's share
+    const int qd = warp & 3, grp = (warp - 2) >> 2;
+    const int x = grp % NA;                       // row block of the item
+    const int cb = (grp / NA) * kNC, ce = cb + kNC;
     bool bad = false;
     int j = 0;
     for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++j) {

@@ -230,7 +230,28 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const float *src,
 // every SM.  Each thread's copy rows and column are fixed for the whole
 // kernel (row rb + k * (NT / (CW / 4)), column 4 * qc of every stage), so a
 // copy costs a pointer add and a predicate.
-template <int PT, int PE, int CW, int S, int NT>
+//
+// PK: the products of expert pairs (j, j + 1) come from one packed
+// `mul.rn.f32x2` (per component the IEEE product, exactly __fmul_rn's), and
+// each chain adds its product with a scalar __fadd_rn, which is never fused.
+// A packed add as well was measured on B200 to change the logits' low bits
+// (the multiply and add of a pair end up contracted), so it is not used.
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul_rn(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+template <int PT, int PE, int CW, int S, int NT, bool PK>
 __global__ void __launch_bounds__(NT, PT * PE >= 64 ? 2 : 4)
     route_logits_pipe_kernel(RouteArgs a) {
   using Tile = PipeTile<PT, PE, CW, S, NT>;
@@ -304,10 +325,29 @@ __global__ void __launch_bounds__(NT, PT * PE >= 64 ? 2 : 4)
       for (int i = 0; i < PT; ++i) hv[i] = hs[8 * i * kStride + 8 * c];
 #pragma unroll
       for (int j = 0; j < PE; ++j) wv[j] = ws[Tile::GE * j * kStride + 8 * c];
+      if constexpr (PK) {
+        static_assert(PE % 2 == 0, "expert pairs");
+        uint64_t w2[PE / 2];
 #pragma unroll
-      for (int i = 0; i < PT; ++i)
+        for (int jj = 0; jj < PE / 2; ++jj) w2[jj] = f2_pack(wv[2 * jj], wv[2 * jj + 1]);
 #pragma unroll
-        for (int j = 0; j < PE; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[j], hv[i]));
+        for (int i = 0; i < PT; ++i) {
+          const uint64_t h2 = f2_pack(hv[i], hv[i]);
+#pragma unroll
+          for (int jj = 0; jj < PE / 2; ++jj) {
+            float p0, p1;
+            f2_unpack(f2_mul_rn(w2[jj], h2), p0, p1);
+            acc[i][2 * jj] = __fadd_rn(acc[i][2 * jj], p0);
+            acc[i][2 * jj + 1] = __fadd_rn(acc[i][2 * jj + 1], p1);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < PT; ++i)
+#pragma unroll
+          for (int j = 0; j < PE; ++j)
+            acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[j], hv[i]));
+      }
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -333,6 +373,16 @@ __global__ void __launch_bounds__(NT, PT * PE >= 64 ? 2 : 4)
   }
 }
 
+// MOE_ROUTE_F32X2=0 runs the pipelined logits with scalar multiplies.
+bool route_packed() {
+  static int v = -1;
+  if (v < 0) {
+    const char *env = getenv("MOE_ROUTE_F32X2");
+    v = env && atoi(env) == 0 ? 0 : 1;
+  }
+  return v == 1;
+}
+
 // MOE_ROUTE_TILE=24|44 pins the block (PT, PE) for measurements; 1 selects
 // the 4 x 4 scalar-staged kernel.
 int route_tile_override() {
@@ -351,17 +401,17 @@ int pipe_ctas(const RouteArgs &a) {
   return ((a.E + TE - 1) / TE) * ((a.T + TT - 1) / TT);
 }
 
-template <int PT, int PE, int CW, int S, int NT>
+template <int PT, int PE, int CW, int S, int NT, bool PK>
 cudaError_t launch_pipe(const RouteArgs &a, cudaStream_t s) {
   using Tile = PipeTile<PT, PE, CW, S, NT>;
   constexpr size_t smem = Tile::kSmem;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(route_logits_pipe_kernel<PT, PE, CW, S, NT>,
+    cudaError_t e = cudaFuncSetAttribute(route_logits_pipe_kernel<PT, PE, CW, S, NT, PK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   dim3 grid((a.E + Tile::TE - 1) / Tile::TE, (a.T + Tile::TT - 1) / Tile::TT);
-  route_logits_pipe_kernel<PT, PE, CW, S, NT><<<grid, NT, smem, s>>>(a);
+  route_logits_pipe_kernel<PT, PE, CW, S, NT, PK><<<grid, NT, smem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -625,10 +675,13 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t s, int *launches) {
     // 4 x 4 blocks while they still give about one CTA per SM, else 2 x 4
     const int pin = route_tile_override();
     cudaError_t e;
-    if (pin == 44 || (pin != 24 && pipe_ctas<4, 4, 256>(a) >= 128))
-      e = launch_pipe<4, 4, 64, 4, 256>(a, s);
+    const bool wide = pin == 44 || (pin != 24 && pipe_ctas<4, 4, 256>(a) >= 128);
+    if (route_packed())
+      e = wide ? launch_pipe<4, 4, 64, 4, 256, true>(a, s)
+               : launch_pipe<2, 4, 128, 4, 256, true>(a, s);
     else
-      e = launch_pipe<2, 4, 128, 4, 256>(a, s);
+      e = wide ? launch_pipe<4, 4, 64, 4, 256, false>(a, s)
+               : launch_pipe<2, 4, 128, 4, 256, false>(a, s);
     if (e != cudaSuccess) return e;
   } else if (a.T >= 16 && a.router_dtype != kRouterF32Seq) {
     const int ne = (a.E + kTE - 1) / kTE;
