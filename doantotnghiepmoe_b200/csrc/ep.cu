@@ -509,6 +509,39 @@ __global__ void ep_wait_combine_kernel(EpP2P p, const uint32_t *epoch_p,
   const float *sc = reinterpret_cast<const float *>(p.base[p.rank] + p.off_cscale);
   const int hb = (H + 31) / 32;
   bool bad = false;
+  const bool vec = (H & 3) == 0 && K <= kMaxTopK &&
+                   (((uintptr_t)out | (uintptr_t)resid) & 15) == 0 &&
+                   (size_t)T * H / 4 < (1u << 31);
+  if (!p.ret16 && vec) {
+    // fp32 rows, 4 columns per thread with 32-bit index math; all K slot
+    // loads issued before the first add, then the single-GPU combine's
+    // slot order (bit-identical)
+    const float *c32 = reinterpret_cast<const float *>(p.base[p.rank] + p.off_contrib);
+    const uint32_t H4 = H / 4, n4 = (uint32_t)((size_t)T * H / 4);
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += gridDim.x * blockDim.x) {
+      const uint32_t t = i / H4, j4 = i - t * H4;
+      float4 acc = resid ? reinterpret_cast<const float4 *>(resid)[i] : make_float4(0, 0, 0, 0);
+      float4 v[kMaxTopK];
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K)
+          v[k] = __ldcg(reinterpret_cast<const float4 *>(c32 + ((size_t)t * K + k) * H) + j4);
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K) {
+          acc.x = __fadd_rn(acc.x, v[k].x);
+          acc.y = __fadd_rn(acc.y, v[k].y);
+          acc.z = __fadd_rn(acc.z, v[k].z);
+          acc.w = __fadd_rn(acc.w, v[k].w);
+        }
+      bad |= !(is_finite_f(acc.x) && is_finite_f(acc.y) && is_finite_f(acc.z) &&
+               is_finite_f(acc.w));
+      reinterpret_cast<float4 *>(out)[i] = acc;
+    }
+    if (bad) set_status(status, kStatusNonFinite);
+    return;
+  }
   if (!p.ret16) {
     // fp32 rows: slot order as the single-GPU combine (bit-identical)
     const float *c32 = reinterpret_cast<const float *>(p.base[p.rank] + p.off_contrib);
@@ -533,9 +566,6 @@ __global__ void ep_wait_combine_kernel(EpP2P p, const uint32_t *epoch_p,
   // slot order as the single-GPU combine; 4 columns per thread (one scale
   // block), all K slot loads issued before the first add (the peers' stores
   // reached these buffers before their flags C, so the loads bypass L1)
-  const bool vec = (H & 3) == 0 && K <= kMaxTopK &&
-                   (((uintptr_t)out | (uintptr_t)resid) & 15) == 0 &&
-                   (size_t)T * H / 4 < (1u << 31);
   if (vec) {
     const uint32_t H4 = H / 4, n4 = (uint32_t)((size_t)T * H / 4);
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4;
@@ -593,12 +623,18 @@ cudaError_t launch_ep_dispatch(const float *x, const int32_t *seg_off, const uin
                                int E, int T, int K, int H, const EpP2P &p, const uint32_t *epoch,
                                uint32_t *done, int grid, uint32_t *status, cudaStream_t s) {
   if (K > kMaxTopK) return cudaErrorInvalidValue;
-  // one warp per token (default) or per route: MOE_EP_DISPATCH=route (the
-  // two measured the same on 2 B200s: 86.5 vs 92.7 us at C4)
-  static const int per_token = [] {
+  // One warp per token digitises a row once for all its routes; one warp
+  // per route keeps every CTA busy when tokens are few.  By default a warp
+  // per token while the tokens fill at least half of the grid's warps
+  // (2 B200s, 2048 tokens a rank: 86.5 us per token vs 92.7 per route),
+  // else a warp per route.  MOE_EP_DISPATCH=token|route pins the mode.
+  static const int pin = [] {
     const char *v = getenv("MOE_EP_DISPATCH");
-    return v && strcmp(v, "route") == 0 ? 0 : 1;
+    if (v && strcmp(v, "route") == 0) return 0;
+    if (v && strcmp(v, "token") == 0) return 1;
+    return -1;
   }();
+  const int per_token = pin >= 0 ? pin : (2 * T >= grid * 8 ? 1 : 0);
   ep_dispatch_kernel<<<grid, 256, 0, s>>>(x, seg_off, ids, gates, r_pos, owner, E, T, K, H, p,
                                           epoch, done, status, per_token);
   return cudaGetLastError();
