@@ -452,9 +452,13 @@ def main():
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--quant", default="int8", choices=["int8", "int4"],
                     help="expert weight format (int4: two signed nibbles per byte)")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="override the config's token count (the workload name says so)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
+    if args.tokens > 0 and args.tokens != cfg["T"]:
+        cfg = dict(cfg, T=args.tokens, workload=f"{cfg['workload']}_as_T{args.tokens}")
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, cfg, rank, world)

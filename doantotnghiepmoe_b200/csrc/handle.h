@@ -21,8 +21,13 @@
 namespace moe {
 namespace host {
 
-// Prefill-sized calls (T >= this) take the tensor-core path under MOE_PATH_AUTO.
-constexpr int kTcMinTokens = 128;
+// Calls of at least this many tokens take the tensor-core path under
+// MOE_PATH_AUTO; smaller ones the single-launch digit decode.  Measured on
+// B200 with 16- and 48-layer stacks (OLMoE E = 64, Qwen3 E = 128, K = 8):
+// the digit launch wins at T = 8 (1.51 vs 1.58 ms, 4.63 vs 4.84 ms), the
+// persistent tensor-core GEMMs from T = 12 (1.71 vs 1.78 ms) and by 24% at
+// T = 24-32 and 37% at T = 64 (7.49 vs 11.90 ms).
+constexpr int kTcMinTokens = 12;
 // Default bounds of the device-side waits, in SM clock cycles: about 1 s for
 // the single-launch kernels' grid barriers and 2 s for the expert-parallel
 // flag waits at the maximum SM clock.

@@ -1291,7 +1291,12 @@ moe_status stack_forward_locked(moe_handle *h, int first_layer, int n_layers, fl
     h->last_launches += 1;
     return MOE_OK;
   }
-  if (h->path != MOE_PATH_TENSOR && use_fused(h, T) && quant >= 0) {
+  // AUTO: the tensor-core layers when every layer can take them at T (as
+  // single-layer calls do), else the exact single launch for small T
+  bool all_tc = h->path == MOE_PATH_AUTO;
+  for (int l = first_layer; all_tc && l < first_layer + n_layers; ++l)
+    all_tc = use_tensor_path(h, h->layers[l], T, h->hbuf);
+  if (h->path != MOE_PATH_TENSOR && !all_tc && use_fused(h, T) && quant >= 0) {
     FusedArgs f = fused_args(h, T);
     f.n_layers = n_layers;
     f.stacked = 1;

@@ -107,9 +107,9 @@ enum {
 
 /* Expert GEMM back-end for a layer call. */
 enum {
-  MOE_PATH_AUTO = 0,        /* the digit decode launch for T < 128 when the layers allow it
+  MOE_PATH_AUTO = 0,        /* the digit decode launch for T < 12 when the layers allow it
                                (INT8, 16-byte aligned rows), else the exact GEMV; tensor
-                               cores from T = 128 */
+                               cores from T = 12 (the measured crossover on B200) */
   MOE_PATH_GEMV = 1,        /* exact-order INT8 GEMV (bit-identical to the CPU path); for
                                small T the whole layer runs as one cooperative launch */
   MOE_PATH_TENSOR = 2,      /* tcgen05 grouped GEMM (within the 1e-3 tolerance) */

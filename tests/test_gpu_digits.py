@@ -1,4 +1,4 @@
-"""GPU tests of the digit decode path (MOE_PATH_DIGITS, the default for T < 128).
+"""GPU tests of the digit decode path (MOE_PATH_DIGITS, the default for T < 12).
 
 Routing must equal the CPU oracle bit for bit (ids and gates); outputs must be
 within the 1e-3 tolerance of the oracle and bit-identical to the tensor-core
@@ -47,7 +47,7 @@ def check(lw, h, resid=None, route_mode=None):
     eng.set_layer_packed(0, *dev)
     if route_mode is not None:
         eng.set_route_mode(route_mode)
-    od, idd, gd, prof = run(eng, h, _lib.MOE_PATH_AUTO, resid)
+    od, idd, gd, prof = run(eng, h, _lib.MOE_PATH_DIGITS, resid)
     assert "digit_decode" in prof, prof
     ot, idt, _, proft = run(eng, h, _lib.MOE_PATH_TENSOR, resid)
     assert "gate_up_tc" in proft
@@ -82,6 +82,43 @@ def test_bf16_router_and_small_shapes():
     check(lw, O.synth_hidden(622, 3, 512))
     lw2 = O.synth_layer(623, 0, 256, 160, 32, 2, True)  # I = 160: partial 16-byte chunks
     check(lw2, O.synth_hidden(624, 12, 256), resid=O.synth_hidden(625, 12, 256))
+
+
+@pytest.mark.parametrize("T,want", [(1, "digit_decode"), (11, "digit_decode"),
+                                    (12, "gate_up_tc"), (64, "gate_up_tc")])
+def test_auto_path_switches_at_twelve_tokens(T, want):
+    """MOE_PATH_AUTO: the single-launch digit decode below 12 tokens, the
+    tensor-core GEMMs from 12 (the measured crossover on B200)."""
+    lw = O.synth_layer(651, 0, 512, 256, 16, 4, True)
+    eng = M.MoeLayerEngine(M.MoeConfig(512, 256, 16, 4, True, T, 1))
+    eng.set_layer_packed(0, *helpers.to_device(lw))
+    _, _, _, prof = run(eng, O.synth_hidden(652, T, 512), _lib.MOE_PATH_AUTO)
+    assert want in prof, prof
+    other = "gate_up_tc" if want == "digit_decode" else "digit_decode"
+    assert other not in prof, prof
+
+
+@pytest.mark.parametrize("T,want", [(4, "digit_decode"), (16, "gate_up_tc")])
+def test_auto_stack_path_switches_at_twelve_tokens(T, want):
+    """moe_stack_forward under MOE_PATH_AUTO follows the same switch: one
+    digit launch for the stack below 12 tokens, the tensor-core layers from
+    12 (never the slower exact single launch)."""
+    layers = [O.synth_layer(653, l, 512, 256, 16, 4, True) for l in range(2)]
+    eng = M.MoeLayerEngine(M.MoeConfig(512, 256, 16, 4, True, T, 2))
+    keep = [helpers.to_device(lw) for lw in layers]
+    for l, t in enumerate(keep):
+        eng.set_layer_packed(l, *t)
+    eng.set_path(_lib.MOE_PATH_AUTO)
+    x0 = O.synth_hidden(654, T, 512)
+    x = torch.from_numpy(x0).cuda()
+    eng.profile(True)
+    eng.stack_forward(0, 2, x, 1e-5)
+    eng.sync_status()
+    prof = eng.profile_read()
+    eng.profile(False)
+    assert want in prof and "fused_decode" not in prof, prof
+    ref_x, _, _ = O.stack_forward(layers, x0, nthreads=8)
+    assert helpers.rel_err(x.cpu().numpy(), ref_x) < TOL
 
 
 def test_router_variant_routes_like_the_tensor_path():
