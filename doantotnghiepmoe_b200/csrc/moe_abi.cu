@@ -1403,7 +1403,7 @@ static void h2d(void *dst, const void *src, size_t bytes, void *pin, bool pinned
 // back on another, so the PCIe transfers hide behind the tensor-core work.
 // MOE_HOST_CHUNK sets the chunk in tokens (0: whole batch).
 static constexpr int kHostChunksMax = 8;
-static constexpr int kHostChunkDefault = 1280;
+static constexpr int kHostChunkDefault = 1024;
 
 static int host_chunk_tokens(moe_handle *h, int layer, int T) {
   static int env = -1;

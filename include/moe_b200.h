@@ -204,7 +204,7 @@ moe_status moe_set_layer_norm(moe_handle *h, int layer, const float *d_norm_w);
  * Buffers in pinned host memory are read and written by DMA directly;
  * pageable ones go through the handle's pinned staging in chunks.  Buffers
  * from moe_host_alloc() take the fastest host-to-device path.  Batches of
- * at least 2 x 1280 tokens on the tensor-core path run in token chunks (up
+ * at least 2 x 1024 tokens on the tensor-core path run in token chunks (up
  * to 8; MOE_HOST_CHUNK sets the chunk, 0 turns it off): a chunk's layer
  * overlaps the next chunk's copy in and the previous chunk's copy out, and
  * the results are bit-identical to one whole-batch call. */

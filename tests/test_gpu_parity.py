@@ -319,7 +319,7 @@ def test_host_call_in_token_chunks_matches_whole_batch():
     ref = O.layer_forward(lw, h[rows], resid=resid[rows])
     assert np.array_equal(want_ids[rows], ref.ids)
     assert helpers.rel_err(want[rows], ref.out) < 1e-3
-    chunked = os.environ.get("MOE_HOST_CHUNK", "1280") != "0"
+    chunked = os.environ.get("MOE_HOST_CHUNK", "1024") != "0"
     for pin in (True, False):
         def mk(a):
             if not pin:
