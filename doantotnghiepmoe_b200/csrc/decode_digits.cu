@@ -150,6 +150,89 @@ __device__ __forceinline__ int warp_sum(int v) {
 }
 
 // ---------------------------------------------------------------------------
+// One token's digit planes by a whole CTA that has no router task: the row
+// (RMS-normalised first in stacks, with the router tasks' exact arithmetic)
+// is staged, its max |x| reduced over the CTA, and its planes and scales
+// written.  Runs while the router tasks compute the logits, so the planes
+// leave the router tasks' critical path.
+// ---------------------------------------------------------------------------
+__device__ void token_digits_cta(const DigitArgs &a, const FusedLayer &L, const float *xin,
+                                 bool stacked, int t, float *stage, DTables &tb) {
+  const int H = a.H, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int full = H / 8;
+  float *x = stage;
+  for (int c = tid; c < H; c += kDT) x[c] = __ldcg(xin + (size_t)t * H + c);
+  __syncthreads();
+  if (stacked) {
+    // the router tasks' RMSNorm, operation for operation
+    if (warp == 0) {
+      float acc = 0.0f;
+      if (lane < 8) {
+        int c = 0;
+        for (; c + 16 <= full; c += 16) {
+          float p[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const float v = x[8 * (c + u) + lane];
+            p[u] = __fmul_rn(v, v);
+          }
+#pragma unroll
+          for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, p[u]);
+        }
+        for (; c < full; ++c) {
+          const float v = x[8 * c + lane];
+          acc = __fadd_rn(acc, __fmul_rn(v, v));
+        }
+      }
+      float sq = -0.0f;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) sq = __fadd_rn(sq, __shfl_sync(0xffffffffu, acc, l));
+      for (int i = full * 8; i < H; ++i) sq = __fadd_rn(sq, __fmul_rn(x[i], x[i]));
+      if (lane == 0) {
+        const float scale = __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, (float)H), a.eps));
+        tb.inv[0] = __fdiv_rn(1.0f, scale);
+      }
+    }
+    __syncthreads();
+    const float inv = tb.inv[0];
+    for (int j = tid; j < H; j += kDT) {
+      const float w = L.norm_w ? L.norm_w[j] : 1.0f;
+      x[j] = __fmul_rn(__fmul_rn(x[j], inv), w);
+    }
+    __syncthreads();
+  }
+  // max |x| over the row (order-free), then the planes, 4 columns a thread
+  float amax = 0.0f;
+  for (int c = 4 * tid; c < H; c += 4 * kDT) {
+    const float4 v = *reinterpret_cast<const float4 *>(x + c);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  // per-warp maxima in the top-k scratch (unused until after the barrier)
+  float *red = tb.u.s.ex[0];
+  if (lane == 0) red[warp] = amax;
+  __syncthreads();
+  amax = 0.0f;
+  for (int w = 0; w < kDW; ++w) amax = fmaxf(amax, red[w]);
+  const float sc = digits::row_scale(amax);
+  const float inv = 1.0f / sc;
+  int8_t *q1 = a.xq + (size_t)t * 2 * H, *q2 = q1 + H;
+  for (int c = 4 * tid; c < H; c += 4 * kDT) {
+    const float4 v = *reinterpret_cast<const float4 *>(x + c);
+    uint32_t p2;
+    const uint32_t p1 = digits::split4(v.x, v.y, v.z, v.w, inv, p2);
+    *reinterpret_cast<uint32_t *>(q1 + c) = p1;
+    *reinterpret_cast<uint32_t *>(q2 + c) = p2;
+  }
+  if (tid == 0) {
+    a.xs1[t] = sc;
+    a.xs2[t] = sc / 254.0f;
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
 // R: router logits (exact order) + the token rows' digit planes.
 // ---------------------------------------------------------------------------
 __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const float *xin,
@@ -165,6 +248,11 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
   // warp reads at the same column fall in different banks
   const int RS = H + kRowPad;
   const bool seq = a.route_mode == kRouteTopkSoftmax && L.router_dtype == kRouterF32;
+  // with CTAs to spare, CTAs [tasks, tasks + T) make the tokens' digit planes
+  // while the router tasks run; otherwise the tasks of expert group 0 do
+  const bool sep = tasks + T <= (int)gridDim.x;
+  if (sep && (int)blockIdx.x >= tasks && (int)blockIdx.x < tasks + T)
+    token_digits_cta(a, L, xin, stacked, (int)blockIdx.x - tasks, stage, tb);
   for (int task = blockIdx.x; task < tasks; task += gridDim.x) {
     const int t0 = (task / nte) * TT, e0 = (task % nte) * RE;
     const int nt = min(TT, T - t0);
@@ -302,7 +390,7 @@ __device__ void router_phase(const DigitArgs &a, const FusedLayer &L, const floa
     }
     // the token rows' digit planes, once per token (expert group 0), on the
     // warps above the ones running the dot (token r on warp kDW - 1 - r)
-    if (e0 == 0 && kDW - 1 - warp < nt) {
+    if (!sep && e0 == 0 && kDW - 1 - warp < nt) {
       const int r = kDW - 1 - warp;
       const float *x = stage + (size_t)r * RS;
       float amax = 0.0f;
@@ -398,7 +486,21 @@ __device__ void select_rank(const float *lg, int E, int K, int norm_topk_prob, i
   int rank[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) rank[j] = 0;
-  for (int f = 0; f < E; ++f) {
+  // 8 keys a step: their shared-memory loads issue back to back
+  int f = 0;
+  for (; f + 8 <= E; f += 8) {
+    uint32_t kf[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) kf[u] = key[f + u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int e = lane + 32 * j;
+        rank[j] += (kf[u] > k[j]) || (kf[u] == k[j] && f + u < e);
+      }
+  }
+  for (; f < E; ++f) {
     const uint32_t kf = key[f];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
