@@ -14,13 +14,17 @@
 // in fp32.  Against the CPU path the layer output stays within the 1e-3
 // relative tolerance with a wide margin (the parity tests assert it).
 //
-// Kernel shape (both GEMMs): one CTA per (128-row weight tile, token tile of
-// up to 128 routes of one expert), 192 threads:
-//   warp 0  : TMA producer (3D tiled loads, 128B swizzle, mbarrier tx count)
-//   warp 1  : TMEM allocator + single-thread MMA issuer (tcgen05.commit
-//             releases a pipeline stage / signals the epilogue)
-//   warps 2-5: epilogue, tcgen05.ld of the accumulators (warp w reads TMEM
-//             lanes 32*(w%4) .. +31).
+// Kernel shapes.  Default (persistent): one CTA per SM walks the work items
+// (64-route tile of one expert x weight rows), 576 threads:
+//   warp 0  : TMA producer (3D tiled loads, 128B swizzle, mbarrier tx count),
+//             one ring running on across items
+//   warp 1  : TMEM allocator + single-thread MMA issuer, alternating between
+//             two TMEM accumulator buffers
+//   warps 2-17: epilogue, tcgen05.ld of the accumulators (warp w reads TMEM
+//             lanes 32*(w%4) .. +31), draining one buffer while the MMAs
+//             fill the other.
+// MOE_TC_PERSISTENT=0: one CTA per (128-row weight tile, route tile of up to
+// 128 routes), 192 threads, the same roles with 4 epilogue warps.
 // Every mbarrier wait is bounded: on expiry the kernel records
 // kStatusTimeout, stops issuing work, waits (bounded) for its in-flight
 // copies, frees its TMEM and returns.
